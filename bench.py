@@ -1,0 +1,354 @@
+"""Benchmark of the specgrove_b200 packed tree-verification step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload accept]
+
+One JSON line is printed by rank 0.  Under torchrun (N > 1) every rank runs
+its own shard of requests (data parallel, no data-path collective); the step
+time is the max over ranks of the CUDA-event time, and `value` aggregates the
+units of all ranks.
+
+Workload `accept` (acceptance sweep): 64 request trees, 4096 packed nodes,
+vocabulary 151936, fp32 target probabilities (inputs 2.49 GB, larger than L2),
+then the accepted-path KV commit of 36 layers x 8 kv heads x 128 bf16.  One
+step = one acceptance launch (Philox uniforms keyed by (seed=step, request,
+node)) + one commit launch, both on device with no host round trip.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+KV_BYTES_PER_TOKEN = 36 * 8 * 128 * 2 * 2  # layers x kv heads x head_dim x bf16 x {K,V}
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling during the timed region (median SM MHz, reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.path is None:
+            return None
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), max=float(parts[2]), power=float(parts[3]),
+                                 hw=parts[5], hwt=parts[6], swt=parts[7], swp=parts[8]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        reasons = set()
+        for r in rows:
+            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                              ("swt", "sw_thermal_slowdown"), ("swp", "sw_power_cap")):
+                if r[key].lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in rows), "sm_max_mhz": max(r["max"] for r in rows),
+                "samples": len(rows), "power_w_max": max(r["power"] for r in rows), "reasons": sorted(reasons)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# Acceptance sweep workload
+# ---------------------------------------------------------------------------
+class AcceptWorkload:
+    name = "acceptance_sweep: 64 trees / 4096 nodes / V=151936 fp32 probs + KV commit 36x8x128 bf16"
+
+    def __init__(self, rank: int, capacity: int = 1024):
+        from specgrove_b200 import workloads
+        from specgrove_b200.arena import PersistentKVArena
+        from specgrove_b200.sampling import PackedTrees
+        self.batch, self.probs = workloads.acceptance_sweep(seed=rank, device="cuda")
+        self.trees = PackedTrees(self.batch.parents, self.batch.tokens, "cuda")
+        self.D = self.trees.max_depth
+        self.T = self.trees.count
+        self.vocab = self.probs.shape[1]
+        self.arena = PersistentKVArena(36, 8, 128, self.T, capacity, dtype=torch.bfloat16)
+        rng = np.random.default_rng(rank)
+        self.lengths0 = rng.integers(64, 257, size=self.T)
+        self.slots = torch.arange(self.T, dtype=torch.long, device="cuda")
+        self.len_in = torch.from_numpy(self.lengths0.astype(np.int64)).cuda()
+        self.len_out = torch.empty_like(self.len_in)
+        self.request_ids = torch.arange(self.T, dtype=torch.long, device="cuda") + 1000 * rank
+        self.status = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def step(self, seed: int, out: torch.Tensor, events=None):
+        from specgrove_b200 import _lib
+        from specgrove_b200._lib import check, ptr, stream_ptr
+        from specgrove_b200.sampling import accept_packed
+        if events is not None:
+            events[0].record()
+        accept_packed(self.probs, self.trees, seed=seed, request_ids=self.request_ids, out=out,
+                      status=self.status)
+        if events is not None:
+            events[1].record()
+        a = self.arena
+        st = _lib.load().sg_kv_commit_accepted(
+            ptr(a.storage), a.plane_rows, a.num_planes, a.row_bytes, a.capacity, ptr(self.slots),
+            ptr(self.len_in), ptr(self.len_out), ptr(out), self.T, self.D, ptr(self.status),
+            stream_ptr())
+        check(st, "sg_kv_commit_accepted")
+        if events is not None:
+            events[2].record()
+
+    def units(self, outs: torch.Tensor) -> int:
+        """accepted tokens (accepted nodes + bonus) over the given step outputs."""
+        return int((outs[..., self.D] + 1).sum())
+
+
+def run_b200(args, world, rank):
+    from specgrove_b200 import _lib
+    hbm, tc, tc_sus, peak_kind = peaks()
+    wl = AcceptWorkload(rank)
+    K, W = args.steps, args.warmup
+    outs = torch.empty((K, wl.T, wl.D + 2), dtype=torch.long, device="cuda")
+    warm = torch.empty((wl.T, wl.D + 2), dtype=torch.long, device="cuda")
+    for i in range(W):
+        wl.step(10_000 + i, warm)
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = _lib.launch_count()
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(K):
+            wl.step(i, outs[i], ev[i])
+        stop.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    launches = _lib.launch_count() - launches0
+    ms_local = start.elapsed_time(stop) / K
+    ms = max_over_ranks(ms_local, world)
+    units_local = wl.units(outs)
+    total_units = sum_over_ranks(units_local, world)
+    value = total_units / (ms * K / 1000.0)
+    if int(wl.status) != 0:
+        raise RuntimeError(f"device status {int(wl.status)}")
+    # roofline of the dominant kernel (acceptance): visited rows x V x 4 bytes per launch
+    accept_ms = [e[0].elapsed_time(e[1]) for e in ev]
+    commit_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    visited = (outs[..., wl.D] + 1).double()        # scan rule: accepted + exit row
+    accept_bytes = float(visited.sum()) / K * wl.vocab * 4
+    commit_bytes = float(visited.sum()) / K * KV_BYTES_PER_TOKEN
+    accept_gbs = accept_bytes / (statistics.mean(accept_ms) / 1000) / 1e9
+    commit_gbs = commit_bytes / (statistics.mean(commit_ms) / 1000) / 1e9
+    # e2e through the public API with host buffers: probabilities and tree
+    # metadata copied from pinned host memory, decisions read back, per step.
+    e2e = e2e_accept(wl, args, world)
+    cpu = cpu_baseline_accept(wl) if (rank == 0 and world == 1) else None
+    clk = clocks.summary()
+    line = {
+        "metric": "accepted tokens/s/GPU", "value": value, "unit": "accepted tokens/s",
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": wl.name, "trees_per_gpu": wl.T, "nodes_per_gpu": wl.trees.total_rows,
+                   "vocab": wl.vocab, "rule": "scan (Philox per node)", "parallelism": f"dp{world}",
+                   "l2": "inputs larger than L2 (2.49 GB probabilities)"},
+        "roofline": {"bound": "hbm", "kernel": "accept_probs_kernel", "achieved": accept_gbs, "peak": hbm,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": accept_gbs / hbm, "traffic": None,
+                     "algorithmic_bytes_per_launch": accept_bytes,
+                     "launch_ms": statistics.mean(accept_ms),
+                     "commit": {"achieved": commit_gbs, "frac": commit_gbs / hbm,
+                                "bytes_per_launch": commit_bytes, "launch_ms": statistics.mean(commit_ms)}},
+        "cpu_baseline": cpu, "clocks": clk, "e2e": e2e, "gpu_launches": launches,
+    }
+    return line
+
+
+def e2e_accept(wl, args, world):
+    from specgrove_b200.sampling import PackedTrees, accept_packed
+    probs_host = wl.probs.cpu().pin_memory()
+    parents, tokens = wl.batch.flat()
+    meta_host = torch.from_numpy(np.concatenate([np.asarray(wl.batch.row_offsets, np.int64), parents,
+                                                 tokens])).pin_memory()
+    probs_dev = torch.empty_like(wl.probs)
+    meta_dev = torch.empty_like(meta_host, device="cuda")
+    out_host = torch.empty((wl.T, wl.D + 2), dtype=torch.long).pin_memory()
+    out_dev = torch.empty((wl.T, wl.D + 2), dtype=torch.long, device="cuda")
+    n = len(wl.batch.row_offsets)
+    trees = PackedTrees.__new__(PackedTrees)
+    trees.count, trees.max_depth, trees.max_nodes = wl.T, wl.D, wl.trees.max_nodes
+    trees.total_rows = wl.trees.total_rows
+    trees.row_offsets = meta_dev[:n]
+    trees.parents = meta_dev[n:n + trees.total_rows]
+    trees.tokens = meta_dev[n + trees.total_rows:]
+    steps = max(2, min(args.steps, 5))
+    units = 0
+
+    def one(seed):
+        probs_dev.copy_(probs_host, non_blocking=True)
+        meta_dev.copy_(meta_host, non_blocking=True)
+        accept_packed(probs_dev, trees, seed=seed, request_ids=wl.request_ids, out=out_dev)
+        out_host.copy_(out_dev, non_blocking=True)
+
+    one(123)
+    torch.cuda.synchronize()
+    barrier(world)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        one(i)
+        torch.cuda.current_stream().synchronize()
+        units += int((out_host[:, wl.D] + 1).sum())
+    stop.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(stop) / steps, world)
+    total = sum_over_ranks(units, world)
+    return {"value": total / (ms * steps / 1000.0), "unit": "accepted tokens/s",
+            "h2d_bytes_per_step": probs_host.numel() * 4 + meta_host.numel() * 8,
+            "d2h_bytes_per_step": out_host.numel() * 8, "steps": steps, "ms_per_step": ms}
+
+
+def cpu_baseline_accept(wl, arith=None):
+    """The reference's rule (sequential fp64 running sums, the CPU helper of
+    fused_tree_sampling.py:2607-2612) over the same trees, all host cores."""
+    from oracle import cpu as oracle
+    probs = wl.probs.cpu().numpy()
+    parents, tokens = wl.batch.flat()
+    arith = oracle.ARITH_FP64 if arith is None else arith
+    rng = np.random.default_rng(0)
+    units, seconds, reps = 0, 0.0, 0
+    while seconds < 10.0 and reps < 50:
+        uniforms = rng.random((wl.T, wl.D + 1))
+        t0 = time.perf_counter()
+        out, _ = oracle.accept_probs(probs, wl.batch.row_offsets, parents, tokens, wl.D, uniforms=uniforms,
+                                     arith=arith)
+        seconds += time.perf_counter() - t0
+        units += int((out[:, wl.D] + 1).sum())
+        reps += 1
+    return {"value": units / seconds, "unit": "accepted tokens/s", "cores": os.cpu_count(),
+            "kind": "port", "sample": f"{reps} full acceptance steps (64 trees, explicit uniforms, "
+                                      "fp64 running-sum rule); KV commit not included"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    wl = AcceptWorkload(rank)
+    cpu = cpu_baseline_accept(wl)
+    line = {"impl": "reference", "metric": "accepted tokens/s/GPU", "value": cpu["value"],
+            "unit": "accepted tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp64",
+            "data": "synthetic", "config": {"workload": wl.name, "parallelism": "cpu"},
+            "cpu_baseline": cpu, "e2e": {"value": cpu["value"], "unit": "accepted tokens/s",
+                                         "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="accept", choices=["accept"])
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_setup(args)
+    try:
+        line = run_reference(args, world, rank) if args.impl == "reference" else run_b200(args, world, rank)
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,159 @@
+/*
+ * specgrove_b200 — C ABI of the B200 (sm_100a) packed tree-verification step.
+ *
+ * Conventions shared by every entry point:
+ *   - every pointer argument is a device pointer owned by the caller, unless
+ *     its comment says "host";
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *   - the return value is an sg_status code (0 = success); nothing throws across
+ *     this boundary; sg_last_error() gives a thread-local detail string;
+ *   - calls are asynchronous on `stream` and re-entrant per stream.  Problems
+ *     that can only be seen on the device (an out-of-range token, a negative or
+ *     non-finite probability, an exhausted cache slot) are reported through the
+ *     optional device word `status` (atomicMax of an sg_status code), which the
+ *     caller reads with the results.
+ */
+#ifndef SPECGROVE_B200_H
+#define SPECGROVE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SG_API __attribute__((visibility("default")))
+#else
+#define SG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum sg_status {
+  SG_OK = 0,
+  SG_ERR_INVALID_ARGUMENT = 1, /* bad sizes, strides, null pointers, alignment */
+  SG_ERR_CUDA = 2,             /* a CUDA runtime call failed */
+  SG_ERR_TREE = 3,             /* tree metadata out of range (device-detected) */
+  SG_ERR_PROBABILITY = 4,      /* negative, non-finite or >= 2^40 probability */
+  SG_ERR_CAPACITY = 5,         /* a request's KV slot would overflow */
+  SG_ERR_UNSUPPORTED = 6,      /* shape or device this build does not handle */
+  SG_ERR_WORKSPACE = 7         /* caller workspace too small */
+};
+
+/* Acceptance rules (sg_tree_accept_probs `rule`). */
+enum sg_accept_rule {
+  /* One uniform per visited depth; token = first index whose exact inclusive
+   * prefix mass exceeds u * row_total (reference fused_tree_sampling.py:538-627). */
+  SG_RULE_SCAN = 0,
+  /* Two uniforms per depth: route among the children by exact cumulative child
+   * mass (rows assumed normalised); on exit draw from the row with the children
+   * removed (reference fused_tree_sampling.py:688-824). */
+  SG_RULE_SPARSE_EXIT = 1
+};
+
+SG_API const char* sg_status_string(int status);
+SG_API const char* sg_last_error(void);
+SG_API int sg_version(void);
+/* Number of kernels this library launched since load (all devices). */
+SG_API uint64_t sg_launch_count(void);
+
+/*
+ * Tree-sampling acceptance over packed fp32 probability rows.
+ *
+ * Replaces the per-request verifier calls of the reference
+ *   fused_tree_sampling.py:2172-2202  tree_verify_ancestral_fused_scan
+ *   fused_tree_sampling.py:2205-2373  tree_verify_ancestral_sparse_exit_fused_scan(_batched)
+ *   sampling.py:903-950               tree_verify_ancestral_batched (same law)
+ * and the kernels they bind (fused.py:538-627 scan, :688-824 sparse exit).
+ *
+ * probs        [total_rows, vocab] fp32, row-major, 16-byte aligned rows when
+ *              vocab % 4 == 0 (otherwise a scalar path is used)
+ * row_offsets  [num_trees + 1] int64: tree t owns rows row_offsets[t] ..
+ *              row_offsets[t+1]-1; local node j of tree t is row row_offsets[t]+j
+ * parents      [total_rows] int64: local parent of each node, -1 for the root,
+ *              parents[j] < j (topological order)
+ * tokens       [total_rows] int64: token of each node; the root entry is ignored
+ * max_depth    common output stride - 2; must be >= every tree's depth
+ * uniforms     explicit uniforms [num_trees, uniform_stride] fp64 in [0,1):
+ *              SG_RULE_SCAN reads u[depth], SG_RULE_SPARSE_EXIT reads
+ *              u[2*depth] (route) and u[2*depth+1] (exit).  NULL selects the
+ *              counter-based stream Philox4x32-10(key=seed, counter=(node,
+ *              request_ids[t], purpose)).
+ * request_ids  [num_trees] int64 keys for the Philox stream (ignored when
+ *              uniforms != NULL; may be NULL, then t is used)
+ * out          [num_trees, max_depth + 2] int64, reference layout
+ *              (fused.py:149-150): slots [0, count) = accepted local nodes,
+ *              out[max_depth] = count, out[max_depth+1] = bonus token; other
+ *              slots are -1.
+ * status       optional device int32 word, atomicMax'ed with an sg_status.
+ */
+SG_API int sg_tree_accept_probs(const float* probs, int64_t vocab,
+                         const int64_t* row_offsets, const int64_t* parents,
+                         const int64_t* tokens, int32_t num_trees,
+                         int32_t max_nodes, int32_t max_depth, int32_t rule,
+                         const double* uniforms, int32_t uniform_stride,
+                         uint64_t seed, const int64_t* request_ids,
+                         int64_t* out, int32_t* status, void* stream);
+
+/*
+ * Walk the trees with one pre-drawn posterior token per node
+ * (reference fused_tree_sampling.py:120-151 fused_tree_follow_kernel, used by
+ * tree_verify_ancestral_same_draw_fused :2376-2414; law of sampling.py:903-950).
+ * posterior    [total_rows] int64 posterior token per packed node
+ * other arguments as sg_tree_accept_probs.
+ */
+SG_API int sg_tree_follow(const int64_t* posterior, const int64_t* row_offsets,
+                   const int64_t* parents, const int64_t* tokens,
+                   int32_t num_trees, int32_t max_nodes, int32_t max_depth,
+                   int64_t* out, int32_t* status, void* stream);
+
+/*
+ * Accepted-path KV commit: copy kept rows inside a slot-strided KV arena or
+ * from a packed source into it.
+ *
+ * Replaces _PersistentRequestCachePool.append_packed_sequence
+ * (continuous_tree_block_decode.py:215-261): for every plane (layer, K|V,
+ * kv head) row dst_rows[i] of `dst` receives row src_rows[i] of `src`.
+ *
+ * dst, src     base pointers of [num_planes, plane_rows, row_bytes] arenas;
+ *              src == dst is the in-place tail compaction
+ * *_plane_rows rows per plane of each arena
+ * row_bytes    bytes per row (head_dim * element size), multiple of 4
+ * src_rows, dst_rows  [num_rows] int64 row indices within a plane
+ * group_offsets [num_groups + 1] int64: rows of one request are
+ *              group_offsets[g] .. group_offsets[g+1]-1.  Within a group, an
+ *              in-place commit must satisfy dst_rows[i] <= src_rows[i] with
+ *              both increasing (true for [0] + accepted nodes); groups must
+ *              not share rows.
+ * status       optional device word; rows out of range set SG_ERR_CAPACITY and
+ *              are skipped.
+ */
+SG_API int sg_kv_commit(void* dst, int64_t dst_plane_rows, const void* src,
+                 int64_t src_plane_rows, int64_t num_planes, int64_t row_bytes,
+                 const int64_t* src_rows, const int64_t* dst_rows,
+                 const int64_t* group_offsets, int32_t num_groups,
+                 int32_t max_group_rows, int32_t* status, void* stream);
+
+/*
+ * Accepted-path commit driven directly by an acceptance output buffer, with no
+ * host round trip: for tree t, keep rows [0] + out[t, 0:count] of the tail
+ * written at slot[t] * capacity + lengths_in[t] + j are moved to
+ * slot[t] * capacity + lengths_in[t] + i, for every plane; lengths_out[t] =
+ * lengths_in[t] + count + 1.  Same arena layout as sg_kv_commit; this is the
+ * in-place form of append_packed_sequence (continuous_tree_block_decode.py:
+ * 215-261) for an engine that writes tree rows into the arena tail.
+ * slots, lengths_in, lengths_out  [num_trees] int64 (lengths_out != lengths_in)
+ * accept_out   [num_trees, max_depth + 2] output of sg_tree_accept_probs /
+ *              sg_tree_follow; max_depth <= 63.
+ */
+SG_API int sg_kv_commit_accepted(void* arena, int64_t plane_rows, int64_t num_planes,
+                          int64_t row_bytes, int64_t capacity, const int64_t* slots,
+                          const int64_t* lengths_in, int64_t* lengths_out,
+                          const int64_t* accept_out, int32_t num_trees,
+                          int32_t max_depth, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPECGROVE_B200_H */

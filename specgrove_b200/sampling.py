@@ -1,0 +1,276 @@
+"""Tree-sampling acceptance through the C ABI, with the reference's verifier API.
+
+The per-request functions keep the names, arguments, return values and error
+behaviour of the reference verifiers in
+``gbv_experiments/fused_tree_sampling.py`` (``_topology`` :2089-2102,
+``tree_verify_ancestral_fused_scan`` :2172-2202,
+``tree_verify_ancestral_sparse_exit_fused_scan`` :2205-2259,
+``..._batched`` :2262-2373, ``tree_verify_ancestral_same_draw_fused``
+:2376-2414), so the decoder's verifier dispatch
+(``continuous_tree_block_decode.py:1965-2107``) can call them unchanged.  They
+draw their uniforms from the request's ``torch.Generator`` exactly as the
+reference does (``torch.rand(max_depth + 1)`` or ``2 * (max_depth + 1)``
+float64 values on the rows' device).
+
+``accept_packed`` is the batched, packed-row entry the B200 engine uses: one
+launch for every tree of a wave, uniforms either explicit or drawn on device
+from Philox4x32-10 keyed by (seed, request, node).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import SG_RULE_SCAN, SG_RULE_SPARSE_EXIT, check, ptr, stream_ptr
+
+
+def _topology(parents, tokens):
+    """Reference ``_topology`` (fused_tree_sampling.py:2089-2102)."""
+    parents = list(parents)
+    tokens = list(tokens)
+    node_count = len(parents)
+    if (node_count < 1 or len(tokens) != node_count - 1
+            or parents[0] != -1
+            or any(parent < 0 or parent >= node for node, parent in enumerate(parents[1:], 1))
+            or len(set(zip(parents[1:], tokens))) != len(tokens)):
+        raise ValueError("Invalid probability-tree topology")
+    depths = [0] * node_count
+    for node in range(1, node_count):
+        depths[node] = depths[parents[node]] + 1
+    return parents, tokens, max(depths)
+
+
+def _check_rows(all_p, node_count, what):
+    if (not all_p.is_cuda or all_p.ndim != 2 or all_p.shape[0] != node_count
+            or all_p.shape[1] < 1 or not all_p.is_floating_point()):
+        raise ValueError(f"{what} probability tensor mismatch")
+
+
+def _validate_probabilities(all_p, normalised: bool):
+    if normalised:
+        valid = (torch.isfinite(all_p).all() & (all_p >= 0).all()
+                 & torch.isclose(all_p.sum(-1), all_p.new_ones(all_p.shape[0]),
+                                 rtol=1e-10, atol=1e-12).all())
+        if not bool(valid):
+            raise FloatingPointError("Sparse-exit verifier requires normalized Target probabilities")
+    else:
+        valid = (torch.isfinite(all_p).all() & (all_p >= 0).all() & (all_p.sum(-1) > 0).all())
+        if not bool(valid):
+            raise FloatingPointError("Invalid Target probabilities for DDTree")
+
+
+def _as_fp32_rows(all_p: torch.Tensor) -> torch.Tensor:
+    if all_p.dtype != torch.float32:
+        all_p = all_p.to(torch.float32)
+    return all_p.contiguous()
+
+
+class PackedTrees:
+    """Device metadata of a batch of trees packed row after row.
+
+    ``parents``/``tokens`` hold one entry per node (root parent -1, root token
+    -1); tree ``t`` owns rows ``row_offsets[t]:row_offsets[t+1]``.
+    """
+
+    def __init__(self, parents_batch, tokens_batch, device, vocab: int | None = None):
+        offsets = [0]
+        flat_parents: list[int] = []
+        flat_tokens: list[int] = []
+        depth = 0
+        max_nodes = 1
+        for parents, tokens in zip(parents_batch, tokens_batch):
+            parents, tokens, d = _topology(parents, tokens)
+            if vocab is not None and any(t < 0 or t >= vocab for t in tokens):
+                raise ValueError("Tree token is outside the Target vocabulary")
+            depth = max(depth, d)
+            max_nodes = max(max_nodes, len(parents))
+            flat_parents += parents
+            flat_tokens += [-1] + tokens
+            offsets.append(len(flat_parents))
+        meta = torch.tensor([flat_parents, flat_tokens], dtype=torch.long)
+        self.count = len(offsets) - 1
+        self.max_depth = depth
+        self.max_nodes = max_nodes
+        self.total_rows = offsets[-1]
+        self.row_offsets_host = offsets
+        pinned = torch.cat([torch.tensor(offsets, dtype=torch.long), meta.reshape(-1)])
+        if torch.device(device).type == "cuda":
+            pinned = pinned.pin_memory()
+        dev = pinned.to(device, non_blocking=True)
+        n = len(offsets)
+        self.row_offsets = dev[:n]
+        self.parents = dev[n:n + self.total_rows]
+        self.tokens = dev[n + self.total_rows:]
+
+
+def accept_packed(probs: torch.Tensor, trees: PackedTrees, *, rule: int = SG_RULE_SCAN,
+                  uniforms: torch.Tensor | None = None, seed: int = 0,
+                  request_ids: torch.Tensor | None = None, max_depth: int | None = None,
+                  out: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                  stream=None) -> torch.Tensor:
+    """One launch of ``sg_tree_accept_probs`` over packed rows; returns the
+    device ``[trees, max_depth + 2]`` int64 output (reference layout)."""
+    if probs.dtype != torch.float32 or not probs.is_cuda or probs.ndim != 2:
+        raise ValueError("accept_packed expects a CUDA float32 [rows, vocab] tensor")
+    probs = probs.contiguous()
+    if probs.shape[0] < trees.total_rows:
+        raise ValueError("fewer probability rows than packed tree nodes")
+    depth = trees.max_depth if max_depth is None else int(max_depth)
+    if depth < trees.max_depth:
+        raise ValueError("max_depth is below the depth of a packed tree")
+    stride = 0
+    if uniforms is not None:
+        if uniforms.dtype != torch.float64 or uniforms.device != probs.device:
+            raise ValueError("uniforms must be float64 on the probabilities' device")
+        uniforms = uniforms.reshape(trees.count, -1).contiguous()
+        stride = uniforms.shape[1]
+    if out is None:
+        out = torch.empty((trees.count, depth + 2), dtype=torch.long, device=probs.device)
+    lib = _lib.load()
+    st = lib.sg_tree_accept_probs(
+        ptr(probs), probs.shape[1], ptr(trees.row_offsets), ptr(trees.parents), ptr(trees.tokens),
+        trees.count, trees.max_nodes, depth, rule, ptr(uniforms), stride, seed & ((1 << 64) - 1),
+        ptr(request_ids), ptr(out), ptr(status), stream_ptr(stream))
+    check(st, "sg_tree_accept_probs")
+    return out
+
+
+def decode_output(packed_row, max_depth: int, vocab: int, tokens, what: str):
+    accepted_count = int(packed_row[max_depth])
+    bonus = int(packed_row[max_depth + 1])
+    if not 0 <= accepted_count <= max_depth or not 0 <= bonus < vocab:
+        raise RuntimeError(f"{what} returned invalid control values")
+    nodes = [int(node) for node in packed_row[:accepted_count]]
+    return nodes, [tokens[node - 1] for node in nodes], bonus
+
+
+def tree_verify_ancestral_fused_scan(parents, tokens, all_p, generator=None, validate: bool = True):
+    """Reference fused_tree_sampling.py:2172-2202 on the B200 kernel."""
+    parents, tokens, max_depth = _topology(parents, tokens)
+    node_count = len(parents)
+    _check_rows(all_p, node_count, "Scan-fused DDTree")
+    if any(token < 0 or token >= all_p.shape[1] for token in tokens):
+        raise ValueError("Tree token is outside the Target vocabulary")
+    if validate:
+        _validate_probabilities(all_p, normalised=False)
+    uniforms = torch.rand(max_depth + 1, dtype=torch.float64, device=all_p.device, generator=generator)
+    trees = PackedTrees([parents], [tokens], all_p.device)
+    out = accept_packed(_as_fp32_rows(all_p), trees, rule=SG_RULE_SCAN, uniforms=uniforms,
+                        max_depth=max_depth)
+    return decode_output(out[0].tolist(), max_depth, all_p.shape[1], tokens,
+                         "Scan-fused tree sampler")
+
+
+def tree_verify_ancestral_sparse_exit_fused_scan(parents, tokens, all_p, generator=None,
+                                                 validate: bool = True):
+    """Reference fused_tree_sampling.py:2205-2259 on the B200 kernel."""
+    parents, tokens, max_depth = _topology(parents, tokens)
+    node_count = len(parents)
+    if not all_p.is_contiguous():
+        raise ValueError("Sparse-exit Target probability tensor mismatch")
+    _check_rows(all_p, node_count, "Sparse-exit Target")
+    if any(token < 0 or token >= all_p.shape[1] for token in tokens):
+        raise ValueError("Tree token is outside the Target vocabulary")
+    if validate:
+        _validate_probabilities(all_p, normalised=True)
+    uniforms = torch.rand(2 * (max_depth + 1), dtype=torch.float64, device=all_p.device,
+                          generator=generator)
+    trees = PackedTrees([parents], [tokens], all_p.device)
+    out = accept_packed(_as_fp32_rows(all_p), trees, rule=SG_RULE_SPARSE_EXIT, uniforms=uniforms,
+                        max_depth=max_depth)
+    return decode_output(out[0].tolist(), max_depth, all_p.shape[1], tokens,
+                         "Sparse-exit sampler")
+
+
+def tree_verify_ancestral_sparse_exit_fused_scan_batched(parents_batch, tokens_batch,
+                                                         probability_batch, generators,
+                                                         validate: bool = True):
+    """Reference fused_tree_sampling.py:2262-2373: ragged or equal-shaped
+    batches both run as ONE launch over packed rows with one host transfer."""
+    count = len(parents_batch)
+    if (count < 1 or len(tokens_batch) != count or len(probability_batch) != count
+            or len(generators) != count):
+        raise ValueError("Sparse-exit batch inputs have different lengths")
+    rows = (list(probability_batch.unbind(0)) if isinstance(probability_batch, torch.Tensor)
+            else list(probability_batch))
+    topologies = []
+    for parents, tokens, all_p in zip(parents_batch, tokens_batch, rows):
+        parents, tokens, max_depth = _topology(parents, tokens)
+        _check_rows(all_p, len(parents), "Sparse-exit Target")
+        if any(token < 0 or token >= all_p.shape[1] for token in tokens):
+            raise ValueError("Tree token is outside the Target vocabulary")
+        if validate:
+            _validate_probabilities(all_p, normalised=True)
+        topologies.append((parents, tokens, max_depth, all_p.shape[1]))
+    if len({vocab for *_, vocab in topologies}) != 1 or len({r.device for r in rows}) != 1:
+        raise ValueError("Sparse-exit batch rows must share vocabulary and device")
+    device = rows[0].device
+    depth = max(t[2] for t in topologies)
+    # Each request consumes 2 * (its max_depth + 1) uniforms from its own
+    # generator, as in the reference; the kernel reads them at stride 2*(depth+1).
+    uniforms = torch.zeros((count, 2 * (depth + 1)), dtype=torch.float64, device=device)
+    for i, ((_, _, d, _), gen) in enumerate(zip(topologies, generators)):
+        uniforms[i, :2 * (d + 1)] = torch.rand(2 * (d + 1), dtype=torch.float64, device=device,
+                                               generator=gen)
+    trees = PackedTrees([t[0] for t in topologies], [t[1] for t in topologies], device)
+    probs = torch.cat([_as_fp32_rows(r) for r in rows], dim=0)
+    out = accept_packed(probs, trees, rule=SG_RULE_SPARSE_EXIT, uniforms=uniforms, max_depth=depth)
+    host = out.tolist()
+    return [decode_output(host[i], depth, topologies[i][3], topologies[i][1], "Sparse-exit sampler")
+            for i in range(count)]
+
+
+def tree_verify_ancestral_same_draw_fused(parents, tokens, all_p, generator=None,
+                                          validate: bool = True):
+    """Reference fused_tree_sampling.py:2376-2414: the reference's multinomial
+    draws (same primitive, shape and order), walked on device."""
+    parents, tokens, max_depth = _topology(parents, tokens)
+    node_count = len(parents)
+    _check_rows(all_p, node_count, "Same-draw DDTree")
+    if any(token < 0 or token >= all_p.shape[1] for token in tokens):
+        raise ValueError("Tree token is outside the Target vocabulary")
+    if validate:
+        _validate_probabilities(all_p, normalised=False)
+    posterior = torch.multinomial(all_p, 1, generator=generator).reshape(-1)
+    trees = PackedTrees([parents], [tokens], all_p.device)
+    out = follow_packed(posterior, trees, max_depth=max_depth)
+    return decode_output(out[0].tolist(), max_depth, all_p.shape[1], tokens,
+                         "Same-draw fused tree walk")
+
+
+def follow_packed(posterior: torch.Tensor, trees: PackedTrees, *, max_depth: int | None = None,
+                  out: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                  stream=None) -> torch.Tensor:
+    depth = trees.max_depth if max_depth is None else int(max_depth)
+    posterior = posterior.to(torch.long).contiguous()
+    if out is None:
+        out = torch.empty((trees.count, depth + 2), dtype=torch.long, device=posterior.device)
+    st = _lib.load().sg_tree_follow(ptr(posterior), ptr(trees.row_offsets), ptr(trees.parents),
+                                    ptr(trees.tokens), trees.count, trees.max_nodes, depth, ptr(out),
+                                    ptr(status), stream_ptr(stream))
+    check(st, "sg_tree_follow")
+    return out
+
+
+def philox_node_uniforms(seed: int, request: int, node: int) -> tuple[float, float]:
+    """Host restatement of the kernel's per-node uniforms (for reproducibility
+    checks): Philox4x32-10, key = seed, counter = (node, request lo, request hi, 0)."""
+    M0, M1, W0, W1 = 0xD2511F53, 0xCD9E8D57, 0x9E3779B9, 0xBB67AE85
+    mask = 0xFFFFFFFF
+    c = [node & mask, request & mask, (request >> 32) & mask, 0]
+    k0, k1 = seed & mask, (seed >> 32) & mask
+    for r in range(10):
+        if r:
+            k0, k1 = (k0 + W0) & mask, (k1 + W1) & mask
+        p0, p1 = M0 * c[0], M1 * c[2]
+        c = [((p1 >> 32) ^ c[1] ^ k0) & mask, p1 & mask, ((p0 >> 32) ^ c[3] ^ k1) & mask, p0 & mask]
+    u = lambda a, b: (((b << 32) | a) >> 11) * (1.0 / 9007199254740992.0)
+    return u(c[0], c[1]), u(c[2], c[3])
+
+
+__all__ = [
+    "PackedTrees", "accept_packed", "follow_packed", "decode_output",
+    "tree_verify_ancestral_fused_scan", "tree_verify_ancestral_sparse_exit_fused_scan",
+    "tree_verify_ancestral_sparse_exit_fused_scan_batched", "tree_verify_ancestral_same_draw_fused",
+    "philox_node_uniforms", "SG_RULE_SCAN", "SG_RULE_SPARSE_EXIT",
+]

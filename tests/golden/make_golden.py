@@ -1,0 +1,280 @@
+"""Generate the golden fixtures under tests/golden/ from the reference itself.
+
+Run in a container where the reference source tree is available:
+
+    python tests/golden/make_golden.py --reference <path to specgrove checkout>
+
+Every expected output below is produced by calling the reference's own
+functions (no restatement):
+
+  accept_scan.npz    ancestral inverse-CDF walk: fused_tree_sampling._topology,
+                     _sample_row_inverse_cdf (fused_tree_sampling.py:2607-2612)
+                     on float64 rows, tree_block_skip.child_for_edge, with the
+                     stop rule of fused_tree_sampling.py:600-620.
+  accept_sparse.npz  sparse-exit walk: child routing by fp64 cumulative child
+                     mass (fused_tree_sampling.py:727-746) and the exit draw of
+                     _sample_row_inverse_cdf on the row with the children zeroed.
+  follow.npz         sampling.tree_verify_ancestral_batched (sampling.py:903-950)
+                     with its `sample` replaced by fixed posterior tokens, as the
+                     reference's own exact-law test does.
+  kv_commit.npz      continuous_tree_block_decode._PersistentRequestCachePool and
+                     append_packed_sequence (:176-261) on random small caches.
+  packed_inputs.npz  continuous_tree_block_decode._packed_block_inputs (:500-546)
+                     on random trees: ids, positions and the additive mask.
+
+The fixtures are small (tens of KB) and deterministic (seeded torch CPU RNG).
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+from pathlib import Path
+from types import SimpleNamespace
+
+import numpy as np
+import torch
+
+OUT = Path(__file__).resolve().parent
+
+
+def random_tree(gen: torch.Generator, n: int, vocab: int, max_children: int = 4,
+                max_depth: int = 8):
+    parents, tokens, depths = [-1], [-1], [0]
+    kids: dict[int, set[int]] = {0: set()}
+    for j in range(1, n):
+        while True:
+            cand = int(torch.randint(0, j, (1,), generator=gen))
+            if len(kids[cand]) < max_children and depths[cand] < max_depth:
+                break
+        while True:
+            tok = int(torch.randint(0, vocab, (1,), generator=gen))
+            if tok not in kids[cand]:
+                break
+        kids[cand].add(tok)
+        kids[j] = set()
+        parents.append(cand)
+        tokens.append(tok)
+        depths.append(depths[cand] + 1)
+    return parents, tokens, depths
+
+
+def tree_rows(gen, parents, tokens, vocab, kind: str):
+    n = len(parents)
+    logits = torch.randn((n, vocab), generator=gen, dtype=torch.float32) * 2.0
+    for j in range(1, n):  # make children likely so walks go deep
+        logits[parents[j], tokens[j]] += float(torch.empty(1).uniform_(2.0, 6.0, generator=gen))
+    probs = torch.softmax(logits, dim=-1)
+    if kind == "sparse_zeros":
+        probs = probs * (torch.rand((n, vocab), generator=gen) > 0.3)
+        probs = probs / probs.sum(-1, keepdim=True)
+    elif kind == "unnormalised":
+        probs = probs * 7.25
+    return probs.to(torch.float32)
+
+
+def build_accept_cases(ref, gen, rule: str):
+    fts = ref.fused
+    cases = []
+    specs = [(1, 64, "softmax"), (2, 64, "softmax"), (5, 64, "softmax"), (9, 500, "softmax"),
+             (17, 300, "softmax"), (8, 1001, "softmax"), (6, 1000, "sparse_zeros"),
+             (20, 256, "softmax"), (33, 256, "softmax"), (4, 2048, "softmax"),
+             (3, 4096, "sparse_zeros")]
+    if rule == "scan":
+        specs += [(13, 300, "unnormalised"), (6, 77, "unnormalised")]
+    for n, vocab, kind in specs:
+        parents, tokens, depths = random_tree(gen, n, vocab)
+        probs = tree_rows(gen, parents, tokens, vocab, kind)
+        _, _, max_depth = fts._topology(parents, tokens[1:])
+        width = (max_depth + 1) * (2 if rule == "sparse" else 1)
+        uniforms = torch.rand(width, dtype=torch.float64, generator=gen)
+        nodes, toks, bonus = reference_walk(ref, parents, tokens, probs, uniforms, max_depth, rule)
+        cases.append(dict(parents=parents, tokens=tokens, probs=probs.numpy(), uniforms=uniforms.numpy(),
+                          max_depth=max_depth, nodes=nodes, bonus=bonus, vocab=vocab))
+    return cases
+
+
+def reference_walk(ref, parents, tokens, probs, uniforms, max_depth, rule):
+    fts, tbs = ref.fused, ref.tbs
+    node, nodes, toks = 0, [], []
+    edge_tokens = tokens[1:]
+    for depth in range(max_depth + 1):
+        row = probs[node].to(torch.float64)
+        if rule == "scan":
+            token = fts._sample_row_inverse_cdf(row, float(uniforms[depth]))
+            child = tbs.child_for_edge(parents, edge_tokens, node, token)
+            if child is not None and depth < max_depth:
+                nodes.append(child)
+                toks.append(token)
+                node = child
+                continue
+            return nodes, toks, token
+        # sparse exit
+        children = [j for j in range(1, len(parents)) if parents[j] == node]
+        cumulative, route = 0.0, None
+        for j in children:
+            cumulative += float(row[edge_tokens[j - 1]])
+            if route is None and float(uniforms[2 * depth]) < cumulative:
+                route = j
+        if route is not None and depth < max_depth:
+            nodes.append(route)
+            toks.append(edge_tokens[route - 1])
+            node = route
+            continue
+        masked = row.clone()
+        for j in children:
+            masked[edge_tokens[j - 1]] = 0.0
+        token = fts._sample_row_inverse_cdf(masked, float(uniforms[2 * depth + 1]))
+        return nodes, toks, token
+    raise AssertionError("walk did not terminate")
+
+
+def pack_cases(cases):
+    offsets = [0]
+    parents, tokens, probs, uniforms, expected = [], [], [], [], []
+    for c in cases:
+        offsets.append(offsets[-1] + len(c["parents"]))
+        parents += c["parents"]
+        tokens += c["tokens"]
+    return np.asarray(offsets, np.int64), np.asarray(parents, np.int64), np.asarray(tokens, np.int64)
+
+
+def save_accept(name: str, cases):
+    offsets, parents, tokens = pack_cases(cases)
+    arrays = {"row_offsets": offsets, "parents": parents, "tokens": tokens}
+    for i, c in enumerate(cases):
+        arrays[f"probs_{i}"] = c["probs"]
+        arrays[f"uniforms_{i}"] = c["uniforms"]
+        arrays[f"max_depth_{i}"] = np.int64(c["max_depth"])
+        arrays[f"nodes_{i}"] = np.asarray(c["nodes"], np.int64)
+        arrays[f"bonus_{i}"] = np.int64(c["bonus"])
+    arrays["count"] = np.int64(len(cases))
+    np.savez_compressed(OUT / name, **arrays)
+
+
+def build_follow(ref, gen):
+    sampling = ref.sampling
+    cases = []
+    for n, vocab in [(1, 16), (4, 8), (9, 32), (17, 64), (40, 128), (64, 50)]:
+        parents, tokens, _ = random_tree(gen, n, vocab)
+        # posterior: mostly a child token so the walk descends, sometimes not
+        posterior = []
+        for j in range(n):
+            kids = [tokens[c] for c in range(1, n) if parents[c] == j]
+            if kids and float(torch.rand(1, generator=gen)) < 0.8:
+                posterior.append(kids[int(torch.randint(0, len(kids), (1,), generator=gen))])
+            else:
+                posterior.append(int(torch.randint(0, vocab, (1,), generator=gen)))
+        fixed = torch.tensor(posterior)
+        original = sampling.sample
+        sampling.sample = lambda probs, generator=None, _f=fixed: _f.clone()
+        try:
+            nodes, toks, bonus = sampling.tree_verify_ancestral_batched(
+                parents, tokens[1:], torch.ones((n, vocab)) / vocab, None, validate=True)
+        finally:
+            sampling.sample = original
+        depth = [0] * n
+        for j in range(1, n):
+            depth[j] = depth[parents[j]] + 1
+        cases.append(dict(parents=parents, tokens=tokens, posterior=posterior, nodes=nodes,
+                          bonus=bonus, max_depth=max(depth)))
+    offsets, parents, tokens = pack_cases(cases)
+    arrays = {"row_offsets": offsets, "parents": parents, "tokens": tokens,
+              "posterior": np.asarray(sum((c["posterior"] for c in cases), []), np.int64),
+              "count": np.int64(len(cases))}
+    for i, c in enumerate(cases):
+        arrays[f"nodes_{i}"] = np.asarray(c["nodes"], np.int64)
+        arrays[f"bonus_{i}"] = np.int64(c["bonus"])
+        arrays[f"max_depth_{i}"] = np.int64(c["max_depth"])
+    np.savez_compressed(OUT / "follow.npz", **arrays)
+
+
+def build_kv_commit(ref, gen):
+    decode = ref.decode
+    heads, dim, layers = 2, 8, 3
+    lengths = [5, 1, 9, 3]
+    capacity = 24
+    sources = []
+    for L in lengths:
+        lay = []
+        for _ in range(layers):
+            k = torch.randn((1, heads, L, dim), generator=gen)
+            v = torch.randn((1, heads, L, dim), generator=gen)
+            lay.append(SimpleNamespace(keys=k, values=v))
+        sources.append(SimpleNamespace(layers=lay, get_seq_length=(lambda L=L: L)))
+    pool = decode._PersistentRequestCachePool(sources, capacity=capacity)
+    before_k = torch.stack(pool.key_storage).clone()
+    before_v = torch.stack(pool.value_storage).clone()
+    rows = [4, 2, 6, 3]
+    q_offsets = [0, 4, 6, 12]
+    total_prefix = sum(lengths)
+    total_q = sum(rows)
+    packed_layers = []
+    for _ in range(layers):
+        k = torch.randn((1, heads, total_prefix + total_q, dim), generator=gen)
+        v = torch.randn((1, heads, total_prefix + total_q, dim), generator=gen)
+        packed_layers.append(SimpleNamespace(keys=k, values=v))
+    packed = SimpleNamespace(layers=packed_layers)
+    keep = [[0, 1, 3], [0], [0, 2, 4, 5], [0, 1]]
+    pool.append_packed_sequence(packed, pool.caches, total_prefix, q_offsets, keep, "cpu")
+    np.savez_compressed(
+        OUT / "kv_commit.npz",
+        before_k=before_k.numpy(), before_v=before_v.numpy(),
+        after_k=torch.stack(pool.key_storage).numpy(), after_v=torch.stack(pool.value_storage).numpy(),
+        packed_k=torch.stack([l.keys[0] for l in packed_layers]).numpy(),
+        packed_v=torch.stack([l.values[0] for l in packed_layers]).numpy(),
+        lengths=np.asarray(lengths, np.int64), capacity=np.int64(capacity),
+        q_offsets=np.asarray(q_offsets, np.int64), packed_old_length=np.int64(total_prefix),
+        keep_flat=np.asarray(sum(keep, []), np.int64),
+        keep_offsets=np.asarray(np.cumsum([0] + [len(k) for k in keep]), np.int64),
+        after_lengths=np.asarray(pool.lengths, np.int64))
+
+
+def build_packed_inputs(ref, gen):
+    decode, tbs, tree_mod = ref.decode, ref.tbs, ref.tree
+    states, blocks, lengths = [], [], []
+    for i, (n, L) in enumerate([(5, 7), (1, 3), (12, 9), (8, 4)]):
+        parents, tokens, depths = random_tree(gen, n, 50)
+        t = tree_mod.Tree(tokens=tokens[1:], parents=parents, depths=depths, path_nodes=[])
+        block = tbs.local_tree_block(t.parents, t.tokens, t.depths, 0, n)
+        st = SimpleNamespace(tree=t, generated=[100 + i], block_root=0, round_prefix_len=L + 2 * i)
+        states.append(st)
+        blocks.append(block)
+        lengths.append(L)
+    offsets = list(np.cumsum([0] + lengths[:-1]))
+    total = sum(lengths)
+    ids, positions, mask, q_offsets = decode._packed_block_inputs(
+        states, blocks, tuple(lengths), tuple(offsets), total, torch.float32, "cpu")
+    np.savez_compressed(
+        OUT / "packed_inputs.npz",
+        ids=ids.numpy(), positions=positions.numpy(), visible=torch.isfinite(mask[0, 0]).numpy(),
+        q_offsets=np.asarray(q_offsets, np.int64), lengths=np.asarray(lengths, np.int64),
+        cache_offsets=np.asarray(offsets, np.int64),
+        parents=np.asarray(sum((list(b.parents) for b in blocks), []), np.int64),
+        tokens=np.asarray(sum(([-1] + list(b.tokens) for b in blocks), []), np.int64),
+        depths=np.asarray(sum((list(b.depths) for b in blocks), []), np.int64),
+        row_counts=np.asarray([len(b.nodes) for b in blocks], np.int64),
+        roots=np.asarray([s.generated[-1] for s in states], np.int64),
+        round_prefix=np.asarray([s.round_prefix_len for s in states], np.int64))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="root of the specgrove checkout")
+    args = ap.parse_args()
+    sys.path.insert(0, str(Path(args.reference) / "code" / "natural" / "src"))
+    from gbv_experiments import continuous_tree_block_decode as decode
+    from gbv_experiments import fused_tree_sampling as fused
+    from gbv_experiments import sampling, tree, tree_block_skip as tbs
+    ref = SimpleNamespace(decode=decode, fused=fused, sampling=sampling, tree=tree, tbs=tbs)
+    gen = torch.Generator().manual_seed(20261201)
+    save_accept("accept_scan.npz", build_accept_cases(ref, gen, "scan"))
+    save_accept("accept_sparse.npz", build_accept_cases(ref, gen, "sparse"))
+    build_follow(ref, gen)
+    build_kv_commit(ref, gen)
+    build_packed_inputs(ref, gen)
+    for p in sorted(OUT.glob("*.npz")):
+        print(p.name, p.stat().st_size)
+
+
+if __name__ == "__main__":
+    main()
