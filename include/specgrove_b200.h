@@ -152,6 +152,27 @@ SG_API int sg_kv_commit_accepted(void* arena, int64_t plane_rows, int64_t num_pl
                           const int64_t* accept_out, int32_t num_trees,
                           int32_t max_depth, int32_t* status, void* stream);
 
+/* Epilogues of sg_gemm_bf16. */
+enum sg_gemm_epilogue {
+  SG_EPI_STORE_BF16 = 0, /* C bf16 [M, ldc] = acc */
+  SG_EPI_STORE_F32 = 1,  /* C fp32 [M, ldc] = acc */
+  SG_EPI_RESIDUAL = 2,   /* C fp32 [M, ldc] += acc; aux bf16 [M, ld_aux] = bf16(C) if aux */
+  SG_EPI_SWIGLU = 3      /* B rows interleaved in 128-row gate/up blocks:
+                            C bf16 [M, N/2] = silu(gate) * up */
+};
+
+/*
+ * tcgen05 GEMM: acc[M, N] = A[M, K] . B[N, K]^T, bf16 operands (row-major,
+ * K contiguous, 16-byte aligned rows), fp32 accumulation in tensor memory,
+ * fused epilogue.  K % 64 == 0, N % 32 == 0.  This is the projection / MLP
+ * GEMM of the target pass (HF Qwen3 q/k/v/o/gate/up/down nn.Linear layers,
+ * called from engine.py:499-517 through transformers' Qwen3Model).
+ */
+SG_API int sg_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb,
+                 void* C, int64_t ldc, int32_t M, int32_t N, int32_t K,
+                 int32_t epilogue, void* aux, int64_t ld_aux, int32_t* status,
+                 void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -41,7 +41,15 @@ _SIGNATURES = {
     "sg_kv_commit_accepted": (ctypes.c_int, [
         c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
         c_int32, c_int32, c_void_p, c_void_p]),
+    "sg_gemm_bf16": (ctypes.c_int, [
+        c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_int32, c_int32,
+        c_void_p, c_int64, c_void_p, c_void_p]),
 }
+
+SG_EPI_STORE_BF16 = 0
+SG_EPI_STORE_F32 = 1
+SG_EPI_RESIDUAL = 2
+SG_EPI_SWIGLU = 3
 
 _lib = None
 

@@ -1,0 +1,360 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a:
+//   acc[M, N] = A[M, K] . B[N, K]^T      (bf16 operands, fp32 accumulate in TMEM)
+// A and B are K-major (row-major with K contiguous), as packed activation rows
+// and nn.Linear weights are.  Tiles are 128 x 256 with K-blocks of 64:
+//   warp 0      TMA producer: A/B tiles -> 128B-swizzled shared memory ring
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=256, K=16)
+//               into one of two TMEM accumulators (2 x 256 columns)
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (32 rows per warp),
+//               apply the fused epilogue, store; frees the accumulator so the
+//               next tile's MMAs overlap this tile's epilogue.
+// Tiles are visited n-major (all M tiles of a weight panel back to back) so a
+// weight panel is read from HBM once and served from L2 to the other M tiles.
+#pragma once
+
+#include "sm100.cuh"
+
+namespace sg {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_TILE = BM * BK * 2;
+constexpr int B_TILE = BN * BK * 2;
+constexpr int STAGE_BYTES = A_TILE + B_TILE;
+constexpr int THREADS = 192;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr int BARRIER_BYTES = 256;
+constexpr size_t SMEM_BYTES = static_cast<size_t>(STAGES) * STAGE_BYTES + 1024 + BARRIER_BYTES;
+constexpr uint32_t IDESC = sm100::idesc_bf16_f32(BM, BN);
+
+struct Shape {
+  int M, N, K;
+  int m_tiles, n_tiles, k_blocks, tiles;
+};
+
+inline Shape make_shape(int M, int N, int K) {
+  Shape s;
+  s.M = M;
+  s.N = N;
+  s.K = K;
+  s.m_tiles = (M + BM - 1) / BM;
+  s.n_tiles = (N + BN - 1) / BN;
+  s.k_blocks = K / BK;
+  s.tiles = s.m_tiles * s.n_tiles;
+  return s;
+}
+
+__device__ __forceinline__ void tile_coords(const Shape& s, int tile, int& m0, int& n0) {
+  m0 = (tile % s.m_tiles) * BM;
+  n0 = (tile / s.m_tiles) * BN;
+}
+
+// Epi must provide:
+//   struct Params;  (int32_t* status member)
+//   static __device__ void apply(const Params&, const Shape&, uint32_t taddr,
+//                                int row, int m0, int n0, int quarter, int lane);
+template <class Epi>
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+            const Shape shape, const typename Epi::Params ep) {
+  using namespace sm100;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_TILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = bars + 2 * STAGES + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tensormap(&tma_a);
+    prefetch_tensormap(&tma_b);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  auto fail_wait = [&](void) {
+    *abort_flag = 1;
+    if (ep.status != nullptr) atomicMax(ep.status, static_cast<int32_t>(SG_ERR_CUDA));
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < shape.tiles && !*abort_flag; tile += gridDim.x) {
+        int m0, n0;
+        tile_coords(shape, tile, m0, n0);
+        for (int kb = 0; kb < shape.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u)) {
+            fail_wait();
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          tma_load_2d(sA + stage * A_TILE, &tma_a, kb * BK, m0, &full[stage]);
+          tma_load_2d(sB + stage * B_TILE, &tma_b, kb * BK, n0, &full[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = blockIdx.x; tile < shape.tiles && !*abort_flag; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u)) {
+          fail_wait();
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < shape.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase)) {
+            fail_wait();
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * A_TILE);
+          const uint32_t b_base = smem_u32(sB + stage * B_TILE);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_bf16(d, desc_k_sw128(a_base + k * 32), desc_k_sw128(b_base + k * 32), IDESC,
+                     (kb | k) != 0 ? 1u : 0u);
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+  } else {
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < shape.tiles; tile += gridDim.x) {
+      if (*abort_flag) break;
+      if (!mbar_wait(&tfull[acc], acc_phase)) {
+        fail_wait();
+        break;
+      }
+      tc_fence_after();
+      int m0, n0;
+      tile_coords(shape, tile, m0, n0);
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      Epi::apply(ep, shape, taddr, m0 + quarter * 32 + lane, m0, n0, quarter, lane);
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// --------------------------------------------------------------- epilogues
+
+// C (bf16, row stride ldc) = acc
+struct EpiStoreBf16 {
+  struct Params {
+    __nv_bfloat16* out;
+    int64_t ldo;
+    int32_t* status;
+  };
+  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int row, int,
+                                               int n0, int, int) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int col = n0 + c * 32;
+      if (col >= s.N) break;
+      float v[32];
+      sm100::tmem_ld32(taddr + c * 32, v);
+      if (row < s.M) {
+        uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(row) * p.ldo + col);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = sm100::pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+          w.y = sm100::pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+          w.z = sm100::pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+          w.w = sm100::pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+          dst[q] = w;
+        }
+      }
+    }
+  }
+};
+
+// C (fp32) = acc
+struct EpiStoreF32 {
+  struct Params {
+    float* out;
+    int64_t ldo;
+    int32_t* status;
+  };
+  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int row, int,
+                                               int n0, int, int) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int col = n0 + c * 32;
+      if (col >= s.N) break;
+      float v[32];
+      sm100::tmem_ld32(taddr + c * 32, v);
+      if (row < s.M) {
+        float4* dst = reinterpret_cast<float4*>(p.out + static_cast<int64_t>(row) * p.ldo + col);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+      }
+    }
+  }
+};
+
+// Residual stream update: x (fp32) += acc, and x_bf16 = bf16(x) for the next GEMM.
+struct EpiResidual {
+  struct Params {
+    float* x;
+    int64_t ldx;
+    __nv_bfloat16* x_bf16;  // may be null
+    int64_t ldb;
+    int32_t* status;
+  };
+  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int row, int,
+                                               int n0, int, int) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int col = n0 + c * 32;
+      if (col >= s.N) break;
+      float v[32];
+      sm100::tmem_ld32(taddr + c * 32, v);
+      if (row < s.M) {
+        float4* xr = reinterpret_cast<float4*>(p.x + static_cast<int64_t>(row) * p.ldx + col);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 x = xr[q];
+          x.x += v[q * 4];
+          x.y += v[q * 4 + 1];
+          x.z += v[q * 4 + 2];
+          x.w += v[q * 4 + 3];
+          xr[q] = x;
+          v[q * 4] = x.x;
+          v[q * 4 + 1] = x.y;
+          v[q * 4 + 2] = x.z;
+          v[q * 4 + 3] = x.w;
+        }
+        if (p.x_bf16 != nullptr) {
+          uint4* dst = reinterpret_cast<uint4*>(p.x_bf16 + static_cast<int64_t>(row) * p.ldb + col);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = sm100::pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+            w.y = sm100::pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+            w.z = sm100::pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+            w.w = sm100::pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+            dst[q] = w;
+          }
+        }
+      }
+    }
+  }
+};
+
+// SwiGLU on a weight whose rows are interleaved in 128-row blocks
+// [gate_0..127, up_0..127, gate_128..255, up_128..255, ...]: each 256-column
+// tile holds matching gate and up columns; out[row, n0/2 + j] = silu(g_j) * u_j.
+struct EpiSwiGlu {
+  struct Params {
+    __nv_bfloat16* out;
+    int64_t ldo;
+    int32_t* status;
+  };
+  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int row, int,
+                                               int n0, int, int) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 64; ++c) {
+      float g[32], u[32];
+      sm100::tmem_ld32(taddr + c * 32, g);
+      sm100::tmem_ld32(taddr + BN / 2 + c * 32, u);
+      const int col = n0 / 2 + c * 32;
+      if (row < s.M && n0 < s.N) {
+        uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(row) * p.ldo + col);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float h[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float gv = g[q * 8 + e];
+            h[e] = gv / (1.0f + __expf(-gv)) * u[q * 8 + e];
+          }
+          uint4 w;
+          w.x = sm100::pack_bf16x2(h[0], h[1]);
+          w.y = sm100::pack_bf16x2(h[2], h[3]);
+          w.z = sm100::pack_bf16x2(h[4], h[5]);
+          w.w = sm100::pack_bf16x2(h[6], h[7]);
+          dst[q] = w;
+        }
+      }
+    }
+  }
+};
+
+// Host launcher: persistent grid of min(tiles, SMs) CTAs.
+template <class Epi>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Shape& shape, const typename Epi::Params& ep,
+           cudaStream_t stream) {
+  static int configured_device_mask = 0;
+  int dev = 0;
+  SG_CUDA_CHECK(cudaGetDevice(&dev));
+  if (!(configured_device_mask & (1 << dev))) {
+    SG_CUDA_CHECK(cudaFuncSetAttribute(gemm_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(SMEM_BYTES)));
+    configured_device_mask |= (1 << dev);
+  }
+  const int sms = device_sm_count();
+  const int grid = shape.tiles < sms ? shape.tiles : sms;
+  if (grid <= 0) return SG_OK;
+  gemm_kernel<Epi><<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, shape, ep);
+  return check_launch("gemm_kernel");
+}
+
+}  // namespace gemm
+}  // namespace sg
