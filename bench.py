@@ -1,18 +1,24 @@
 """Benchmark of the specgrove_b200 packed tree-verification step.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload accept]
+                    [--workload verify|verify4b|accept]
 
 One JSON line is printed by rank 0.  Under torchrun (N > 1) every rank runs
-its own shard of requests (data parallel, no data-path collective); the step
-time is the max over ranks of the CUDA-event time, and `value` aggregates the
-units of all ranks.
+its own shard of requests with a full model replica (data parallel, no
+data-path collective; weak scaling); the step time is the max over ranks of
+the CUDA-event time and `value` aggregates the accepted tokens of all ranks.
 
-Workload `accept` (acceptance sweep): 64 request trees, 4096 packed nodes,
-vocabulary 151936, fp32 target probabilities (inputs 2.49 GB, larger than L2),
-then the accepted-path KV commit of 36 layers x 8 kv heads x 128 bf16.  One
-step = one acceptance launch (Philox uniforms keyed by (seed=step, request,
-node)) + one commit launch, both on device with no host round trip.
+Workload `verify` (default): Qwen3-8B shape
+(36 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128, intermediate 12288,
+vocab 151936), random-init bf16 weights, 64 requests per GPU with cache
+prefixes uniform in [1024, 4096] (synthetic KV), one canonical best-first
+tree per request cut to its tier (tier mix 40x16 + 12x32 + 8x64 + 4x128 rows
+= 2048 rows).  One step = one packed verify pass: target forward over the
+2048 rows, LM head fused with online softmax and Gumbel-max sampling, tree
+walk, and commit of the accepted rows' KV.  Weights (16.4 GB) and KV
+(~24 GB read per step) are far larger than L2, so no flush is needed.
+`verify4b` is configuration 3 (Qwen3-4B shape, 16 requests, 512 rows);
+`accept` is the kernel-isolated acceptance sweep (configuration 2).
 """
 from __future__ import annotations
 
@@ -188,6 +194,184 @@ class AcceptWorkload:
         return int((outs[..., self.D] + 1).sum())
 
 
+class VerifyWorkload:
+    def __init__(self, rank: int, config: str):
+        from specgrove_b200 import workloads
+        from specgrove_b200.engine import QWEN3_4B, QWEN3_8B, B200Engine, Wave, Weights
+        if config == "verify4b":
+            self.shape, mix, prefix = QWEN3_4B, workloads.TIER_MIX_CONFIG3, (512, 2048)
+            self.name = "config3: Qwen3-4B shape, 16 requests, prefixes U[512,2048], tiers {16,32,64}, 512 rows"
+        else:
+            self.shape, mix, prefix = QWEN3_8B, workloads.TIER_MIX_CONFIG4, (1024, 4096)
+            self.name = "config4: Qwen3-8B shape, 64 requests, prefixes U[1024,4096], tiers {16,32,64,128}, 2048 rows"
+        self.weights = Weights.random(self.shape, seed=1234)           # full replica on every rank
+        self.wl = workloads.verify_workload(self.shape.vocab, mix, prefix, seed=rank)
+        R = len(self.wl.trees)
+        rows = sum(len(t[0]) for t in self.wl.trees)
+        self.capacity = prefix[1] + max(self.wl.tiers) + 16
+        self.engine = B200Engine(self.weights, num_slots=R, capacity=self.capacity, max_rows=rows)
+        g = torch.Generator(device="cuda").manual_seed(rank)
+        self.engine.arena.storage.normal_(0.0, 1.0, generator=g)       # synthetic cache prefixes
+        self.wave = Wave(self.wl.trees, list(range(R)), self.wl.cache_lengths,
+                         request_ids=[rank * 1_000_000 + i for i in range(R)])
+        self.dw = self.wave.to("cuda")
+        self.R, self.rows, self.D = R, rows, self.wave.max_depth
+        self.lengths_out = torch.empty(R, dtype=torch.long, device="cuda")
+
+    def step(self, seed: int, out: torch.Tensor, trace=None):
+        self.engine.verify_device(self.dw, seed=seed, commit=True, accept_out=out, lengths_out=self.lengths_out,
+                                  trace=trace)
+
+    def units(self, outs: torch.Tensor) -> int:
+        return int((outs[..., self.D] + 1).sum())
+
+    def attention_bytes(self) -> float:
+        s = self.shape
+        per_token = s.num_kv_heads * s.head_dim * 2 * 2
+        return float(sum((L + len(t[0])) * per_token for L, t in zip(self.wl.cache_lengths, self.wl.trees)))
+
+    def pass_flops(self) -> float:
+        s = self.shape
+        f = self.rows * s.gemm_flops_per_row()
+        for L, (par, _) in zip(self.wl.cache_lengths, self.wl.trees):
+            depth = [0] * len(par)
+            for j in range(1, len(par)):
+                depth[j] = depth[par[j]] + 1
+            f += sum(s.attention_flops(L + d + 1) for d in depth)
+        return float(f)
+
+
+def make_events(n):
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+    for e in evs:           # materialise the cudaEvent_t handles
+        e.record()
+    torch.cuda.synchronize()
+    return evs
+
+
+def run_verify(args, world, rank):
+    from specgrove_b200 import _lib
+    from specgrove_b200.engine import TRACE_EVENTS, TRACE_STAGES
+    hbm, tc, tc_sus, peak_kind = peaks()
+    wl = VerifyWorkload(rank, args.workload)
+    K, W = args.steps, args.warmup
+    outs = torch.empty((K, wl.R, wl.D + 2), dtype=torch.long, device="cuda")
+    warm = torch.empty((wl.R, wl.D + 2), dtype=torch.long, device="cuda")
+    for i in range(W):
+        wl.step(10_000 + i, warm)
+    torch.cuda.synchronize()
+    traces = [make_events(TRACE_EVENTS) for _ in range(K)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = _lib.launch_count()
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(K):
+            wl.step(i, outs[i], traces[i])
+        stop.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    launches = _lib.launch_count() - launches0
+    if int(wl.engine.status) != 0:
+        raise RuntimeError(f"device status {int(wl.engine.status)}")
+    ms = max_over_ranks(start.elapsed_time(stop) / K, world)
+    total_units = sum_over_ranks(wl.units(outs), world)
+    value = total_units / (ms * K / 1000.0)
+    stages = {name: statistics.mean(t[i].elapsed_time(t[i + 1]) for t in traces)
+              for i, name in enumerate(TRACE_STAGES)}
+    attn_ms = stages["L0 attention"]
+    attn_bytes = wl.attention_bytes()                  # one layer's K/V reads
+    attn_gbs = attn_bytes / (attn_ms / 1000) / 1e9
+    flops = wl.pass_flops()
+    pass_tflops = flops / (ms / 1000) / 1e12
+    e2e = e2e_verify(wl, args, world)
+    cpu = cpu_baseline_verify(wl) if (rank == 0 and world == 1 and not args.no_cpu) else None
+    clk = clocks.summary()
+    line = {
+        "metric": "accepted tokens/s/GPU", "value": value, "unit": "accepted tokens/s",
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, "
+        "synthetic KV prefixes, seeded best-first trees)",
+        "config": {"workload": wl.name, "model": "Qwen3-8B shape" if wl.shape.hidden == 4096 else "Qwen3-4B shape",
+                   "requests_per_gpu": wl.R, "rows_per_gpu": wl.rows, "global_batch_rows": wl.rows * world,
+                   "verify_pass_us_per_row": ms * 1000 / wl.rows, "temperature": 1.0,
+                   "parallelism": f"dp{world}", "l2": "inputs larger than L2 (16.4 GB weights, ~24 GB KV/step)"},
+        "roofline": {"bound": "hbm", "kernel": "tree_attention_kernel (layer 0)", "achieved": attn_gbs,
+                     "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": attn_gbs / hbm, "traffic": None,
+                     "algorithmic_bytes_per_launch": attn_bytes, "launch_ms": attn_ms,
+                     "pass": {"bound": "tensor", "achieved": pass_tflops, "peak": tc_sus, "unit": "TFLOP/s",
+                              "frac": pass_tflops / tc_sus, "algorithmic_flops_per_step": flops,
+                              "peak_kind": peak_kind + " sustained"}},
+        "stages_ms": {k: round(v, 4) for k, v in stages.items()},
+        "cpu_baseline": cpu, "clocks": clk, "e2e": e2e, "gpu_launches": launches,
+    }
+    return line
+
+
+def e2e_verify(wl, args, world):
+    """Through the public API with host buffers: the wave (tree metadata,
+    tokens, lengths) is copied from pinned host memory, the pass runs, the
+    decisions are read back, every step."""
+    host = wl.wave.host.pin_memory()
+    dev = wl.dw.buf
+    out_dev = torch.empty((wl.R, wl.D + 2), dtype=torch.long, device="cuda")
+    out_host = torch.empty_like(out_dev, device="cpu").pin_memory()
+    steps = max(3, min(args.steps, 10))
+
+    def one(seed):
+        dev.copy_(host, non_blocking=True)
+        wl.step(seed, out_dev)
+        out_host.copy_(out_dev, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return int((out_host[:, wl.D] + 1).sum())
+
+    one(777)
+    barrier(world)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    units = 0
+    start.record()
+    for i in range(steps):
+        units += one(50_000 + i)
+    stop.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(stop) / steps, world)
+    total = sum_over_ranks(units, world)
+    return {"value": total / (ms * steps / 1000.0), "unit": "accepted tokens/s",
+            "h2d_bytes_per_step": host.numel() * 8, "d2h_bytes_per_step": out_host.numel() * 8,
+            "steps": steps, "ms_per_step": ms}
+
+
+def cpu_baseline_verify(wl, requests: int = 4, budget_s: float = 20.0):
+    """The reference's step restated on the host (oracle/forward.py: torch fp32
+    target pass with the packed tree mask, fp32 softmax, fp64 walk) on a
+    bounded slice: the first `requests` requests of the wave, all layers."""
+    from oracle.forward import CpuWeights, verify_step
+    torch.set_num_threads(os.cpu_count())
+    cw = CpuWeights(wl.weights)
+    trees = wl.wl.trees[:requests]
+    lengths = wl.wl.cache_lengths[:requests]
+    store = wl.engine.arena
+    prefixes = []
+    for i, L in enumerate(lengths):
+        base = i * store.capacity
+        prefixes.append([(store.key_storage[l][:, base:base + L].float().cpu(),
+                          store.value_storage[l][:, base:base + L].float().cpu())
+                         for l in range(wl.shape.num_layers)])
+    rows = sum(len(t[0]) for t in trees)
+    units, seconds, reps = 0, 0.0, 0
+    while reps < 1 or (seconds < budget_s and reps < 5):
+        t0 = time.perf_counter()
+        res, _ = verify_step(cw, prefixes, trees, lengths, seed=reps)
+        seconds += time.perf_counter() - t0
+        units += sum(len(nodes) + 1 for nodes, _ in res)
+        reps += 1
+    return {"value": units / seconds, "unit": "accepted tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "us_per_row": seconds / reps / rows * 1e6,
+            "sample": f"{reps} step(s) of {requests} requests ({rows} rows), all {wl.shape.num_layers} layers, "
+                      f"torch fp32 on {torch.get_num_threads()} threads"}
+
+
 def run_b200(args, world, rank):
     from specgrove_b200 import _lib
     hbm, tc, tc_sus, peak_kind = peaks()
@@ -316,13 +500,21 @@ def cpu_baseline_accept(wl, arith=None):
 
 
 def run_reference(args, world, rank):
+    """The reference's CPU path for the same workload and metric: the oracle
+    port (the reference's step restated in torch fp32 / C), all host cores."""
     if rank != 0:
         return None
-    wl = AcceptWorkload(rank)
-    cpu = cpu_baseline_accept(wl)
+    if args.workload == "accept":
+        wl = AcceptWorkload(rank)
+        cpu = cpu_baseline_accept(wl)
+        dtype = "fp64"
+    else:
+        wl = VerifyWorkload(rank, args.workload)
+        cpu = cpu_baseline_verify(wl, requests=2, budget_s=10.0)
+        dtype = "fp32"
     line = {"impl": "reference", "metric": "accepted tokens/s/GPU", "value": cpu["value"],
             "unit": "accepted tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp64",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
             "data": "synthetic", "config": {"workload": wl.name, "parallelism": "cpu"},
             "cpu_baseline": cpu, "e2e": {"value": cpu["value"], "unit": "accepted tokens/s",
                                          "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -335,13 +527,19 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="accept", choices=["accept"])
+    ap.add_argument("--workload", default="verify", choices=["verify", "verify4b", "accept"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = dist_setup(args)
     try:
-        line = run_reference(args, world, rank) if args.impl == "reference" else run_b200(args, world, rank)
+        if args.impl == "reference":
+            line = run_reference(args, world, rank)
+        elif args.workload == "accept":
+            line = run_b200(args, world, rank)
+        else:
+            line = run_verify(args, world, rank)
         if rank == 0 and line is not None:
             print(json.dumps(line), flush=True)
     finally:

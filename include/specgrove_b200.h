@@ -173,6 +173,97 @@ SG_API int sg_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb,
                  int32_t epilogue, void* aux, int64_t ld_aux, int32_t* status,
                  void* stream);
 
+/* ------------------------------------------------------------------------
+ * The packed tree-verification pass (Qwen3 decoder shape).
+ * ------------------------------------------------------------------------ */
+
+/* Per-layer weight pointers, in this order, W_COUNT = 8 per layer:
+ *   0 input RMSNorm [hidden] bf16
+ *   1 fused q|k|v projection [(nq + 2 nkv) * head_dim, hidden] bf16
+ *   2 q RMSNorm [head_dim] bf16      3 k RMSNorm [head_dim] bf16
+ *   4 o projection [hidden, nq * head_dim] bf16
+ *   5 post-attention RMSNorm [hidden] bf16
+ *   6 gate|up projection, rows interleaved in 128-row blocks
+ *     (gate 0..127, up 0..127, gate 128..255, ...) [2 * intermediate, hidden]
+ *   7 down projection [hidden, intermediate] bf16
+ * (HF Qwen3DecoderLayer: input_layernorm, self_attn.{q,k,v}_proj,
+ *  self_attn.{q,k}_norm, self_attn.o_proj, post_attention_layernorm,
+ *  mlp.{gate,up}_proj, mlp.down_proj.) */
+#define SG_LAYER_WEIGHTS 8
+
+typedef struct {
+  int32_t num_layers, hidden, num_q_heads, num_kv_heads, head_dim, intermediate, vocab;
+  float rms_eps;
+  const void* embed;        /* [vocab, hidden] bf16 */
+  const void* final_norm;   /* [hidden] bf16 */
+  const void* lm_head;      /* [vocab, hidden] bf16 */
+  const float* inv_freq;    /* [head_dim / 2] rotary inverse frequencies */
+  const void* const* layers;/* host array [num_layers * SG_LAYER_WEIGHTS] of device pointers */
+} sg_model_desc;
+
+/* Persistent KV arena: bf16 [num_layers, 2 (K, V), num_kv_heads,
+ * num_slots * capacity, head_dim]; request slot s owns rows
+ * [s * capacity, (s + 1) * capacity) of every plane (the layout of
+ * _PersistentRequestCachePool.key_storage / value_storage,
+ * continuous_tree_block_decode.py:176-213, in one allocation). */
+typedef struct {
+  void* storage;
+  int64_t num_slots, capacity;
+} sg_arena_desc;
+
+/* One wave: every request's tree rows packed back to back. */
+typedef struct {
+  int32_t num_requests, num_rows, max_rows_per_request, max_depth;
+  const int64_t* row_offsets;    /* [R + 1] */
+  const int64_t* parents;        /* [Q] local parent, -1 for the root */
+  const int64_t* tokens;         /* [Q] input token (root row: last committed token) */
+  const int64_t* slots;          /* [R] arena slot */
+  const int64_t* cache_lengths;  /* [R] committed KV rows L_i */
+  const int64_t* position_base;  /* [R] rotary position of the root row */
+  const int64_t* request_ids;    /* [R] Philox key per request (NULL: index) */
+  uint64_t seed;
+  float temperature;
+  int32_t commit;                /* 1: move accepted rows' KV to L_i.. */
+  int64_t* accept_out;           /* [R, max_depth + 2] reference layout */
+  int64_t* lengths_out;          /* [R] L_i + accepted + 1 (commit) */
+  int64_t* posterior;            /* optional [Q] sampled token per row */
+  float* lse;                    /* optional [Q] log-normaliser per row */
+  float* child_logprob;          /* optional [Q] log p_parent(token), 0 at roots */
+  float* hidden_out;             /* optional [Q, hidden] fp32 last residual stream */
+  int32_t* status;               /* optional device status word */
+  void* const* trace_events;     /* optional host array of SG_TRACE_EVENTS
+                                    cudaEvent_t recorded at stage boundaries */
+} sg_wave_desc;
+
+/* Stage boundaries recorded into sg_wave_desc.trace_events (the stage
+ * timings of the reference's StageMeter, engine.py:151-177, at kernel
+ * granularity; layer-0 boundaries time each per-layer kernel once):
+ *  0 start  1 tree metadata + embedding  2 L0 input norm  3 L0 QKV GEMM
+ *  4 L0 q/k norm + RoPE + KV tail write  5 L0 tree attention  6 L0 O GEMM
+ *  7 L0 post norm  8 L0 gate/up GEMM  9 L0 down GEMM  10 all layers
+ *  11 final norm  12 LM head + sampling GEMM  13 combine (+ child log-probs)
+ *  14 tree walk  15 commit (end) */
+#define SG_TRACE_EVENTS 16
+
+/* Builds TMA descriptors for every weight and allocates the activation
+ * workspace for up to max_rows packed rows (cudaMalloc, freed by destroy). */
+SG_API int sg_engine_create(const sg_model_desc* model, const sg_arena_desc* arena,
+                     int32_t max_rows, int32_t max_requests, void** engine_out);
+SG_API int sg_engine_destroy(void* engine);
+SG_API size_t sg_engine_workspace_bytes(void* engine);
+
+/*
+ * One packed tree-verification step, enqueued on `stream` with no host
+ * synchronisation (capturable in a CUDA graph): target forward over the
+ * packed rows with request-isolated tree attention reading the arena, new
+ * K/V written at each request's arena tail, LM head fused with online
+ * softmax and Gumbel-max sampling (one posterior draw per row: the law of
+ * sampling.py:903-950), tree walk into accept_out, optional commit.
+ * Replaces continuous_tree_block_decode.py:1748-2129 (pack, target,
+ * select_commit stages).
+ */
+SG_API int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,355 @@
+// The packed tree-verification pass: one target forward over every request's
+// selected tree rows, fused LM head + sampling, tree walk and KV commit.
+//
+// Reference call chain replaced (continuous_tree_block_decode.py:1748-2246):
+//   _pack_cache_sequence (:313-361)  -> not needed: attention reads the arena
+//   _packed_block_inputs (:500-546)  -> tree_meta_kernel (bitsets, positions)
+//   engine.target_hidden_forward     -> embed + 36 x {norm, QKV GEMM, q/k norm
+//     (engine.py:499-517)               + RoPE + arena tail write, tree
+//                                       attention, O GEMM + residual, norm,
+//                                       gate/up GEMM + SwiGLU, down GEMM +
+//                                       residual}
+//   lm_head + probabilities          -> LM-head GEMM with online softmax and
+//     (:1809-1824)                      Gumbel-max sampling epilogue
+//   verifier (:1965-2107)            -> tree walk over the sampled tokens
+//   append_packed_sequence (:2121)   -> in-place arena commit
+#include <cuda_bf16.h>
+
+#include <memory>
+#include <vector>
+
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "layers.cuh"
+
+namespace sg {
+
+
+namespace {
+
+enum { W_IN_NORM = 0, W_QKV, W_Q_NORM, W_K_NORM, W_O, W_POST_NORM, W_GATE_UP, W_DOWN, W_COUNT };
+
+struct LayerMaps {
+  CUtensorMap qkv, o, gate_up, down;
+};
+
+struct Engine {
+  sg_model_desc model;
+  std::vector<const void*> layer_ptrs;
+  sg_arena_desc arena;
+  int max_rows, max_requests;
+  int device;
+  // tensor maps
+  std::vector<LayerMaps> maps;
+  CUtensorMap lm_map, xn_map, attn_map, h_map, kv_map;
+  // workspace
+  void* workspace = nullptr;
+  size_t workspace_bytes = 0;
+  float* x;
+  __nv_bfloat16 *xn, *qkv, *q, *attn, *h;
+  float4* partials;
+  float* lse_ws;
+  int64_t* posterior_ws;
+  layers::RowMeta meta;
+  int vocab_tiles;
+};
+
+template <typename T>
+T* carve(uint8_t*& cursor, size_t count) {
+  uintptr_t p = (reinterpret_cast<uintptr_t>(cursor) + 255) & ~uintptr_t(255);
+  cursor = reinterpret_cast<uint8_t*>(p + count * sizeof(T));
+  return reinterpret_cast<T*>(p);
+}
+
+inline void trace(const sg_wave_desc& w, int point, cudaStream_t stream) {
+  if (w.trace_events != nullptr && w.trace_events[point] != nullptr)
+    cudaEventRecord(static_cast<cudaEvent_t>(w.trace_events[point]), stream);
+}
+
+size_t workspace_size(const sg_model_desc& m, int rows) {
+  const size_t H = m.hidden, D = m.head_dim, I = m.intermediate;
+  const size_t qkv = (m.num_q_heads + 2 * m.num_kv_heads) * D;
+  const size_t vt = (m.vocab + gemm::BN - 1) / gemm::BN;
+  size_t s = 0;
+  s += rows * H * 4 + 256;                    // x
+  s += rows * H * 2 + 256;                    // xn
+  s += rows * qkv * 2 + 256;                  // qkv
+  s += rows * m.num_q_heads * D * 2 + 256;    // q
+  s += rows * m.num_q_heads * D * 2 + 256;    // attn
+  s += rows * I * 2 + 256;                    // h
+  s += rows * vt * 16 + 256;                  // partials
+  s += rows * 4 + 256;                        // lse
+  s += rows * 8 + 256;                        // posterior
+  s += rows * layers::kAncWords * 4 + 256;    // anc
+  s += rows * 4 * 3 + 3 * 256;                // position, tree, local
+  s += rows * 8 + 256;                        // request id
+  return s + 4096;
+}
+
+int check_model(const sg_model_desc& m) {
+  if (m.num_layers < 1 || m.hidden < 64 || m.num_q_heads < 1 || m.num_kv_heads < 1 ||
+      m.num_q_heads % m.num_kv_heads != 0 || (m.head_dim != 64 && m.head_dim != 128) || m.intermediate < 64 ||
+      m.vocab < 32)
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_engine_create: bad model shape");
+  if (m.hidden % gemm::BK != 0 || (m.num_q_heads * m.head_dim) % gemm::BK != 0 ||
+      m.intermediate % gemm::BK != 0 || (2 * m.intermediate) % gemm::BN != 0 || m.vocab % 32 != 0 ||
+      m.hidden % 32 != 0)
+    return fail(SG_ERR_UNSUPPORTED, "sg_engine_create: shape not tileable (hidden, q width, intermediate % 64, "
+                                    "2*intermediate % 256, vocab % 32)");
+  if (m.embed == nullptr || m.final_norm == nullptr || m.lm_head == nullptr || m.inv_freq == nullptr ||
+      m.layers == nullptr)
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_engine_create: null weight");
+  return SG_OK;
+}
+
+}  // namespace
+}  // namespace sg
+
+using sg::Engine;
+
+extern "C" int sg_engine_create(const sg_model_desc* model, const sg_arena_desc* arena, int32_t max_rows,
+                                int32_t max_requests, void** engine_out) {
+  using namespace sg;
+  if (model == nullptr || arena == nullptr || engine_out == nullptr)
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_engine_create: null argument");
+  *engine_out = nullptr;
+  int st = check_model(*model);
+  if (st != SG_OK) return st;
+  if (max_rows < 1 || max_requests < 1 || arena->storage == nullptr || arena->num_slots < 1 || arena->capacity < 1)
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_engine_create: bad sizes");
+  std::unique_ptr<Engine> e(new Engine());
+  e->model = *model;
+  e->layer_ptrs.assign(model->layers, model->layers + static_cast<size_t>(model->num_layers) * W_COUNT);
+  e->model.layers = e->layer_ptrs.data();
+  e->arena = *arena;
+  e->max_rows = max_rows;
+  e->max_requests = max_requests;
+  SG_CUDA_CHECK(cudaGetDevice(&e->device));
+  const sg_model_desc& m = e->model;
+  const int H = m.hidden, D = m.head_dim, I = m.intermediate;
+  const int qkv_n = (m.num_q_heads + 2 * m.num_kv_heads) * D;
+  const int qw = m.num_q_heads * D;
+  for (int l = 0; l < m.num_layers; ++l)
+    for (int w = 0; w < W_COUNT; ++w)
+      if (e->layer_ptrs[l * W_COUNT + w] == nullptr) return fail(SG_ERR_INVALID_ARGUMENT, "null layer weight");
+  e->maps.resize(m.num_layers);
+  for (int l = 0; l < m.num_layers; ++l) {
+    const void* const* lw = &e->layer_ptrs[l * W_COUNT];
+    LayerMaps& lm = e->maps[l];
+    if ((st = make_tmap_2d_bf16(&lm.qkv, lw[W_QKV], H, qkv_n, H * 2, gemm::BK, gemm::BN)) != SG_OK) return st;
+    if ((st = make_tmap_2d_bf16(&lm.o, lw[W_O], qw, H, qw * 2, gemm::BK, gemm::BN)) != SG_OK) return st;
+    if ((st = make_tmap_2d_bf16(&lm.gate_up, lw[W_GATE_UP], H, 2 * I, H * 2, gemm::BK, gemm::BN)) != SG_OK)
+      return st;
+    if ((st = make_tmap_2d_bf16(&lm.down, lw[W_DOWN], I, H, I * 2, gemm::BK, gemm::BN)) != SG_OK) return st;
+  }
+  if ((st = make_tmap_2d_bf16(&e->lm_map, m.lm_head, H, m.vocab, H * 2, gemm::BK, gemm::BN)) != SG_OK) return st;
+  {
+    const uint64_t plane_rows = static_cast<uint64_t>(arena->num_slots) * arena->capacity;
+    const uint64_t planes = static_cast<uint64_t>(m.num_layers) * 2 * m.num_kv_heads;
+    if ((st = make_tmap_3d_bf16(&e->kv_map, arena->storage, D, plane_rows, planes, D * 2, plane_rows * D * 2, 64,
+                                128)) != SG_OK)
+      return st;
+  }
+
+  e->workspace_bytes = workspace_size(m, max_rows);
+  SG_CUDA_CHECK(cudaMalloc(&e->workspace, e->workspace_bytes));
+  uint8_t* cur = static_cast<uint8_t*>(e->workspace);
+  e->x = carve<float>(cur, static_cast<size_t>(max_rows) * H);
+  e->xn = carve<__nv_bfloat16>(cur, static_cast<size_t>(max_rows) * H);
+  e->qkv = carve<__nv_bfloat16>(cur, static_cast<size_t>(max_rows) * qkv_n);
+  e->q = carve<__nv_bfloat16>(cur, static_cast<size_t>(max_rows) * qw);
+  e->attn = carve<__nv_bfloat16>(cur, static_cast<size_t>(max_rows) * qw);
+  e->h = carve<__nv_bfloat16>(cur, static_cast<size_t>(max_rows) * I);
+  e->vocab_tiles = (m.vocab + gemm::BN - 1) / gemm::BN;
+  e->partials = carve<float4>(cur, static_cast<size_t>(max_rows) * e->vocab_tiles);
+  e->lse_ws = carve<float>(cur, max_rows);
+  e->posterior_ws = carve<int64_t>(cur, max_rows);
+  e->meta.anc = carve<uint32_t>(cur, static_cast<size_t>(max_rows) * layers::kAncWords);
+  e->meta.position = carve<int32_t>(cur, max_rows);
+  e->meta.tree = carve<int32_t>(cur, max_rows);
+  e->meta.local = carve<int32_t>(cur, max_rows);
+  e->meta.request_id = carve<int64_t>(cur, max_rows);
+  if (static_cast<size_t>(cur - static_cast<uint8_t*>(e->workspace)) > e->workspace_bytes) {
+    cudaFree(e->workspace);
+    return fail(SG_ERR_WORKSPACE, "sg_engine_create: workspace layout overflow");
+  }
+  if ((st = make_tmap_2d_bf16(&e->xn_map, e->xn, H, max_rows, H * 2, gemm::BK, gemm::BM)) != SG_OK) return st;
+  if ((st = make_tmap_2d_bf16(&e->attn_map, e->attn, qw, max_rows, qw * 2, gemm::BK, gemm::BM)) != SG_OK) return st;
+  if ((st = make_tmap_2d_bf16(&e->h_map, e->h, I, max_rows, I * 2, gemm::BK, gemm::BM)) != SG_OK) return st;
+  *engine_out = e.release();
+  return SG_OK;
+}
+
+extern "C" int sg_engine_destroy(void* engine) {
+  if (engine == nullptr) return SG_OK;
+  Engine* e = static_cast<Engine*>(engine);
+  if (e->workspace != nullptr) cudaFree(e->workspace);
+  delete e;
+  return SG_OK;
+}
+
+extern "C" size_t sg_engine_workspace_bytes(void* engine) {
+  return engine == nullptr ? 0 : static_cast<Engine*>(engine)->workspace_bytes;
+}
+
+extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stream_ptr) {
+  using namespace sg;
+  if (engine == nullptr || wave == nullptr) return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: null argument");
+  Engine* e = static_cast<Engine*>(engine);
+  const sg_wave_desc& w = *wave;
+  const sg_model_desc& m = e->model;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const int R = w.num_requests, Q = w.num_rows;
+  if (R < 1 || Q < R || Q > e->max_rows || R > e->max_requests || w.max_depth < 0 ||
+      w.max_rows_per_request < 1 || w.max_rows_per_request > layers::kMaxTreeRows)
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: wave sizes out of range");
+  if (w.row_offsets == nullptr || w.parents == nullptr || w.tokens == nullptr || w.slots == nullptr ||
+      w.cache_lengths == nullptr || w.position_base == nullptr || w.accept_out == nullptr)
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: null wave array");
+  if (w.commit && w.lengths_out == nullptr)
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: commit needs lengths_out");
+  if (!(w.temperature > 0.f)) return fail(SG_ERR_UNSUPPORTED, "sg_verify_pass: temperature must be positive");
+  int dev = 0;
+  SG_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev != e->device) return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: engine belongs to another device");
+
+  const int H = m.hidden, D = m.head_dim, I = m.intermediate;
+  const int nq = m.num_q_heads, nkv = m.num_kv_heads;
+  const int qkv_n = (nq + 2 * nkv) * D;
+  const int qw = nq * D;
+  const int64_t plane_rows = e->arena.num_slots * e->arena.capacity;
+  const int64_t plane_stride = plane_rows * D;  // elements between kv heads
+  __nv_bfloat16* arena = static_cast<__nv_bfloat16*>(e->arena.storage);
+  int st;
+
+  trace(w, 0, stream);
+  if ((st = layers::launch_tree_meta(w.row_offsets, w.parents, w.position_base, w.request_ids, R, Q, e->meta, w.status,
+                                     stream)) != SG_OK)
+    return st;
+  if ((st = layers::launch_embed(w.tokens, static_cast<const __nv_bfloat16*>(m.embed), m.vocab, H, Q, e->x, w.status,
+                                 stream)) != SG_OK)
+    return st;
+
+  trace(w, 1, stream);
+  const gemm::Shape s_qkv = gemm::make_shape(Q, qkv_n, H);
+  const gemm::Shape s_o = gemm::make_shape(Q, H, qw);
+  const gemm::Shape s_gu = gemm::make_shape(Q, 2 * I, H);
+  const gemm::Shape s_down = gemm::make_shape(Q, H, I);
+  for (int l = 0; l < m.num_layers; ++l) {
+    const void* const* lw = &e->layer_ptrs[static_cast<size_t>(l) * W_COUNT];
+    const LayerMaps& lm = e->maps[l];
+    __nv_bfloat16* k_plane0 = arena + static_cast<int64_t>(l) * 2 * nkv * plane_stride;
+    __nv_bfloat16* v_plane0 = k_plane0 + static_cast<int64_t>(nkv) * plane_stride;
+
+    if ((st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(lw[W_IN_NORM]), H, Q, m.rms_eps, e->xn,
+                                     stream)) != SG_OK)
+      return st;
+    if (l == 0) trace(w, 2, stream);
+    gemm::EpiStoreBf16::Params pq{e->qkv, qkv_n, w.status};
+    if ((st = gemm::launch<gemm::EpiStoreBf16>(e->xn_map, lm.qkv, s_qkv, pq, stream)) != SG_OK) return st;
+    if (l == 0) trace(w, 3, stream);
+
+    layers::QkvPost qp;
+    qp.qkv = e->qkv;
+    qp.q_norm = static_cast<const __nv_bfloat16*>(lw[W_Q_NORM]);
+    qp.k_norm = static_cast<const __nv_bfloat16*>(lw[W_K_NORM]);
+    qp.inv_freq = m.inv_freq;
+    qp.position = e->meta.position;
+    qp.tree = e->meta.tree;
+    qp.local = e->meta.local;
+    qp.slots = w.slots;
+    qp.cache_len = w.cache_lengths;
+    qp.q_out = e->q;
+    qp.k_plane0 = k_plane0;
+    qp.v_plane0 = v_plane0;
+    qp.plane_stride = plane_stride;
+    qp.capacity = e->arena.capacity;
+    qp.plane_rows = plane_rows;
+    qp.nq = nq;
+    qp.nkv = nkv;
+    qp.head_dim = D;
+    qp.rows = Q;
+    qp.eps = m.rms_eps;
+    qp.status = w.status;
+    if ((st = layers::launch_qkv_post(qp, stream)) != SG_OK) return st;
+    if (l == 0) trace(w, 4, stream);
+
+    attn::Params ap;
+    ap.q = e->q;
+    ap.out = e->attn;
+    ap.k0 = k_plane0;
+    ap.v0 = v_plane0;
+    ap.plane_stride = plane_stride;
+    ap.capacity = e->arena.capacity;
+    ap.plane_rows = plane_rows;
+    ap.num_rows = Q;
+    ap.row_offsets = w.row_offsets;
+    ap.slots = w.slots;
+    ap.cache_len = w.cache_lengths;
+    ap.anc = e->meta.anc;
+    ap.nq = nq;
+    ap.nkv = nkv;
+    ap.group = nq / nkv;
+    ap.plane_k0 = l * 2 * nkv;
+    ap.plane_v0 = l * 2 * nkv + nkv;
+    ap.status = w.status;
+    ap.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
+    if ((st = attn::launch(e->kv_map, ap, R, w.max_rows_per_request, D, stream)) != SG_OK) return st;
+    if (l == 0) trace(w, 5, stream);
+
+    gemm::EpiResidual::Params po{e->x, H, nullptr, 0, w.status};
+    if ((st = gemm::launch<gemm::EpiResidual>(e->attn_map, lm.o, s_o, po, stream)) != SG_OK) return st;
+    if (l == 0) trace(w, 6, stream);
+    if ((st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(lw[W_POST_NORM]), H, Q, m.rms_eps,
+                                     e->xn, stream)) != SG_OK)
+      return st;
+    if (l == 0) trace(w, 7, stream);
+    gemm::EpiSwiGlu::Params pg{e->h, I, w.status};
+    if ((st = gemm::launch<gemm::EpiSwiGlu>(e->xn_map, lm.gate_up, s_gu, pg, stream)) != SG_OK) return st;
+    if (l == 0) trace(w, 8, stream);
+    gemm::EpiResidual::Params pd{e->x, H, nullptr, 0, w.status};
+    if ((st = gemm::launch<gemm::EpiResidual>(e->h_map, lm.down, s_down, pd, stream)) != SG_OK) return st;
+    if (l == 0) trace(w, 9, stream);
+  }
+  trace(w, 10, stream);
+  if (w.hidden_out != nullptr)
+    SG_CUDA_CHECK(cudaMemcpyAsync(w.hidden_out, e->x, static_cast<size_t>(Q) * H * 4, cudaMemcpyDeviceToDevice,
+                                  stream));
+  if ((st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(m.final_norm), H, Q, m.rms_eps, e->xn,
+                                   stream)) != SG_OK)
+    return st;
+  trace(w, 11, stream);
+  gemm::EpiLmHead::Params pl;
+  pl.partials = e->partials;
+  pl.n_tiles = e->vocab_tiles;
+  pl.row_local = e->meta.local;
+  pl.row_request = e->meta.request_id;
+  pl.seed = w.seed;
+  pl.inv_temp = 1.0f / w.temperature;
+  pl.status = w.status;
+  if ((st = gemm::launch<gemm::EpiLmHead>(e->xn_map, e->lm_map, gemm::make_shape(Q, m.vocab, H), pl, stream)) !=
+      SG_OK)
+    return st;
+  trace(w, 12, stream);
+  float* lse = w.lse != nullptr ? w.lse : e->lse_ws;
+  int64_t* posterior = w.posterior != nullptr ? w.posterior : e->posterior_ws;
+  if ((st = layers::launch_lm_combine(e->partials, e->vocab_tiles, Q, lse, posterior, stream)) != SG_OK) return st;
+  if (w.child_logprob != nullptr &&
+      (st = layers::launch_child_logprob(e->xn, static_cast<const __nv_bfloat16*>(m.lm_head), H, m.vocab, w.tokens, w.parents,
+                                         w.row_offsets, e->meta.tree, e->meta.local, lse, 1.0f / w.temperature, Q,
+                                         w.child_logprob, stream)) != SG_OK)
+    return st;
+  trace(w, 13, stream);
+  if ((st = sg_tree_follow(posterior, w.row_offsets, w.parents, w.tokens, R, w.max_rows_per_request, w.max_depth,
+                           w.accept_out, w.status, stream)) != SG_OK)
+    return st;
+  trace(w, 14, stream);
+  if (w.commit) {
+    if ((st = sg_kv_commit_accepted(arena, plane_rows, static_cast<int64_t>(m.num_layers) * 2 * nkv,
+                                    static_cast<int64_t>(D) * 2, e->arena.capacity, w.slots, w.cache_lengths,
+                                    w.lengths_out, w.accept_out, R, w.max_depth, w.status, stream)) != SG_OK)
+      return st;
+  }
+  trace(w, 15, stream);
+  return SG_OK;
+}

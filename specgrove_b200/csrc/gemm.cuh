@@ -337,6 +337,74 @@ struct EpiSwiGlu {
   }
 };
 
+
+// LM head fused with online softmax and Gumbel-max sampling: full-vocabulary
+// logits never reach HBM.  Per (row, 256-column vocab tile) the epilogue
+// writes {tile max, sum exp(l - max), best l + Gumbel noise, its column};
+// a combine kernel turns the tiles into lse[row] and the row's posterior
+// token.  argmax_j (l_j + G_j) with G_j = -log(-log U_j) is an exact draw from
+// softmax(l); U_j comes from Philox4x32-10 keyed by the seed with counter
+// (column / 4, node, request lo, 0x80000000 | request hi), a stream disjoint
+// from the acceptance walk's (whose 4th counter word is 0).
+struct EpiLmHead {
+  struct Params {
+    float4* partials;          // [rows, n_tiles]
+    int n_tiles;
+    const int32_t* row_local;  // [rows] node index within the tree
+    const int64_t* row_request;// [rows] request key
+    uint64_t seed;
+    float inv_temp;
+    int32_t* status;
+  };
+  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int row, int,
+                                               int n0, int, int) {
+    const bool rv = row < s.M;
+    const uint32_t node = rv ? static_cast<uint32_t>(p.row_local[row]) : 0u;
+    const uint64_t req = rv ? static_cast<uint64_t>(p.row_request[row]) : 0ull;
+    const uint32_t k0 = static_cast<uint32_t>(p.seed), k1 = static_cast<uint32_t>(p.seed >> 32);
+    float m = -INFINITY, sum = 0.f, best = -INFINITY;
+    int bidx = n0;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int col0 = n0 + c * 32;
+      if (col0 >= s.N) break;
+      float v[32];
+      sm100::tmem_ld32(taddr + c * 32, v);
+      float cm = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        v[e] *= p.inv_temp;
+        cm = fmaxf(cm, v[e]);
+      }
+      const float mn = fmaxf(m, cm);
+      float add = 0.f;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) add += __expf(v[e] - mn);
+      sum = sum * __expf(m - mn) + add;
+      m = mn;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const U32x4 r = philox4x32_10(
+            U32x4{static_cast<uint32_t>(col0 >> 2) + q, node, static_cast<uint32_t>(req),
+                  0x80000000u | (static_cast<uint32_t>(req >> 32) & 0x7fffffffu)},
+            k0, k1);
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float u = (static_cast<float>(w[e] >> 8) + 0.5f) * (1.0f / 16777216.0f);
+          const float key = v[q * 4 + e] - __logf(-__logf(u));
+          if (key > best) {
+            best = key;
+            bidx = col0 + q * 4 + e;
+          }
+        }
+      }
+    }
+    if (rv) p.partials[static_cast<int64_t>(row) * p.n_tiles + n0 / BN] =
+        make_float4(m, sum, best, __int_as_float(bidx));
+  }
+};
+
 // Host launcher: persistent grid of min(tiles, SMs) CTAs.
 template <class Epi>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Shape& shape, const typename Epi::Params& ep,

@@ -1,0 +1,317 @@
+// Memory-bound per-layer kernels of the packed verify pass.
+//
+// They restate the Qwen3 decoder-layer pieces that the reference runs through
+// HF transformers (Qwen3Model via engine.py:499-517): embedding lookup,
+// RMSNorm, per-head q/k RMSNorm + rotary embedding, and the packed-input
+// construction of continuous_tree_block_decode.py:500-546 (positions =
+// round_prefix_len + depth, ancestor-or-self visibility of Tree.visibility,
+// tree.py:19-26) — here as per-row ancestor bitsets built on device.
+#include <math.h>
+
+#include "layers.cuh"
+
+namespace sg {
+namespace layers {
+namespace {
+
+__device__ __forceinline__ void report(int32_t* status, int code) {
+  if (status != nullptr) atomicMax(status, code);
+}
+
+// One thread per tree: parents precede children, so one ordered pass gives
+// depth and the ancestor-or-self bitset of every node.
+__global__ void tree_meta_kernel(const int64_t* __restrict__ row_offsets, const int64_t* __restrict__ parents,
+                                 const int64_t* __restrict__ position_base, const int64_t* __restrict__ request_ids,
+                                 int num_trees, int num_rows, RowMeta meta, int32_t* status) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= num_trees) return;
+  const int64_t r0 = row_offsets[t];
+  const int64_t r1 = row_offsets[t + 1];
+  const int n = static_cast<int>(r1 - r0);
+  if (r0 < 0 || r1 > num_rows || n < 1 || n > kMaxTreeRows) {
+    report(status, SG_ERR_TREE);
+    return;
+  }
+  const int64_t base = position_base[t];
+  const int64_t rid = request_ids != nullptr ? request_ids[t] : t;
+  int depth[kMaxTreeRows];
+  for (int j = 0; j < n; ++j) {
+    const int64_t q = r0 + j;
+    const int64_t par = parents[q];
+    uint32_t* anc = meta.anc + q * kAncWords;
+    if (j == 0) {
+      if (par != -1) report(status, SG_ERR_TREE);
+      depth[0] = 0;
+#pragma unroll
+      for (int w = 0; w < kAncWords; ++w) anc[w] = 0u;
+    } else {
+      int p = static_cast<int>(par);
+      if (par < 0 || par >= j) {
+        report(status, SG_ERR_TREE);
+        p = 0;
+      }
+      depth[j] = depth[p] + 1;
+      const uint32_t* pa = meta.anc + (r0 + p) * kAncWords;
+#pragma unroll
+      for (int w = 0; w < kAncWords; ++w) anc[w] = pa[w];
+    }
+    anc[j >> 5] |= 1u << (j & 31);
+    meta.position[q] = static_cast<int32_t>(base + depth[j]);
+    meta.tree[q] = t;
+    meta.local[q] = j;
+    meta.request_id[q] = rid;
+  }
+}
+
+__global__ void embed_kernel(const int64_t* __restrict__ tokens, const __nv_bfloat16* __restrict__ embed,
+                             int64_t vocab, int hidden, float* __restrict__ x, int32_t* status) {
+  const int row = blockIdx.x;
+  int64_t tok = tokens[row];
+  if (tok < 0 || tok >= vocab) {
+    if (threadIdx.x == 0) report(status, SG_ERR_TREE);
+    tok = 0;
+  }
+  const __nv_bfloat162* src = reinterpret_cast<const __nv_bfloat162*>(embed + tok * hidden);
+  float2* dst = reinterpret_cast<float2*>(x + static_cast<int64_t>(row) * hidden);
+  for (int i = threadIdx.x; i < hidden / 2; i += blockDim.x) dst[i] = __bfloat1622float2(src[i]);
+}
+
+// y = bf16(x * rsqrt(mean(x^2) + eps) * w); one CTA of 256 threads per row.
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                                                      int hidden, float eps, __nv_bfloat16* __restrict__ out) {
+  const int row = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(row) * hidden);
+  const int n4 = hidden / 4;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+    const float4 v = xr[i];
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  __shared__ float red[8];
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1) t += __shfl_xor_sync(0xffffffffu, t, d);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float rstd = rsqrtf(red[0] / static_cast<float>(hidden) + eps);
+  const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(w);
+  uint2* o = reinterpret_cast<uint2*>(out + static_cast<int64_t>(row) * hidden);
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+    const float4 v = xr[i];
+    const float2 wa = __bfloat1622float2(w2[2 * i]);
+    const float2 wb = __bfloat1622float2(w2[2 * i + 1]);
+    __nv_bfloat162 a = __floats2bfloat162_rn(v.x * rstd * wa.x, v.y * rstd * wa.y);
+    __nv_bfloat162 b = __floats2bfloat162_rn(v.z * rstd * wb.x, v.w * rstd * wb.y);
+    uint2 packed;
+    packed.x = *reinterpret_cast<uint32_t*>(&a);
+    packed.y = *reinterpret_cast<uint32_t*>(&b);
+    o[i] = packed;
+  }
+}
+
+// One warp per (row, head).  Heads [0, nq) are queries, [nq, nq+nkv) keys,
+// [nq+nkv, nq+2nkv) values.  Lane l holds dims l + 32 i; the rotary pairs
+// (d, d + D/2) therefore sit in the same lane.
+template <int D>
+__global__ void __launch_bounds__(256) qkv_post_kernel(const QkvPost p) {
+  constexpr int PER = D / 32;
+  constexpr int HALF = D / 2;
+  const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int heads = p.nq + 2 * p.nkv;
+  if (warp_global >= p.rows * heads) return;
+  const int row = warp_global / heads;
+  const int head = warp_global % heads;
+  const __nv_bfloat16* src = p.qkv + static_cast<int64_t>(row) * heads * D + static_cast<int64_t>(head) * D;
+  float v[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) v[i] = __bfloat162float(src[lane + 32 * i]);
+  const bool is_q = head < p.nq;
+  const bool is_k = !is_q && head < p.nq + p.nkv;
+  if (is_q || is_k) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) ss += v[i] * v[i];
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+    const float rstd = rsqrtf(ss / static_cast<float>(D) + p.eps);
+    const __nv_bfloat16* w = is_q ? p.q_norm : p.k_norm;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) v[i] = v[i] * rstd * __bfloat162float(w[lane + 32 * i]);
+    // rotate_half rotary embedding: out_d = x_d cos - x_{d+H} sin (d < H),
+    //                                out_{d+H} = x_{d+H} cos + x_d sin.
+    const float pos = static_cast<float>(p.position[row]);
+#pragma unroll
+    for (int i = 0; i < PER / 2; ++i) {
+      const int d = lane + 32 * i;  // < HALF
+      const float angle = pos * p.inv_freq[d];
+      float s, c;
+      sincosf(angle, &s, &c);
+      const float x1 = v[i], x2 = v[i + PER / 2];
+      v[i] = x1 * c - x2 * s;
+      v[i + PER / 2] = x2 * c + x1 * s;
+    }
+    (void)HALF;
+  }
+  __nv_bfloat16* dst;
+  if (is_q) {
+    dst = p.q_out + static_cast<int64_t>(row) * p.nq * D + static_cast<int64_t>(head) * D;
+  } else {
+    const int kvh = is_k ? head - p.nq : head - p.nq - p.nkv;
+    const int t = p.tree[row];
+    if (t < 0) {  // row of a rejected tree (reported by tree_meta)
+      return;
+    }
+    const int64_t arena_row = p.slots[t] * p.capacity + p.cache_len[t] + p.local[row];
+    if (arena_row < 0 || arena_row >= p.plane_rows || p.cache_len[t] + p.local[row] >= p.capacity) {
+      if (lane == 0) report(p.status, SG_ERR_CAPACITY);
+      return;
+    }
+    __nv_bfloat16* plane = (is_k ? p.k_plane0 : p.v_plane0) + static_cast<int64_t>(kvh) * p.plane_stride;
+    dst = plane + arena_row * D;
+  }
+#pragma unroll
+  for (int i = 0; i < PER; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(v[i]);
+}
+
+// lse and Gumbel-max token of every row from the per-vocab-tile partials
+// (max, sum exp(l - max), best perturbed logit, its column).
+__global__ void lm_combine_kernel(const float4* __restrict__ partials, int n_tiles, int rows,
+                                  float* __restrict__ lse, int64_t* __restrict__ posterior) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float4* pr = partials + static_cast<int64_t>(row) * n_tiles;
+  float m = -INFINITY;
+  for (int t = lane; t < n_tiles; t += 32) m = fmaxf(m, pr[t].x);
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
+  float s = 0.f, best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int t = lane; t < n_tiles; t += 32) {
+    const float4 v = pr[t];
+    s += v.y * __expf(v.x - m);
+    const int col = __float_as_int(v.w);
+    if (v.z > best || (v.z == best && col < idx)) {
+      best = v.z;
+      idx = col;
+    }
+  }
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, d);
+    const float ob = __shfl_xor_sync(0xffffffffu, best, d);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, d);
+    if (ob > best || (ob == best && oi < idx)) {
+      best = ob;
+      idx = oi;
+    }
+  }
+  if (lane == 0) {
+    if (lse != nullptr) lse[row] = m + logf(s);
+    if (posterior != nullptr) posterior[row] = idx;
+  }
+}
+
+// log p_parent(token) for every non-root row: logit recomputed as a dot
+// product of the parent's final hidden row with the token's LM-head row.
+__global__ void child_logprob_kernel(const __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ w,
+                                     int hidden, int64_t vocab, const int64_t* __restrict__ tokens,
+                                     const int64_t* __restrict__ parents, const int64_t* __restrict__ row_offsets,
+                                     const int32_t* __restrict__ tree, const int32_t* __restrict__ local,
+                                     const float* __restrict__ lse, float inv_temp, int rows,
+                                     float* __restrict__ logprob) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  if (tree[row] < 0 || local[row] == 0) {
+    if (lane == 0) logprob[row] = tree[row] < 0 ? NAN : 0.f;
+    return;
+  }
+  const int64_t par = parents[row];
+  const int64_t tok = tokens[row];
+  if (par < 0 || par >= local[row] || tok < 0 || tok >= vocab) {  // invalid tree: reported by tree_meta
+    if (lane == 0) logprob[row] = NAN;
+    return;
+  }
+  const int64_t prow = row_offsets[tree[row]] + par;
+  const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(h + prow * hidden);
+  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(w + tok * hidden);
+  float acc = 0.f;
+  for (int i = lane; i < hidden / 2; i += 32) {
+    const float2 x = __bfloat1622float2(a[i]);
+    const float2 y = __bfloat1622float2(b[i]);
+    acc += x.x * y.x + x.y * y.y;
+  }
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
+  if (lane == 0) logprob[row] = acc * inv_temp - lse[prow];
+}
+
+}  // namespace
+
+int launch_tree_meta(const int64_t* row_offsets, const int64_t* parents, const int64_t* position_base,
+                     const int64_t* request_ids, int num_trees, int num_rows, RowMeta meta, int32_t* status,
+                     cudaStream_t stream) {
+  if (num_trees <= 0) return SG_OK;
+  // rows not claimed by a valid tree keep tree = -1 and are skipped downstream
+  SG_CUDA_CHECK(cudaMemsetAsync(meta.tree, 0xff, static_cast<size_t>(num_rows) * sizeof(int32_t), stream));
+  tree_meta_kernel<<<(num_trees + 63) / 64, 64, 0, stream>>>(row_offsets, parents, position_base, request_ids,
+                                                               num_trees, num_rows, meta, status);
+  return check_launch("tree_meta_kernel");
+}
+
+int launch_embed(const int64_t* tokens, const __nv_bfloat16* embed, int64_t vocab, int hidden, int rows, float* x,
+                 int32_t* status, cudaStream_t stream) {
+  if (rows <= 0) return SG_OK;
+  embed_kernel<<<rows, 256, 0, stream>>>(tokens, embed, vocab, hidden, x, status);
+  return check_launch("embed_kernel");
+}
+
+int launch_rmsnorm(const float* x, const __nv_bfloat16* weight, int hidden, int rows, float eps,
+                   __nv_bfloat16* out, cudaStream_t stream) {
+  if (rows <= 0) return SG_OK;
+  if (hidden % 4 != 0) return fail(SG_ERR_UNSUPPORTED, "rmsnorm: hidden % 4 != 0");
+  rmsnorm_kernel<<<rows, 256, 0, stream>>>(x, weight, hidden, eps, out);
+  return check_launch("rmsnorm_kernel");
+}
+
+int launch_qkv_post(const QkvPost& p, cudaStream_t stream) {
+  if (p.rows <= 0) return SG_OK;
+  const int64_t warps = static_cast<int64_t>(p.rows) * (p.nq + 2 * p.nkv);
+  const unsigned grid = static_cast<unsigned>((warps + 7) / 8);
+  if (p.head_dim == 128)
+    qkv_post_kernel<128><<<grid, 256, 0, stream>>>(p);
+  else if (p.head_dim == 64)
+    qkv_post_kernel<64><<<grid, 256, 0, stream>>>(p);
+  else
+    return fail(SG_ERR_UNSUPPORTED, "qkv_post: head_dim must be 64 or 128");
+  return check_launch("qkv_post_kernel");
+}
+
+int launch_lm_combine(const float4* partials, int n_tiles, int rows, float* lse, int64_t* posterior,
+                      cudaStream_t stream) {
+  if (rows <= 0) return SG_OK;
+  lm_combine_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(partials, n_tiles, rows, lse, posterior);
+  return check_launch("lm_combine_kernel");
+}
+
+int launch_child_logprob(const __nv_bfloat16* h, const __nv_bfloat16* lm_head, int hidden, int64_t vocab,
+                         const int64_t* tokens,
+                         const int64_t* parents, const int64_t* row_offsets, const int32_t* tree,
+                         const int32_t* local, const float* lse, float inv_temp, int rows, float* logprob,
+                         cudaStream_t stream) {
+  if (rows <= 0) return SG_OK;
+  child_logprob_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(h, lm_head, hidden, vocab, tokens, parents, row_offsets, tree,
+                                                           local, lse, inv_temp, rows, logprob);
+  return check_launch("child_logprob_kernel");
+}
+
+}  // namespace layers
+}  // namespace sg

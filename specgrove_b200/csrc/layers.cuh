@@ -1,0 +1,65 @@
+// Memory-bound per-layer kernels of the packed verify pass (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+
+namespace sg {
+namespace layers {
+
+constexpr int kMaxTreeRows = 256;               // rows per request tree (root included)
+constexpr int kAncWords = kMaxTreeRows / 32;    // ancestor bitset words per row
+
+// Per-row metadata derived on device from the wave's tree description.
+struct RowMeta {
+  uint32_t* anc;        // [Q][kAncWords] ancestor-or-self bitset over local rows
+  int32_t* position;    // [Q] rotary position = position_base[req] + depth
+  int32_t* tree;        // [Q] request (tree) index of the row
+  int32_t* local;       // [Q] local node index
+  int64_t* request_id;  // [Q] Philox key of the row's request
+};
+
+int launch_tree_meta(const int64_t* row_offsets, const int64_t* parents, const int64_t* position_base,
+                     const int64_t* request_ids, int num_trees, int num_rows, RowMeta meta, int32_t* status,
+                     cudaStream_t stream);
+
+int launch_embed(const int64_t* tokens, const __nv_bfloat16* embed, int64_t vocab, int hidden, int rows,
+                 float* x, int32_t* status, cudaStream_t stream);
+
+int launch_rmsnorm(const float* x, const __nv_bfloat16* weight, int hidden, int rows, float eps,
+                   __nv_bfloat16* out, cudaStream_t stream);
+
+struct QkvPost {
+  const __nv_bfloat16* qkv;     // [Q, (nq + 2 nkv) * D]
+  const __nv_bfloat16* q_norm;  // [D]
+  const __nv_bfloat16* k_norm;  // [D]
+  const float* inv_freq;        // [D/2]
+  const int32_t* position;      // [Q]
+  const int32_t* tree;          // [Q]
+  const int32_t* local;         // [Q]
+  const int64_t* slots;         // [R]
+  const int64_t* cache_len;     // [R]
+  __nv_bfloat16* q_out;         // [Q, nq * D]
+  __nv_bfloat16* k_plane0;      // K plane of kv head 0 of this layer
+  __nv_bfloat16* v_plane0;      // V plane of kv head 0 of this layer
+  int64_t plane_stride;         // elements between consecutive kv heads' planes
+  int64_t capacity;             // rows per slot
+  int64_t plane_rows;           // rows per plane (slots * capacity)
+  int nq, nkv, head_dim, rows;
+  float eps;
+  int32_t* status;
+};
+int launch_qkv_post(const QkvPost& p, cudaStream_t stream);
+
+int launch_lm_combine(const float4* partials, int n_tiles, int rows, float* lse, int64_t* posterior,
+                      cudaStream_t stream);
+
+int launch_child_logprob(const __nv_bfloat16* h, const __nv_bfloat16* lm_head, int hidden, int64_t vocab,
+                         const int64_t* tokens,
+                         const int64_t* parents, const int64_t* row_offsets, const int32_t* tree,
+                         const int32_t* local, const float* lse, float inv_temp, int rows, float* logprob,
+                         cudaStream_t stream);
+
+}  // namespace layers
+}  // namespace sg

@@ -104,3 +104,66 @@ def acceptance_sweep(seed: int = 0, trees: int = 64, total_nodes: int = 4096, vo
         tokens_all.append(tokens)
         depths_all.append(depths)
     return TreeBatch(parents_all, tokens_all, depths_all, offsets), probs
+
+
+# ---------------------------------------------------------------------------
+# Verify-pass waves (configurations 3 and 4)
+# ---------------------------------------------------------------------------
+def best_first_tree(logs, ids, budget: int, rank_caps=None):
+    """Best-first DDTree over per-depth top-k draft tokens (the product-
+    probability heap of tree.py:148-212 with depth_reward = 0): returns
+    (parents incl. root -1, tokens per node (root -1), depths)."""
+    import heapq
+    length = len(logs)
+    caps = rank_caps or [len(logs[0])] * length
+    parents, tokens, depths = [-1], [-1], [0]
+    heap = [(-logs[0][0], 0, 0, 0, 0.0)]
+    while heap and len(tokens) - 1 < budget:
+        neg, parent, depth, rank, parent_log = heapq.heappop(heap)
+        node = len(parents)
+        tokens.append(int(ids[depth][rank]))
+        parents.append(parent)
+        depths.append(depth + 1)
+        if rank + 1 < caps[depth]:
+            heapq.heappush(heap, (-(parent_log + logs[depth][rank + 1]), parent, depth, rank + 1, parent_log))
+        if depth + 1 < length:
+            heapq.heappush(heap, (neg - logs[depth + 1][0], node, depth + 1, 0, -neg))
+    return parents, tokens, depths
+
+
+# (rows incl. root) -> count; each mix sums to the configuration's row budget
+TIER_MIX_CONFIG4 = {16: 40, 32: 12, 64: 8, 128: 4}   # 64 requests, 2048 rows
+TIER_MIX_CONFIG3 = {16: 8, 32: 4, 64: 4}             # 16 requests, 512 rows
+
+
+@dataclass
+class VerifyWorkload:
+    trees: list            # per request (parents, tokens with the root token first)
+    cache_lengths: list
+    tiers: list
+
+
+def verify_workload(vocab: int, tier_mix: dict, prefix_range: tuple, seed: int = 0, block: int = 16,
+                    draft_scale: float = 4.0, top_k: int = 4, device="cuda") -> VerifyWorkload:
+    """One wave: per request a canonical best-first tree (block 16 draft
+    positions, top-4 children per depth from softmax(4 N(0,1)) draft logits)
+    cut to its tier (ancestor-closed best-first prefix, decode.py:571-586),
+    prefix lengths uniform in prefix_range, tokens uniform over the vocab."""
+    rng = np.random.default_rng(seed)
+    tiers = [t for t, c in sorted(tier_mix.items()) for _ in range(c)]
+    rng.shuffle(tiers)
+    R = len(tiers)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    trees, lengths = [], []
+    budget = max(tiers) - 1
+    for i in range(R):
+        draft = torch.randn((block, vocab), generator=gen, device=device) * draft_scale
+        logq = torch.log_softmax(draft, -1)
+        vals, idx = torch.topk(logq, top_k, dim=-1)
+        parents, tokens, _ = best_first_tree(vals.tolist(), idx.tolist(), budget, [top_k] * block)
+        n = tiers[i]
+        parents, tokens = parents[:n], tokens[:n]
+        tokens[0] = int(rng.integers(0, vocab))        # root row: last committed token
+        trees.append((parents, tokens))
+        lengths.append(int(rng.integers(prefix_range[0], prefix_range[1] + 1)))
+    return VerifyWorkload(trees, lengths, tiers)

@@ -169,3 +169,32 @@ def test_philox_known_answer():
     u = philox_node_uniforms(0, 0, 0)
     v = ((0xe169c58d << 32) | 0x6627e8d5) >> 11
     assert u[0] == v / 2.0**53
+
+
+def test_packed_inputs_restatement_matches_reference(golden_dir):
+    from oracle.packed_inputs import packed_block_inputs
+    z = np.load(golden_dir / "packed_inputs.npz")
+    counts = z["row_counts"].tolist()
+    offsets = np.cumsum([0] + counts)
+    trees = []
+    for i, n in enumerate(counts):
+        par = z["parents"][offsets[i]:offsets[i + 1]].tolist()
+        tok = z["tokens"][offsets[i]:offsets[i + 1]].tolist()
+        tok[0] = int(z["roots"][i])
+        trees.append((par, tok))
+    ids, pos, mask, q_off = packed_block_inputs(trees, z["lengths"].tolist(), z["round_prefix"].tolist())
+    np.testing.assert_array_equal(ids.numpy(), z["ids"])
+    np.testing.assert_array_equal(pos.numpy(), z["positions"])
+    np.testing.assert_array_equal(np.isfinite(mask[0, 0].numpy()), z["visible"])
+    assert list(q_off) == z["q_offsets"].tolist()
+
+
+def test_wave_builder_validates_like_reference():
+    from specgrove_b200.engine import Wave
+    w = Wave([([-1, 0, 0, 1], [5, 6, 7, 8]), ([-1], [9])], [0, 3], [10, 20], [12, 21], [7, 8])
+    assert w.num_rows == 5 and w.max_depth == 2 and w.max_rows_per_request == 4
+    assert w.row_offsets == [0, 4, 5]
+    with pytest.raises(ValueError, match="precede"):
+        Wave([([-1, 1], [1, 2])], [0], [0])
+    with pytest.raises(ValueError, match="repeat"):
+        Wave([([-1, 0, 0], [1, 2, 2])], [0], [0])

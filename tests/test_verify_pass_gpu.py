@@ -1,0 +1,217 @@
+"""The packed verify pass against the reference's BF16-SDPA target path.
+
+The reference scores a wave with HF ``Qwen3Model`` over a packed
+DynamicCache and the dense tree mask of ``_packed_block_inputs``
+(continuous_tree_block_decode.py:500-546, engine.py:499-517), then
+``log_softmax(logits.float())``.  Here the same random-init model (packed
+into engine weights) runs through ``sg_verify_pass``; per-node fp32
+log-probabilities log p_parent(token) and per-row log-normalisers must match
+within the north-star tolerance of 2e-2 max abs.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.packed_inputs import packed_block_inputs
+from specgrove_b200.engine import B200Engine, Weights, Wave
+from specgrove_b200.workloads import random_topology
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2  # max abs error on per-node fp32 log-probs
+
+
+def hf_model(layers=2, hidden=512, nq=8, nkv=2, head_dim=128, inter=1024, vocab=4096, seed=0, logit_scale=3.0):
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    torch.manual_seed(seed)
+    cfg = Qwen3Config(vocab_size=vocab, hidden_size=hidden, intermediate_size=inter, num_hidden_layers=layers,
+                      num_attention_heads=nq, num_key_value_heads=nkv, head_dim=head_dim, rope_theta=1.0e6,
+                      max_position_embeddings=8192, tie_word_embeddings=False, rms_norm_eps=1e-6,
+                      attn_implementation="sdpa")
+    model = Qwen3ForCausalLM(cfg)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if "norm" in name:
+                p.uniform_(0.8, 1.2)
+            elif "embed" in name:
+                p.normal_(0.0, 1.0)
+            else:
+                p.normal_(0.0, 1.0 / math.sqrt(p.shape[1]))
+        model.lm_head.weight.mul_(logit_scale)
+    # Load it the way the reference loads its target (engine.py:270-282):
+    # from_pretrained(torch_dtype=bf16), which keeps the rotary inv_freq in
+    # fp32 (a plain .to(bf16) would round it and shift every rotary angle).
+    import tempfile
+    with tempfile.TemporaryDirectory() as d:
+        model.save_pretrained(d)
+        model = Qwen3ForCausalLM.from_pretrained(d, dtype=torch.bfloat16, attn_implementation="sdpa")
+    return model.to("cuda").eval()
+
+
+def make_trees(rng, count, vocab, lo, hi):
+    trees = []
+    for _ in range(count):
+        n = int(rng.integers(lo, hi + 1))
+        parents, _ = random_topology(rng, n, 16, 4)
+        tokens = [int(rng.integers(0, vocab))]
+        kids = {}
+        for j in range(1, n):
+            used = kids.setdefault(parents[j], set())
+            while True:
+                t = int(rng.integers(0, vocab))
+                if t not in used:
+                    break
+            used.add(t)
+            tokens.append(t)
+        trees.append((parents, tokens))
+    return trees
+
+
+def hf_wave_logprobs(model, prompts, trees):
+    """The reference's target pass: per-request prefill caches, packed
+    DynamicCache, dense tree mask, HF Qwen3Model, lm_head, fp32 log_softmax."""
+    from transformers import DynamicCache
+    caches = []
+    with torch.no_grad():
+        for p in prompts:
+            c = DynamicCache()
+            model(input_ids=torch.tensor([p], device="cuda"), past_key_values=c, use_cache=True)
+            caches.append(c)
+        packed = DynamicCache()
+        for l in range(model.config.num_hidden_layers):
+            k = torch.cat([c.layers[l].keys for c in caches], dim=-2)
+            v = torch.cat([c.layers[l].values for c in caches], dim=-2)
+            packed.update(k, v, l)
+        lengths = [len(p) for p in prompts]
+        ids, pos, mask, q_off = packed_block_inputs(trees, lengths, lengths, dtype=torch.bfloat16, device="cuda")
+        out = model.model(input_ids=ids, past_key_values=packed, position_ids=pos, attention_mask=mask,
+                          use_cache=True)
+        logits = model.lm_head(out.last_hidden_state)[0].float()
+    return torch.log_softmax(logits, dim=-1), caches
+
+
+def fp32_truth_logprobs(weights, prompts, trees):
+    """Exact-arithmetic target (the oracle's torch fp32 restatement of the
+    pass, on the GPU): prefixes prefilled in fp32, then the packed wave."""
+    from oracle.forward import CpuWeights, verify_logits
+    cw = CpuWeights(weights, lazy=False, device="cuda")
+    s = weights.shape
+    empty = torch.zeros(s.num_kv_heads, 0, s.head_dim, device="cuda")
+    prefixes = []
+    for p in prompts:
+        _, _, kv = verify_logits(cw, [[(empty, empty)] * s.num_layers], [([-1] + list(range(len(p) - 1)), p)], [0],
+                                 return_kv=True)
+        prefixes.append([(k.transpose(0, 1), v.transpose(0, 1)) for k, v in kv])
+    logits, _ = verify_logits(cw, prefixes, trees, [len(p) for p in prompts])
+    return torch.log_softmax(logits, -1), torch.logsumexp(logits, -1)
+
+
+def node_index(trees):
+    parent_rows, tokens, rows, off = [], [], [], 0
+    for par, tok in trees:
+        for j in range(1, len(par)):
+            parent_rows.append(off + par[j])
+            tokens.append(tok[j])
+            rows.append(off + j)
+        off += len(par)
+    t = lambda a: torch.tensor(a, device="cuda")
+    return t(parent_rows), t(tokens), t(rows)
+
+
+@pytest.mark.parametrize("scale", [1.0, 3.0])
+@pytest.mark.parametrize("geometry", [dict(), dict(nq=4, nkv=2, head_dim=64, hidden=256, inter=768)])
+def test_logprobs_match_hf_bf16_sdpa(cuda_lib, geometry, scale):
+    """Per-node log p_parent(token) of the B200 pass vs (a) the reference's
+    BF16-SDPA path and (b) the fp32 truth.  The reference path itself rounds
+    activations, q/k/rotary terms and the logits to bf16, which costs it up to
+    ~0.02 (logit std 1) or ~0.06 (std 3) against the truth; the B200 pass must
+    be at least as accurate as the reference and, where the reference's bf16
+    logit rounding is below the bound (std 1), within 1.5e-2 of the truth and
+    within 1e-2 (mean) / 3e-2 (max) of the reference path."""
+    model = hf_model(**geometry, logit_scale=scale)
+    vocab = model.config.vocab_size
+    rng = np.random.default_rng(1)
+    prompts = [rng.integers(0, vocab, size=int(rng.integers(32, 300))).tolist() for _ in range(5)]
+    trees = make_trees(rng, 5, vocab, 1, 40)
+    hf_lp, caches = hf_wave_logprobs(model, prompts, trees)
+    weights = Weights.from_hf(model)
+    truth_lp, truth_lse = fp32_truth_logprobs(weights, prompts, trees)
+
+    engine = B200Engine(weights, num_slots=5, capacity=512, max_rows=512)
+    slots = [3, 0, 4, 1, 2]  # arena slots need not follow request order
+    engine.prefill(prompts, slots)
+    for i, s in enumerate(slots):   # prefill KV vs the reference's cache (post-RoPE keys)
+        L = len(prompts[i])
+        for l in range(model.config.num_hidden_layers):
+            ours_k = engine.arena.key_storage[l][:, s * 512: s * 512 + L].float()
+            assert (ours_k - caches[i].layers[l].keys[0].float()).abs().max().item() < 0.1
+    Q = sum(len(t[0]) for t in trees)
+    lse, child = torch.empty(Q, device="cuda"), torch.empty(Q, device="cuda")
+    engine.verify(Wave(trees, slots, [len(p) for p in prompts]), seed=5, lse=lse, child_logprob=child, commit=False)
+    torch.cuda.synchronize()
+    pr, tk, rows = node_index(trees)
+    ours, hf, truth = child[rows], hf_lp[pr, tk], truth_lp[pr, tk]
+    err_ours, err_ref = (ours - truth).abs().max().item(), (hf - truth).abs().max().item()
+    assert err_ours <= err_ref, (err_ours, err_ref)
+    assert (lse - truth_lse).abs().max().item() < TOL
+    if scale == 1.0:
+        assert err_ours < 0.75 * TOL, err_ours
+        diff = (ours - hf).abs()
+        assert diff.mean().item() < TOL / 2, diff.mean().item()
+        assert diff.max().item() < 1.5 * TOL, diff.max().item()
+
+
+def test_commit_keeps_accepted_rows_and_lengths(cuda_lib):
+    model = hf_model(layers=1, hidden=256, nq=4, nkv=2, head_dim=64, inter=512, vocab=1024, logit_scale=20.0)
+    rng = np.random.default_rng(2)
+    prompts = [rng.integers(0, 1024, size=40).tolist() for _ in range(3)]
+    engine = B200Engine(Weights.from_hf(model), num_slots=3, capacity=256, max_rows=256)
+    engine.prefill(prompts, [0, 1, 2])
+    # greedy-like chain trees built from the model's own argmax continue deep
+    trees = make_trees(rng, 3, 1024, 10, 30)
+    wave = Wave(trees, [0, 1, 2], [40, 40, 40])
+    before = engine.arena.storage.clone()
+    dw = wave.to("cuda")
+    out = engine.verify_device(dw, seed=3, commit=False)
+    tail = engine.arena.storage.clone()  # tree rows written at L..L+n
+    lengths_out = torch.empty(3, dtype=torch.long, device="cuda")
+    out2 = engine.verify_device(dw, seed=3, commit=True, lengths_out=lengths_out)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2)  # same seed, same decisions
+    D = wave.max_depth
+    for i in range(3):
+        count = int(out[i, D])
+        keep = [0] + out[i, :count].tolist()
+        assert int(lengths_out[i]) == 40 + len(keep)
+        base = i * 256 + 40
+        for k, node in enumerate(keep):
+            assert torch.equal(engine.arena.storage[:, :, :, base + k], tail[:, :, :, base + node])
+        assert torch.equal(engine.arena.storage[:, :, :, i * 256:base], before[:, :, :, i * 256:base])
+
+
+def test_gumbel_sampling_law(cuda_lib):
+    """The fused LM-head sampler draws each row's posterior token from
+    softmax(logits / T): empirical frequencies over seeds vs HF's fp32 probs."""
+    model = hf_model(layers=1, hidden=256, nq=4, nkv=2, head_dim=64, inter=512, vocab=512, logit_scale=1.0)
+    rng = np.random.default_rng(3)
+    prompts = [rng.integers(0, 512, size=20).tolist()]
+    trees = [([-1, 0, 0], [7, 8, 9])]
+    ref_lp, _ = hf_wave_logprobs(model, prompts, trees)
+    T = 0.35
+    engine = B200Engine(Weights.from_hf(model), num_slots=1, capacity=64, max_rows=64)
+    engine.prefill(prompts, [0])
+    dw = Wave(trees, [0], [20]).to("cuda")
+    N = 3000
+    post = torch.empty((N, 3), dtype=torch.long, device="cuda")
+    for s in range(N):
+        engine.verify_device(dw, seed=1000 + s, temperature=T, commit=False, posterior=post[s])
+    torch.cuda.synchronize()
+    for row in range(3):
+        p = torch.softmax(ref_lp[row] / T, -1)  # logits/T up to a row constant
+        emp = torch.bincount(post[:, row], minlength=512).float() / N
+        tv = 0.5 * (emp - p).abs().sum().item()
+        # TV of an N-sample empirical law around the truth: ~ sqrt(k / N) for k effective categories
+        k_eff = 1.0 / (p ** 2).sum().item()
+        assert tv < 0.1 + 0.8 * math.sqrt(min(k_eff, 512) / N), (row, tv, k_eff)
