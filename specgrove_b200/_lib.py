@@ -87,8 +87,13 @@ def check(status: int, where: str) -> None:
         raise SpecgroveError(status, where)
 
 
+# Entry points taking struct descriptors; bound with their ctypes structures
+# in specgrove_b200.engine.
+STRUCT_SYMBOLS = ["sg_engine_create", "sg_engine_destroy", "sg_engine_workspace_bytes", "sg_verify_pass"]
+
+
 def exported_symbols() -> list[str]:
-    return list(_SIGNATURES)
+    return list(_SIGNATURES) + STRUCT_SYMBOLS
 
 
 def ptr(tensor) -> int | None:
