@@ -264,6 +264,38 @@ SG_API size_t sg_engine_workspace_bytes(void* engine);
  */
 SG_API int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stream);
 
+/*
+ * Fused LM-head sampling that allocates no device memory.  No counterpart in
+ * the reference: it exists for callers that cannot call cudaMalloc, such as
+ * a serving process that has handed its device memory to its own pool
+ * allocator, or a foreign-language caller whose FFI only passes in buffers
+ * it allocated itself.
+ *
+ * Same computation and output as the sampling stage of sg_verify_pass:
+ * final RMSNorm of the residual rows x (fp32 [rows, hidden], e.g. the
+ * pass's hidden_out) with final_norm (bf16 [hidden]), LM head (bf16
+ * [vocab, hidden]) fused with online softmax and Gumbel-max sampling keyed
+ * by (seed, row_request[r], row_node[r]), then lse[r] and posterior[r].
+ *
+ * Its scratch (normalised rows and per-vocab-tile partials,
+ * rows * (2 * hidden + 16 * ceil(vocab / 256)) bytes plus alignment) lives in
+ * one library-owned device array of SG_LM_HEAD_STATIC_SCRATCH_BYTES, present
+ * on every GPU that loads the library until the process exits; larger
+ * requests fail with SG_ERR_WORKSPACE.  The first call on each device looks
+ * up the array's device address (cudaGetSymbolAddress) and caches it; make
+ * that first call before any stream capture.  All calls share the array:
+ * calls whose executions overlap on the GPU (other streams, other host
+ * threads) race and must be serialised by the caller.  Nothing needs
+ * clearing between calls: every scratch value read is written earlier in the
+ * same call.
+ */
+#define SG_LM_HEAD_STATIC_SCRATCH_BYTES (8u << 20)
+SG_API int sg_lm_head_sample_static(const float* x, const void* final_norm, const void* lm_head,
+                             int32_t rows, int32_t hidden, int32_t vocab, float rms_eps,
+                             const int32_t* row_node, const int64_t* row_request,
+                             uint64_t seed, float temperature, float* lse,
+                             int64_t* posterior, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -44,6 +44,9 @@ _SIGNATURES = {
     "sg_gemm_bf16": (ctypes.c_int, [
         c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_int32, c_int32,
         c_void_p, c_int64, c_void_p, c_void_p]),
+    "sg_lm_head_sample_static": (ctypes.c_int, [
+        c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, ctypes.c_float, c_void_p, c_void_p, c_uint64,
+        ctypes.c_float, c_void_p, c_void_p, c_void_p]),
 }
 
 SG_EPI_STORE_BF16 = 0
