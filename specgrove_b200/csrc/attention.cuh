@@ -23,12 +23,16 @@ struct Params {
   const uint32_t* anc;       // [Q][kAncWords]
   int nq, nkv, group;
   int plane_k0, plane_v0;    // arena plane of kv head 0's K and V for this layer
+  const int32_t* order;      // [R] requests in launch order (longest first), or null
   float scale_log2;          // softmax scale * log2(e)
   int32_t* status;
 };
 
+// Keys per K/V tile of the tree attention (and rows of the kv_map box).
+constexpr int kKeyTile = 64;
+
 // kv_map: 3-D TMA map over the whole arena (head_dim, plane rows, planes),
-// box (64, 128, 1), 128-byte swizzle.
+// box (64, kKeyTile, 1), 128-byte swizzle.
 int launch(const CUtensorMap& kv_map, const Params& p, int num_requests, int max_rows_per_request, int head_dim,
            cudaStream_t stream);
 

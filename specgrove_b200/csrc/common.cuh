@@ -9,7 +9,7 @@
 #include <cstdio>
 #include <string>
 
-#include "../../include/specgrove_b200.h"
+#include "specgrove_b200.h"
 
 namespace sg {
 

@@ -83,6 +83,7 @@ size_t workspace_size(const sg_model_desc& m, int rows) {
   s += rows * layers::kAncWords * 4 + 256;    // anc
   s += rows * 4 * 3 + 3 * 256;                // position, tree, local
   s += rows * 8 + 256;                        // request id
+  s += rows * 4 + 256;                        // attention order (R <= rows)
   return s + 4096;
 }
 
@@ -147,7 +148,7 @@ extern "C" int sg_engine_create(const sg_model_desc* model, const sg_arena_desc*
     const uint64_t plane_rows = static_cast<uint64_t>(arena->num_slots) * arena->capacity;
     const uint64_t planes = static_cast<uint64_t>(m.num_layers) * 2 * m.num_kv_heads;
     if ((st = make_tmap_3d_bf16(&e->kv_map, arena->storage, D, plane_rows, planes, D * 2, plane_rows * D * 2, 64,
-                                128)) != SG_OK)
+                                attn::kKeyTile)) != SG_OK)
       return st;
   }
 
@@ -169,6 +170,7 @@ extern "C" int sg_engine_create(const sg_model_desc* model, const sg_arena_desc*
   e->meta.tree = carve<int32_t>(cur, max_rows);
   e->meta.local = carve<int32_t>(cur, max_rows);
   e->meta.request_id = carve<int64_t>(cur, max_rows);
+  e->meta.order = carve<int32_t>(cur, max_rows);
   if (static_cast<size_t>(cur - static_cast<uint8_t*>(e->workspace)) > e->workspace_bytes) {
     cudaFree(e->workspace);
     return fail(SG_ERR_WORKSPACE, "sg_engine_create: workspace layout overflow");
@@ -230,6 +232,8 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
                                  stream)) != SG_OK)
     return st;
 
+  if ((st = layers::launch_attention_order(w.row_offsets, w.cache_lengths, R, e->meta.order, stream)) != SG_OK)
+    return st;
   trace(w, 1, stream);
   const gemm::Shape s_qkv = gemm::make_shape(Q, qkv_n, H);
   const gemm::Shape s_o = gemm::make_shape(Q, H, qw);
@@ -292,6 +296,7 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
     ap.group = nq / nkv;
     ap.plane_k0 = l * 2 * nkv;
     ap.plane_v0 = l * 2 * nkv + nkv;
+    ap.order = e->meta.order;
     ap.status = w.status;
     ap.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
     if ((st = attn::launch(e->kv_map, ap, R, w.max_rows_per_request, D, stream)) != SG_OK) return st;

@@ -63,6 +63,22 @@ __global__ void tree_meta_kernel(const int64_t* __restrict__ row_offsets, const 
   }
 }
 
+// Launch order of the tree attention: requests by decreasing K/V length
+// (cache prefix + tree rows), ties by index, so the longest CTAs start first
+// and the grid's tail is short.  One CTA; R is small.
+__global__ void order_kernel(const int64_t* __restrict__ row_offsets, const int64_t* __restrict__ cache_len,
+                             int num_trees, int32_t* __restrict__ order) {
+  for (int i = threadIdx.x; i < num_trees; i += blockDim.x) {
+    const int64_t li = cache_len[i] + row_offsets[i + 1] - row_offsets[i];
+    int rank = 0;
+    for (int j = 0; j < num_trees; ++j) {
+      const int64_t lj = cache_len[j] + row_offsets[j + 1] - row_offsets[j];
+      rank += (lj > li || (lj == li && j < i)) ? 1 : 0;
+    }
+    order[rank] = i;
+  }
+}
+
 __global__ void embed_kernel(const int64_t* __restrict__ tokens, const __nv_bfloat16* __restrict__ embed,
                              int64_t vocab, int hidden, float* __restrict__ x, int32_t* status) {
   const int row = blockIdx.x;
@@ -255,6 +271,13 @@ __global__ void child_logprob_kernel(const __nv_bfloat16* __restrict__ h, const 
 }
 
 }  // namespace
+
+int launch_attention_order(const int64_t* row_offsets, const int64_t* cache_len, int num_trees, int32_t* order,
+                           cudaStream_t stream) {
+  if (num_trees <= 0) return SG_OK;
+  order_kernel<<<1, 1024, 0, stream>>>(row_offsets, cache_len, num_trees, order);
+  return check_launch("order_kernel");
+}
 
 int launch_tree_meta(const int64_t* row_offsets, const int64_t* parents, const int64_t* position_base,
                      const int64_t* request_ids, int num_trees, int num_rows, RowMeta meta, int32_t* status,

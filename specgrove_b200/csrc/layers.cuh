@@ -18,11 +18,15 @@ struct RowMeta {
   int32_t* tree;        // [Q] request (tree) index of the row
   int32_t* local;       // [Q] local node index
   int64_t* request_id;  // [Q] Philox key of the row's request
+  int32_t* order;       // [R] requests by decreasing K/V length (attention launch order)
 };
 
 int launch_tree_meta(const int64_t* row_offsets, const int64_t* parents, const int64_t* position_base,
                      const int64_t* request_ids, int num_trees, int num_rows, RowMeta meta, int32_t* status,
                      cudaStream_t stream);
+
+int launch_attention_order(const int64_t* row_offsets, const int64_t* cache_len, int num_trees, int32_t* order,
+                           cudaStream_t stream);
 
 int launch_embed(const int64_t* tokens, const __nv_bfloat16* embed, int64_t vocab, int hidden, int rows,
                  float* x, int32_t* status, cudaStream_t stream);
