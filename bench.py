@@ -195,7 +195,7 @@ class AcceptWorkload:
 
 
 class VerifyWorkload:
-    def __init__(self, rank: int, config: str):
+    def __init__(self, rank: int, config: str, layers: int | None = None):
         from specgrove_b200 import workloads
         from specgrove_b200.engine import QWEN3_4B, QWEN3_8B, B200Engine, Wave, Weights
         if config == "verify4b":
@@ -204,6 +204,11 @@ class VerifyWorkload:
         else:
             self.shape, mix, prefix = QWEN3_8B, workloads.TIER_MIX_CONFIG4, (1024, 4096)
             self.name = "config4: Qwen3-8B shape, 64 requests, prefixes U[1024,4096], tiers {16,32,64,128}, 2048 rows"
+        if layers is not None and layers != self.shape.num_layers:
+            import dataclasses
+            # profiling captures only: fewer layers keep an ncu capture small
+            self.shape = dataclasses.replace(self.shape, num_layers=layers)
+            self.name += f" [PROFILING ONLY: {layers} layers]"
         self.weights = Weights.random(self.shape, seed=1234)           # full replica on every rank
         self.wl = workloads.verify_workload(self.shape.vocab, mix, prefix, seed=rank)
         R = len(self.wl.trees)
@@ -217,8 +222,22 @@ class VerifyWorkload:
         self.dw = self.wave.to("cuda")
         self.R, self.rows, self.D = R, rows, self.wave.max_depth
         self.lengths_out = torch.empty(R, dtype=torch.long, device="cuda")
+        # Per-wave allocator score exchange across data-parallel ranks (the
+        # only collective of the step; a few KB over NCCL).
+        self.exchange = None
+        import torch.distributed as dist
+        if dist.is_initialized() and dist.get_world_size() > 1:
+            from specgrove_b200.allocator import RequestScores, ScoreExchange
+            rng = np.random.default_rng(1000 + rank)
+            self.scores = RequestScores(progress=[0] * R, ages=[0] * R,
+                                        service_weights=[float(x) for x in rng.choice([1.0, 2.0, 4.0], size=R)],
+                                        utilities=self.wl.utilities)
+            self.exchange = ScoreExchange(R, len(self.wl.tier_options), "cuda")
+            self.exchange.pack(self.scores)
 
     def step(self, seed: int, out: torch.Tensor, trace=None):
+        if self.exchange is not None:
+            self.exchange.exchange()
         self.engine.verify_device(self.dw, seed=seed, commit=True, accept_out=out, lengths_out=self.lengths_out,
                                   trace=trace)
 
@@ -253,7 +272,7 @@ def run_verify(args, world, rank):
     from specgrove_b200 import _lib
     from specgrove_b200.engine import TRACE_EVENTS, TRACE_STAGES
     hbm, tc, tc_sus, peak_kind = peaks()
-    wl = VerifyWorkload(rank, args.workload)
+    wl = VerifyWorkload(rank, args.workload, args.layers)
     K, W = args.steps, args.warmup
     outs = torch.empty((K, wl.R, wl.D + 2), dtype=torch.long, device="cuda")
     warm = torch.empty((wl.R, wl.D + 2), dtype=torch.long, device="cuda")
@@ -294,6 +313,7 @@ def run_verify(args, world, rank):
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, "
         "synthetic KV prefixes, seeded best-first trees)",
         "config": {"workload": wl.name, "model": "Qwen3-8B shape" if wl.shape.hidden == 4096 else "Qwen3-4B shape",
+                   "collective": "per-step NCCL all_gather_into_tensor of allocator scores" if world > 1 else None,
                    "requests_per_gpu": wl.R, "rows_per_gpu": wl.rows, "global_batch_rows": wl.rows * world,
                    "verify_pass_us_per_row": ms * 1000 / wl.rows, "temperature": 1.0,
                    "parallelism": f"dp{world}", "l2": "inputs larger than L2 (16.4 GB weights, ~24 GB KV/step)"},
@@ -304,6 +324,7 @@ def run_verify(args, world, rank):
                               "frac": pass_tflops / tc_sus, "algorithmic_flops_per_step": flops,
                               "peak_kind": peak_kind + " sustained"}},
         "stages_ms": {k: round(v, 4) for k, v in stages.items()},
+        "profiling_only": args.layers is not None and args.layers != 36,
         "cpu_baseline": cpu, "clocks": clk, "e2e": e2e, "gpu_launches": launches,
     }
     return line
@@ -509,7 +530,7 @@ def run_reference(args, world, rank):
         cpu = cpu_baseline_accept(wl)
         dtype = "fp64"
     else:
-        wl = VerifyWorkload(rank, args.workload)
+        wl = VerifyWorkload(rank, args.workload, args.layers)
         cpu = cpu_baseline_verify(wl, requests=2, budget_s=10.0)
         dtype = "fp32"
     line = {"impl": "reference", "metric": "accepted tokens/s/GPU", "value": cpu["value"],
@@ -529,6 +550,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="verify", choices=["verify", "verify4b", "accept"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="profiling only: build the model with this many layers (not a benchmark number)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -112,11 +112,12 @@ def acceptance_sweep(seed: int = 0, trees: int = 64, total_nodes: int = 4096, vo
 def best_first_tree(logs, ids, budget: int, rank_caps=None):
     """Best-first DDTree over per-depth top-k draft tokens (the product-
     probability heap of tree.py:148-212 with depth_reward = 0): returns
-    (parents incl. root -1, tokens per node (root -1), depths)."""
+    (parents incl. root -1, tokens per node (root -1), depths, prefix log
+    masses (root 0))."""
     import heapq
     length = len(logs)
     caps = rank_caps or [len(logs[0])] * length
-    parents, tokens, depths = [-1], [-1], [0]
+    parents, tokens, depths, masses = [-1], [-1], [0], [0.0]
     heap = [(-logs[0][0], 0, 0, 0, 0.0)]
     while heap and len(tokens) - 1 < budget:
         neg, parent, depth, rank, parent_log = heapq.heappop(heap)
@@ -124,11 +125,12 @@ def best_first_tree(logs, ids, budget: int, rank_caps=None):
         tokens.append(int(ids[depth][rank]))
         parents.append(parent)
         depths.append(depth + 1)
+        masses.append(-neg)
         if rank + 1 < caps[depth]:
             heapq.heappush(heap, (-(parent_log + logs[depth][rank + 1]), parent, depth, rank + 1, parent_log))
         if depth + 1 < length:
             heapq.heappush(heap, (neg - logs[depth + 1][0], node, depth + 1, 0, -neg))
-    return parents, tokens, depths
+    return parents, tokens, depths, masses
 
 
 # (rows incl. root) -> count; each mix sums to the configuration's row budget
@@ -141,6 +143,8 @@ class VerifyWorkload:
     trees: list            # per request (parents, tokens with the root token first)
     cache_lengths: list
     tiers: list
+    tier_options: list     # rows incl. root of every tier in the mix
+    utilities: list        # per request, draft expected tokens of each tier option
 
 
 def verify_workload(vocab: int, tier_mix: dict, prefix_range: tuple, seed: int = 0, block: int = 16,
@@ -156,14 +160,18 @@ def verify_workload(vocab: int, tier_mix: dict, prefix_range: tuple, seed: int =
     gen = torch.Generator(device=device).manual_seed(seed)
     trees, lengths = [], []
     budget = max(tiers) - 1
+    options = sorted(tier_mix)
+    utilities = []
     for i in range(R):
         draft = torch.randn((block, vocab), generator=gen, device=device) * draft_scale
         logq = torch.log_softmax(draft, -1)
         vals, idx = torch.topk(logq, top_k, dim=-1)
-        parents, tokens, _ = best_first_tree(vals.tolist(), idx.tolist(), budget, [top_k] * block)
+        parents, tokens, _, masses = best_first_tree(vals.tolist(), idx.tolist(), budget, [top_k] * block)
+        # expected draft tokens of each tier's prefix (continuous_tree_block_decode.py:560-568)
+        utilities.append([1.0 + float(np.exp(np.asarray(masses[1:t])).sum()) for t in options])
         n = tiers[i]
         parents, tokens = parents[:n], tokens[:n]
         tokens[0] = int(rng.integers(0, vocab))        # root row: last committed token
         trees.append((parents, tokens))
         lengths.append(int(rng.integers(prefix_range[0], prefix_range[1] + 1)))
-    return VerifyWorkload(trees, lengths, tiers)
+    return VerifyWorkload(trees, lengths, tiers, options, utilities)

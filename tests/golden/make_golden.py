@@ -21,6 +21,10 @@ functions (no restatement):
                      append_packed_sequence (:176-261) on random small caches.
   packed_inputs.npz  continuous_tree_block_decode._packed_block_inputs (:500-546)
                      on random trees: ids, positions and the additive mask.
+  allocator.json     continuous_tree_block_decode._allocate_global_tree_budgets
+                     (:706-795) on random problems (linear and measured-curve
+                     cost models) and _draft_tree_expected_tokens (:560-568) on
+                     probability_tree (tree.py:148-212) outputs.
 
 The fixtures are small (tens of KB) and deterministic (seeded torch CPU RNG).
 """
@@ -257,6 +261,37 @@ def build_packed_inputs(ref, gen):
         round_prefix=np.asarray([s.round_prefix_len for s in states], np.int64))
 
 
+def build_allocator(ref, gen):
+    import json
+    decode, tree_mod = ref.decode, ref.tree
+    problems = []
+    for case in range(12):
+        count = int(torch.randint(2, 9, (1,), generator=gen))
+        options = [15, 31, 63] if case % 2 else [11, 23, 45]
+        states = [SimpleNamespace(generated=[0] * int(torch.randint(0, 200, (1,), generator=gen)),
+                                  age=int(torch.randint(0, 30, (1,), generator=gen)), request_id=i)
+                  for i in range(count)]
+        utilities = [[1.0 + float(torch.rand(1, generator=gen)) * 3 * (k + 1) for k in range(len(options))]
+                     for _ in range(count)]
+        row_budget = count * (options[0] + 1) + int(torch.randint(0, count * 40 + 1, (1,), generator=gen))
+        curve = [[12, 24.5], [46, 24.6], [96, 24.8], [193, 25.1], [384, 39.0]] if case % 3 == 0 else None
+        fixed = None if curve else 20.0 + case
+        c = 1.0 if case % 4 else 0.0
+        alloc = decode._allocate_global_tree_budgets(
+            states, options, utilities, row_budget=row_budget, fixed_row_equivalent=fixed, criticality_weight=c,
+            max_new_tokens=256, row_cost_curve=curve)
+        problems.append(dict(progress=[len(s.generated) for s in states], ages=[s.age for s in states],
+                             options=options, utilities=utilities, row_budget=row_budget, curve=curve,
+                             fixed=fixed, criticality=c, max_new_tokens=256, allocation=list(alloc)))
+    trees = []
+    for case in range(4):
+        q = torch.softmax(3 * torch.randn((8, 64), generator=gen, dtype=torch.float64), -1)
+        t = tree_mod.probability_tree(q, 15, rank_caps=(4,) * 8)
+        trees.append(dict(masses=list(t.draft_prefix_log_masses), parents=list(t.parents),
+                          expected=decode._draft_tree_expected_tokens(t)))
+    (OUT / "allocator.json").write_text(json.dumps({"problems": problems, "trees": trees}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the specgrove checkout")
@@ -272,7 +307,8 @@ def main():
     build_follow(ref, gen)
     build_kv_commit(ref, gen)
     build_packed_inputs(ref, gen)
-    for p in sorted(OUT.glob("*.npz")):
+    build_allocator(ref, gen)
+    for p in sorted(OUT.glob("*.*")):
         print(p.name, p.stat().st_size)
 
 

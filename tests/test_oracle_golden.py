@@ -198,3 +198,17 @@ def test_wave_builder_validates_like_reference():
         Wave([([-1, 1], [1, 2])], [0], [0])
     with pytest.raises(ValueError, match="repeat"):
         Wave([([-1, 0, 0], [1, 2, 2])], [0], [0])
+
+
+def test_allocator_matches_reference(golden_dir):
+    import json
+    from specgrove_b200.allocator import allocate_tree_budgets, critical_path_weights, draft_tree_expected_tokens
+    z = json.loads((golden_dir / "allocator.json").read_text())
+    for p in z["problems"]:
+        weights = critical_path_weights(p["progress"], p["ages"], p["criticality"], p["max_new_tokens"])
+        curve = [tuple(x) for x in p["curve"]] if p["curve"] else None
+        alloc = allocate_tree_budgets(weights, p["options"], p["utilities"], row_budget=p["row_budget"],
+                                      fixed_row_equivalent=p["fixed"], row_cost_curve=curve)
+        assert list(alloc) == p["allocation"]
+    for t in z["trees"]:
+        assert draft_tree_expected_tokens(t["masses"]) == pytest.approx(t["expected"], rel=1e-12)
