@@ -1,4 +1,5 @@
 // Library-wide C ABI helpers: status strings, error detail, launch counter.
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -22,6 +23,14 @@ void set_error(const char* fmt, ...) {
 }
 
 void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+  static const bool enabled = [] {
+    const char* v = getenv("SG_PDL");
+    return v == nullptr || v[0] != '0';
+  }();
+  return enabled;
+}
 
 int device_sm_count() {
   int dev = 0;

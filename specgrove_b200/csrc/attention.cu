@@ -91,6 +91,8 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xchg + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+  pdl_trigger();
+  pdl_wait();  // q, the K/V tail and the launch order come from earlier kernels
   const int mtile = blockIdx.x;
   const int kvh = blockIdx.y;
   const int req = p.order != nullptr ? p.order[blockIdx.z] : static_cast<int>(blockIdx.z);
@@ -427,8 +429,7 @@ int launch_cfg(const CUtensorMap& map, const Params& p, dim3 grid, cudaStream_t 
                                        static_cast<int>(L::SMEM)));
     configured |= 1 << dev;
   }
-  kernel<<<grid, L::THREADS, L::SMEM, stream>>>(map, p);
-  return check_launch("tree_attention_tc_kernel");
+  return launch_pdl("tree_attention_tc_kernel", kernel, grid, dim3(L::THREADS), L::SMEM, stream, map, p);
 }
 
 }  // namespace

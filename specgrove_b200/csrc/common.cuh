@@ -46,6 +46,49 @@ inline int check_launch(const char* kernel) {
 
 int device_sm_count();
 
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with launch_pdl may start
+// while the previous kernel in the stream is still finishing: it triggers its
+// own dependents at entry (pdl_trigger), does setup that touches no global
+// data (barrier init, TMEM allocation, tensor-map prefetch), then calls
+// pdl_wait before its first global read, which returns once every preceding
+// kernel has completed and its writes are visible.  In a kernel launched
+// without the attribute both are no-ops.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_trigger() {
+#ifdef __CUDA_ARCH__
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#endif
+}
+__device__ __forceinline__ void pdl_wait() {
+#ifdef __CUDA_ARCH__
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+}
+
+bool pdl_enabled();  // SG_PDL=0 disables programmatic dependent launch
+
+template <typename... Params, typename... Args>
+int launch_pdl(const char* name, void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+               cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+  if (err != cudaSuccess) {
+    set_error("%s launch failed: %s", name, cudaGetErrorString(err));
+    return SG_ERR_CUDA;
+  }
+  return check_launch(name);
+}
+
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
 

@@ -75,6 +75,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -95,6 +96,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // activations and the residual stream come from the previous kernel
 
   auto fail_wait = [&](void) {
     *abort_flag = 1;
@@ -420,8 +422,8 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Shape& shape, con
   const int sms = device_sm_count();
   const int grid = shape.tiles < sms ? shape.tiles : sms;
   if (grid <= 0) return SG_OK;
-  gemm_kernel<Epi><<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, shape, ep);
-  return check_launch("gemm_kernel");
+  return launch_pdl("gemm_kernel", gemm_kernel<Epi>, dim3(grid), dim3(THREADS), SMEM_BYTES, stream, ta, tb, shape,
+                    ep);
 }
 
 }  // namespace gemm

@@ -95,6 +95,8 @@ __global__ void embed_kernel(const int64_t* __restrict__ tokens, const __nv_bflo
 // y = bf16(x * rsqrt(mean(x^2) + eps) * w); one CTA of 256 threads per row.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                                                       int hidden, float eps, __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(row) * hidden);
   const int n4 = hidden / 4;
@@ -138,6 +140,8 @@ template <int D>
 __global__ void __launch_bounds__(256) qkv_post_kernel(const QkvPost p) {
   constexpr int PER = D / 32;
   constexpr int HALF = D / 2;
+  pdl_trigger();
+  pdl_wait();
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int heads = p.nq + 2 * p.nkv;
@@ -301,8 +305,7 @@ int launch_rmsnorm(const float* x, const __nv_bfloat16* weight, int hidden, int 
                    __nv_bfloat16* out, cudaStream_t stream) {
   if (rows <= 0) return SG_OK;
   if (hidden % 4 != 0) return fail(SG_ERR_UNSUPPORTED, "rmsnorm: hidden % 4 != 0");
-  rmsnorm_kernel<<<rows, 256, 0, stream>>>(x, weight, hidden, eps, out);
-  return check_launch("rmsnorm_kernel");
+  return launch_pdl("rmsnorm_kernel", rmsnorm_kernel, dim3(rows), dim3(256), 0, stream, x, weight, hidden, eps, out);
 }
 
 int launch_qkv_post(const QkvPost& p, cudaStream_t stream) {
@@ -310,12 +313,10 @@ int launch_qkv_post(const QkvPost& p, cudaStream_t stream) {
   const int64_t warps = static_cast<int64_t>(p.rows) * (p.nq + 2 * p.nkv);
   const unsigned grid = static_cast<unsigned>((warps + 7) / 8);
   if (p.head_dim == 128)
-    qkv_post_kernel<128><<<grid, 256, 0, stream>>>(p);
-  else if (p.head_dim == 64)
-    qkv_post_kernel<64><<<grid, 256, 0, stream>>>(p);
-  else
-    return fail(SG_ERR_UNSUPPORTED, "qkv_post: head_dim must be 64 or 128");
-  return check_launch("qkv_post_kernel");
+    return launch_pdl("qkv_post_kernel", qkv_post_kernel<128>, dim3(grid), dim3(256), 0, stream, p);
+  if (p.head_dim == 64)
+    return launch_pdl("qkv_post_kernel", qkv_post_kernel<64>, dim3(grid), dim3(256), 0, stream, p);
+  return fail(SG_ERR_UNSUPPORTED, "qkv_post: head_dim must be 64 or 128");
 }
 
 int launch_lm_combine(const float4* partials, int n_tiles, int rows, float* lse, int64_t* posterior,
