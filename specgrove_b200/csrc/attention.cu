@@ -417,6 +417,489 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
   }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent tensor-memory-resident kernel, 128-key tiles, split-KV softmax.
+//
+// One CTA per SM draws work items — (request, kv head, 128-row query block),
+// longest requests first — from a per-launch atomic counter, and every role
+// streams across item boundaries: the TMA warp fetches the next item and
+// starts its K/V loads while the current item's last tiles are computed.
+//
+// Q and P live in TMEM and feed the MMAs as the A operand, so shared memory
+// holds only the K/V ring and the tensor core reads just K or V from it.
+// S = Q K^T of a 128-key tile is one N=128 MMA chain.  The two softmax warps
+// of a TMEM lane quarter (one SM sub-partition) each own one 64-key half of
+// every tile with their own running max, sum and O accumulator (split-KV
+// inside the CTA), so they never exchange anything per tile; the halves merge
+// once per item.  The MMA thread follows a fixed schedule with blocking
+// waits: QK^T of tile j as soon as K_j has landed and S_{j-1} has been read,
+// then PV of tile j-1 (two independent N=D chains, one per half) once P_{j-1}
+// is written.  The exponentials of tile j overlap PV_{j-1}.
+//
+// TMEM columns (512): O_half0 [0, D), O_half1 [D, 2D), Q [2D, 2.5D) as bf16
+// pairs, P_half0 / P_half1 (32 columns each, bf16 pairs), S (128 fp32).
+template <int D, int STAGES>
+struct TmLayout {
+  static constexpr int BN = 128;                          // keys per tile
+  static constexpr int HK = BN / 2;                       // keys per softmax half
+  static constexpr int THREADS = 64 + 256;                // TMA, MMA, 8 softmax warps
+  static constexpr int HALVES = D / 64;                   // 64-dim swizzle blocks
+  static constexpr uint32_t KV_HALF = BN * 128;           // 128 keys x 64 dims
+  static constexpr uint32_t KV_BYTES = HALVES * KV_HALF;  // one K or V tile
+  static constexpr uint32_t OFF_K = 0;
+  static constexpr uint32_t OFF_V = STAGES * KV_BYTES;
+  static constexpr uint32_t OFF_RED = 2 * STAGES * KV_BYTES;  // [2 halves][2: max, sum][128] floats
+  static constexpr uint32_t OFF_ITEM = OFF_RED + 4 * 128 * 4;  // [2] published work items
+  static constexpr uint32_t OFF_BAR = OFF_ITEM + 128;
+  static constexpr size_t SMEM = OFF_BAR + 256;
+  static constexpr uint32_t O_COL = 0;                    // + half * D
+  static constexpr uint32_t Q_COL = 2 * D;
+  static constexpr uint32_t P_COL = Q_COL + D / 2;        // + half * HK / 2
+  static constexpr uint32_t S_COL = P_COL + HK;           // + half * HK
+  static_assert(S_COL + BN <= 512, "TMEM column map");
+  static_assert(SMEM <= 232448, "shared memory");
+};
+
+// One work item as published by the TMA warp (tiles < 0: no more work).
+struct WorkItem {
+  int64_t q0;        // first packed query row of the request
+  int64_t lp;        // cached prefix length L
+  int32_t kvh;
+  int32_t m_base;    // first query row (token-major x group) of the block
+  int32_t n;         // tree rows of the request
+  int32_t tiles;     // 128-key tiles over L + n keys
+  int32_t row0;      // first arena row of the request's slot
+  int32_t active_q;  // TMEM lane quarters holding at least one query row
+};
+static_assert(sizeof(WorkItem) <= 64, "work item slot");
+
+template <int D, int STAGES>
+__global__ void __launch_bounds__(TmLayout<D, STAGES>::THREADS, 1)
+tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Params p) {
+  using L = TmLayout<D, STAGES>;
+  constexpr int BN = L::BN;
+  constexpr int HK = L::HK;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if ((smem_u32(smem) & 1023u) != 0u) {
+    if (threadIdx.x == 0 && p.status != nullptr) atomicMax(p.status, static_cast<int32_t>(SG_ERR_UNSUPPORTED));
+    return;
+  }
+  WorkItem* items = reinterpret_cast<WorkItem*>(smem + L::OFF_ITEM);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* kv_full = bars;               // [STAGES]
+  uint64_t* kv_empty = kv_full + STAGES;  // [STAGES]
+  uint64_t* s_full = kv_empty + STAGES;   // S of a tile written
+  uint64_t* s_free = s_full + 1;          // S read by every softmax thread
+  uint64_t* p_full = s_free + 1;          // P (both halves) written
+  uint64_t* o_done = p_full + 1;          // PV of a tile complete
+  uint64_t* q_full = o_done + 1;          // Q rows of an item in TMEM
+  uint64_t* merge = q_full + 1;           // [4 quarters] per-item (max, sum) exchange
+  uint64_t* item_full = merge + 4;        // [2] work item published
+  uint64_t* item_empty = item_full + 2;   // [2] work item read by every consumer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    // Per-tile and per-item barriers count every softmax thread.
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 256);
+    mbar_init(p_full, 256);
+    mbar_init(o_done, 1);
+    mbar_init(q_full, 256);
+    for (int i = 0; i < 4; ++i) mbar_init(&merge[i], 64);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], 1 + 256);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tensormap(&kv_map);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();  // q, the K/V tail and the work list come from earlier kernels
+
+  auto give_up = [&]() {
+    *abort_flag = 1;
+    if (p.status != nullptr) atomicMax(p.status, static_cast<int32_t>(SG_ERR_CUDA));
+  };
+  // Consumers: wait for work item `seq`, copy it, release the slot.
+  auto next_item = [&](int seq, WorkItem& it) -> bool {
+    if (!mbar_wait(&item_full[seq & 1], (seq >> 1) & 1)) return false;
+    it = items[seq & 1];
+    mbar_arrive(&item_empty[seq & 1]);
+    return true;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------ scheduler + TMA producer
+    if (lane == 0) {
+      const int total = *p.num_items;
+      int64_t gt = 0;  // tiles loaded so far (across items)
+      for (int seq = 0;; ++seq) {
+        WorkItem it;
+        it.tiles = -1;
+        while (!*abort_flag) {
+          const int i = atomicAdd(p.work_counter, 1);
+          if (i >= total) break;
+          const int code = p.items[i];
+          const int req = code >> 16;
+          const int64_t q0 = p.row_offsets[req];
+          const int64_t q1 = p.row_offsets[req + 1];
+          const int64_t lp = p.cache_len[req];
+          const int64_t slot = p.slots[req];
+          if (q0 < 0 || q1 > p.num_rows || q1 - q0 < 1 || q1 - q0 > layers::kMaxTreeRows) continue;
+          const int n = static_cast<int>(q1 - q0);
+          const int m_base = (code & 0xff) * BM;
+          if (m_base >= n * p.group) continue;
+          // Never read outside the request's own slot (the QKV kernel reports
+          // the capacity error for such a request).
+          if (slot < 0 || (slot + 1) * p.capacity > p.plane_rows || lp < 0 || lp + n > p.capacity) continue;
+          it.q0 = q0;
+          it.lp = lp;
+          it.kvh = (code >> 8) & 0xff;
+          it.m_base = m_base;
+          it.n = n;
+          it.tiles = static_cast<int>((lp + n + BN - 1) / BN);
+          it.row0 = static_cast<int>(slot * p.capacity);
+          it.active_q = min(4, (n * p.group - m_base + 31) / 32);
+          break;
+        }
+        if (!mbar_wait(&item_empty[seq & 1], ((seq >> 1) & 1) ^ 1u)) {
+          give_up();
+          break;
+        }
+        items[seq & 1] = it;
+        mbar_arrive(&item_full[seq & 1]);
+        if (it.tiles < 0) break;
+        const int plane_k = p.plane_k0 + it.kvh, plane_v = p.plane_v0 + it.kvh;
+        for (int j = 0; j < it.tiles; ++j, ++gt) {
+          const int s = static_cast<int>(gt % STAGES);
+          if (*abort_flag || !mbar_wait(&kv_empty[s], static_cast<uint32_t>((gt / STAGES) & 1) ^ 1u)) {
+            give_up();
+            break;
+          }
+          mbar_arrive_expect_tx(&kv_full[s], 2 * L::KV_BYTES);
+          const int row = it.row0 + j * BN;
+#pragma unroll
+          for (int h = 0; h < L::HALVES; ++h)
+#pragma unroll
+            for (int rb = 0; rb < BN / kKeyTile; ++rb) {  // the map's box is kKeyTile rows
+              const uint32_t off = h * L::KV_HALF + rb * kKeyTile * 128;
+              tma_load_3d(smem + L::OFF_K + s * L::KV_BYTES + off, &kv_map, h * 64, row + rb * kKeyTile, plane_k,
+                          &kv_full[s]);
+              tma_load_3d(smem + L::OFF_V + s * L::KV_BYTES + off, &kv_map, h * 64, row + rb * kKeyTile, plane_v,
+                          &kv_full[s]);
+            }
+        }
+        if (*abort_flag) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_qk = idesc_bf16_f32(BM, BN);
+      const uint32_t idesc_pv = idesc_bf16_f32(BM, D) | (1u << 16);  // B (V) is MN-major
+      int64_t gt = 0;  // tiles consumed so far (across items)
+      bool ok = true;
+      for (int seq = 0; ok; ++seq) {
+        WorkItem it;
+        if (!next_item(seq, it)) {
+          ok = false;
+          break;
+        }
+        if (it.tiles < 0) break;
+        if (!mbar_wait(q_full, seq & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int j = 0; j <= it.tiles; ++j) {
+          const int64_t g = gt + j;
+          if (j < it.tiles) {  // S_j = Q K_j^T
+            const int s = static_cast<int>(g % STAGES);
+            if (!mbar_wait(&kv_full[s], static_cast<uint32_t>((g / STAGES) & 1)) ||
+                (g > 0 && !mbar_wait(s_free, static_cast<uint32_t>((g - 1) & 1)))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t k_addr = smem_u32(smem + L::OFF_K + s * L::KV_BYTES);
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks) {
+              const uint32_t koff = (ks >> 2) * L::KV_HALF + (ks & 3) * 32;
+              mma_bf16_ta(tmem + L::S_COL, tmem + L::Q_COL + ks * 8, desc_k_sw128(k_addr + koff), idesc_qk,
+                          ks > 0 ? 1u : 0u);
+            }
+            mma_commit(s_full);
+          }
+          if (j > 0) {  // O_h += P_{j-1,h} V_{j-1,h}
+            if (!mbar_wait(p_full, static_cast<uint32_t>((g - 1) & 1))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const int s = static_cast<int>((g - 1) % STAGES);
+            const uint32_t v_addr = smem_u32(smem + L::OFF_V + s * L::KV_BYTES);
+#pragma unroll
+            for (int ks = 0; ks < HK / 16; ++ks)
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {  // the two halves' chains interleave
+                const uint64_t bdesc = desc_mn_sw128(v_addr + (h * HK + ks * 16) * 128, L::KV_HALF, 1024);
+                mma_bf16_ta(tmem + L::O_COL + h * D, tmem + L::P_COL + h * (HK / 2) + ks * 8, bdesc, idesc_pv,
+                            (j > 1 || ks > 0) ? 1u : 0u);
+              }
+            mma_commit(&kv_empty[s]);
+            mma_commit(o_done);
+          }
+        }
+        gt += it.tiles;
+      }
+      if (!ok) give_up();
+    }
+  } else {
+    // --------------------------------------------------------------- softmax
+    // Warp w serves TMEM lane quarter w % 4 (the lanes it may access) and key
+    // half hf = (w - 2) / 4 of every tile, one 64-key row per thread.  A warp
+    // whose quarter holds no query row of an item still takes every barrier
+    // step of every tile (it only skips the work): parity waits are exact
+    // only for a waiter at most one phase away from the barrier, so no warp
+    // may skip phases and later rejoin.
+    const int quarter = warp & 3;
+    const int hf = (warp - 2) >> 2;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const float c2 = p.scale_log2;
+    float* red = reinterpret_cast<float*>(smem + L::OFF_RED);
+    int64_t gt = 0;
+    int merges = 0;  // items this quarter was active in (merge barrier phase)
+    bool ok = true;
+    for (int seq = 0; ok; ++seq) {
+      WorkItem it;
+      if (!next_item(seq, it)) {
+        ok = false;
+        break;
+      }
+      if (it.tiles < 0) break;
+      const int tiles = it.tiles;
+      if (quarter >= it.active_q) {
+        // Idle quarter: take every barrier step of every tile (no work).
+        tc_fence_before();
+        mbar_arrive(q_full);
+        for (int j = 0; j < tiles && ok; ++j) {
+          const int64_t g = gt + j;
+          if (!mbar_wait(s_full, static_cast<uint32_t>(g & 1))) ok = false;
+          mbar_arrive(s_free);
+          if (ok && j > 0 && !mbar_wait(o_done, static_cast<uint32_t>((g - 1) & 1))) ok = false;
+          mbar_arrive(p_full);
+        }
+        if (ok && !mbar_wait(o_done, static_cast<uint32_t>((gt + tiles - 1) & 1))) ok = false;
+        gt += tiles;
+        continue;
+      }
+      const int rows_total = it.n * p.group;
+      const int m_row = it.m_base + r;
+      const bool valid = m_row < rows_total;
+      const int tok = valid ? m_row / p.group : 0;
+      const int head = it.kvh * p.group + (valid ? m_row % p.group : 0);
+      const int64_t kv_total = it.lp + it.n;
+      {  // half of the Q row -> TMEM, two bf16 per column
+        constexpr int QW = D / 4;
+        uint32_t qw[QW];
+        const uint4* src = reinterpret_cast<const uint4*>(p.q + ((it.q0 + tok) * p.nq + head) * D + hf * (D / 2));
+#pragma unroll
+        for (int c = 0; c < QW / 4; ++c) {
+          const uint4 v = valid ? src[c] : make_uint4(0u, 0u, 0u, 0u);
+          qw[4 * c + 0] = v.x;
+          qw[4 * c + 1] = v.y;
+          qw[4 * c + 2] = v.z;
+          qw[4 * c + 3] = v.w;
+        }
+        if constexpr (QW == 32)
+          tmem_st32u(tmem + lane_base + L::Q_COL + hf * QW, qw);
+        else
+          tmem_st16u(tmem + lane_base + L::Q_COL + hf * QW, qw);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(q_full);
+      }
+      uint32_t anc[layers::kAncWords];
+      const uint32_t* ap = p.anc + (it.q0 + tok) * layers::kAncWords;
+#pragma unroll
+      for (int w = 0; w < layers::kAncWords; ++w) anc[w] = ap[w];
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int j = 0; j < tiles; ++j) {
+        const int64_t g = gt + j;
+        if (!mbar_wait(s_full, static_cast<uint32_t>(g & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float sv[HK];
+        {
+          uint32_t raw[HK];
+          tmem_ld32_nowait(tmem + lane_base + L::S_COL + hf * HK, raw);
+          tmem_ld32_nowait(tmem + lane_base + L::S_COL + hf * HK + 32, raw + 32);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < HK; ++e) sv[e] = __uint_as_float(raw[e]);
+        }
+        tc_fence_before();
+        mbar_arrive(s_free);
+        const int64_t key0 = static_cast<int64_t>(j) * BN + hf * HK;
+        if (key0 + HK > it.lp) {  // this half reaches the tree keys or the end
+#pragma unroll
+          for (int e = 0; e < HK; ++e) {
+            const int64_t key = key0 + e;
+            bool vis = true;
+            if (key >= it.lp) {
+              const int k = static_cast<int>(key - it.lp);
+              vis = key < kv_total && ((anc[k >> 5] >> (k & 31)) & 1u);
+            }
+            if (!vis) sv[e] = -INFINITY;
+          }
+        }
+        float mt;
+        {  // pairwise max
+          float t[HK / 2];
+#pragma unroll
+          for (int e = 0; e < HK / 2; ++e) t[e] = fmaxf(sv[2 * e], sv[2 * e + 1]);
+#pragma unroll
+          for (int w = HK / 4; w >= 1; w >>= 1)
+#pragma unroll
+            for (int e = 0; e < w; ++e) t[e] = fmaxf(t[e], t[e + w]);
+          mt = t[0] * c2;
+        }
+        // Lazy rescaling: move the reference max only when the tile max
+        // exceeds it by more than 2^8 (the first tile always sets it).
+        const bool grow = j == 0 || mt > m_run + kRescaleThreshold;
+        const bool rescale = j > 0 && __any_sync(0xffffffffu, grow);
+        float alpha = 1.f;
+        if (grow) {
+          alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - mt);
+          m_run = mt;
+        }
+        // A row whose keys so far are all masked has m_run = -inf; its P is
+        // then 0 (not NaN) with the offset taken as 0.
+        const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        uint32_t pw[HK / 2];
+#pragma unroll
+        for (int c = 0; c < HK / 8; ++c) {
+          float e8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            e8[e] = fast_exp2(fmaf(sv[c * 8 + e], c2, neg_m));
+            acc[e] += e8[e];
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) pw[c * 4 + e] = pack_bf16x2(e8[2 * e], e8[2 * e + 1]);
+        }
+        l_run = l_run * alpha + (((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7])));
+        // P and this half's O accumulator were last used by PV of tile g-1
+        if (j > 0 && !mbar_wait(o_done, static_cast<uint32_t>((g - 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (rescale) {  // rare: the row max grew by more than 2^8
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float o[32];
+            tmem_ld32(tmem + lane_base + L::O_COL + hf * D + c * 32, o);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] *= alpha;
+            tmem_st32(tmem + lane_base + L::O_COL + hf * D + c * 32, o);
+          }
+        }
+        tmem_st32u(tmem + lane_base + L::P_COL + hf * (HK / 2), pw);
+        tmem_wait_st();
+        if (key0 + HK > kv_total) {
+          // Keys past the request's tail come from stale arena rows (possibly
+          // NaN bit patterns); P is 0 there, but 0 * NaN is NaN in the MMA,
+          // so zero those rows of this half of the V tile before P is released.
+          const int s = static_cast<int>(g % STAGES);
+          for (int v = r; v < HK; v += 32 * it.active_q) {
+            if (key0 + v < kv_total) continue;
+            uint8_t* vrow = smem + L::OFF_V + s * L::KV_BYTES + (hf * HK + v) * 128;
+#pragma unroll
+            for (int h = 0; h < L::HALVES; ++h)
+#pragma unroll
+              for (int c = 0; c < 8; ++c)
+                *reinterpret_cast<uint4*>(vrow + h * L::KV_HALF + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+          }
+          fence_proxy_async_smem();
+        }
+        tc_fence_before();
+        mbar_arrive(p_full);
+      }
+      if (ok && !mbar_wait(o_done, static_cast<uint32_t>((gt + tiles - 1) & 1))) ok = false;
+      if (!ok) break;
+      // Merge the two halves' (max, sum, O): each warp writes out half of the
+      // O columns.  The next item's first PV overwrites O only after every
+      // softmax thread arrived on that item's q_full.
+      red[(hf * 2 + 0) * 128 + r] = m_run;
+      red[(hf * 2 + 1) * 128 + r] = l_run;
+      tc_fence_before();
+      mbar_arrive(&merge[quarter]);
+      if (!mbar_wait(&merge[quarter], merges & 1)) {
+        ok = false;
+        break;
+      }
+      ++merges;
+      {
+        const float m0 = red[0 * 128 + r], l0 = red[1 * 128 + r];
+        const float m1 = red[2 * 128 + r], l1 = red[3 * 128 + r];
+        const float m = fmaxf(m0, m1);
+        const float w0 = m0 == -INFINITY ? 0.f : fast_exp2(m0 - m);
+        const float w1 = m1 == -INFINITY ? 0.f : fast_exp2(m1 - m);
+        const float inv = 1.f / (l0 * w0 + l1 * w1);
+        tc_fence_after();
+        __nv_bfloat16* dst = p.out + ((it.q0 + tok) * p.nq + head) * D + hf * (D / 2);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          float o0[32], o1[32];
+          const uint32_t col = hf * (D / 2) + c * 32;
+          tmem_ld32(tmem + lane_base + L::O_COL + col, o0);
+          tmem_ld32(tmem + lane_base + L::O_COL + D + col, o1);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o0[e] = (o0[e] * w0 + o1[e] * w1) * inv;
+          if (valid) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 w;
+              w.x = pack_bf16x2(o0[q * 8 + 0], o0[q * 8 + 1]);
+              w.y = pack_bf16x2(o0[q * 8 + 2], o0[q * 8 + 3]);
+              w.z = pack_bf16x2(o0[q * 8 + 4], o0[q * 8 + 5]);
+              w.w = pack_bf16x2(o0[q * 8 + 6], o0[q * 8 + 7]);
+              d4[q] = w;
+            }
+          }
+        }
+      }
+      gt += tiles;
+    }
+    if (!ok) give_up();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 template <int D, int BN, int STAGES, int SPLIT>
 int launch_cfg(const CUtensorMap& map, const Params& p, dim3 grid, cudaStream_t stream) {
   using L = Layout<D, BN, STAGES, SPLIT>;
@@ -430,6 +913,26 @@ int launch_cfg(const CUtensorMap& map, const Params& p, dim3 grid, cudaStream_t 
     configured |= 1 << dev;
   }
   return launch_pdl("tree_attention_tc_kernel", kernel, grid, dim3(L::THREADS), L::SMEM, stream, map, p);
+}
+
+template <int D, int STAGES>
+int launch_tm(const CUtensorMap& map, const Params& p, int num_requests, cudaStream_t stream) {
+  using L = TmLayout<D, STAGES>;
+  auto kernel = tree_attention_tm_kernel<D, STAGES>;
+  static int configured = 0;
+  int dev = 0;
+  SG_CUDA_CHECK(cudaGetDevice(&dev));
+  if (!(configured & (1 << dev))) {
+    SG_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(L::SMEM)));
+    configured |= 1 << dev;
+  }
+  if (p.items == nullptr || p.num_items == nullptr || p.work_counter == nullptr)
+    return fail(SG_ERR_INVALID_ARGUMENT, "tree attention: missing work list");
+  // One CTA per SM; every (request, kv head) has at least one item.
+  const int ctas = static_cast<int>(min64(device_sm_count(), static_cast<int64_t>(num_requests) * p.nkv));
+  return launch_pdl("tree_attention_tm_kernel", kernel, dim3(static_cast<unsigned>(ctas)), dim3(L::THREADS), L::SMEM,
+                    stream, map, p);
 }
 
 }  // namespace
@@ -449,6 +952,17 @@ int launch(const CUtensorMap& kv_map, const Params& p, int num_requests, int max
     const char* v = getenv("SG_ATTN_SPLIT");
     return v != nullptr ? atoi(v) : 2;
   }();
+  static const int impl = [] {
+    const char* v = getenv("SG_ATTN_IMPL");
+    return v != nullptr ? atoi(v) : 6;
+  }();
+  if (impl >= 5) {
+    if (head_dim == 128) {
+      if (impl == 5) return launch_tm<128, 2>(kv_map, p, num_requests, stream);
+      return launch_tm<128, 3>(kv_map, p, num_requests, stream);
+    }
+    if (head_dim == 64) return launch_tm<64, 4>(kv_map, p, num_requests, stream);
+  }
   if (head_dim == 128) {
     if (split == 1) return launch_cfg<128, kKeyTile, 4, 1>(kv_map, p, grid, stream);
     return launch_cfg<128, kKeyTile, 4, 2>(kv_map, p, grid, stream);

@@ -24,6 +24,9 @@ struct Params {
   int nq, nkv, group;
   int plane_k0, plane_v0;    // arena plane of kv head 0's K and V for this layer
   const int32_t* order;      // [R] requests in launch order (longest first), or null
+  const int32_t* items;      // persistent kernel: request << 16 | kv_head << 8 | 128-row block
+  const int32_t* num_items;  // [1]
+  int32_t* work_counter;     // next item; zero before the launch
   float scale_log2;          // softmax scale * log2(e)
   int32_t* status;
 };

@@ -51,6 +51,7 @@ struct Engine {
   float* lse_ws;
   int64_t* posterior_ws;
   layers::RowMeta meta;
+  layers::AttentionWork work;
   int vocab_tiles;
 };
 
@@ -64,6 +65,14 @@ T* carve(uint8_t*& cursor, size_t count) {
 inline void trace(const sg_wave_desc& w, int point, cudaStream_t stream) {
   if (w.trace_events != nullptr && w.trace_events[point] != nullptr)
     cudaEventRecord(static_cast<cudaEvent_t>(w.trace_events[point]), stream);
+}
+
+// Upper bound on the tree attention's (request, kv head, 128-row block)
+// items: per kv head, sum over requests of ceil(n_i * G / 128) <= rows * G /
+// 128 + requests, and requests <= rows.
+int attention_item_capacity(const sg_model_desc& m, int rows) {
+  const int G = m.num_q_heads / m.num_kv_heads;
+  return m.num_kv_heads * ((rows * G + 127) / 128 + rows);
 }
 
 size_t workspace_size(const sg_model_desc& m, int rows) {
@@ -84,6 +93,8 @@ size_t workspace_size(const sg_model_desc& m, int rows) {
   s += rows * 4 * 3 + 3 * 256;                // position, tree, local
   s += rows * 8 + 256;                        // request id
   s += rows * 4 + 256;                        // attention order (R <= rows)
+  s += attention_item_capacity(m, rows) * 4 + 256;  // attention work list
+  s += (m.num_layers + 1) * 4 + 256;          // item count, per-layer work counters
   return s + 4096;
 }
 
@@ -171,6 +182,11 @@ extern "C" int sg_engine_create(const sg_model_desc* model, const sg_arena_desc*
   e->meta.local = carve<int32_t>(cur, max_rows);
   e->meta.request_id = carve<int64_t>(cur, max_rows);
   e->meta.order = carve<int32_t>(cur, max_rows);
+  e->work.order = e->meta.order;
+  e->work.item_capacity = attention_item_capacity(m, max_rows);
+  e->work.items = carve<int32_t>(cur, e->work.item_capacity);
+  e->work.num_items = carve<int32_t>(cur, 1);
+  e->work.counters = carve<int32_t>(cur, m.num_layers);
   if (static_cast<size_t>(cur - static_cast<uint8_t*>(e->workspace)) > e->workspace_bytes) {
     cudaFree(e->workspace);
     return fail(SG_ERR_WORKSPACE, "sg_engine_create: workspace layout overflow");
@@ -232,7 +248,8 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
                                  stream)) != SG_OK)
     return st;
 
-  if ((st = layers::launch_attention_order(w.row_offsets, w.cache_lengths, R, e->meta.order, stream)) != SG_OK)
+  if ((st = layers::launch_attention_work(w.row_offsets, w.cache_lengths, R, nq / nkv, nkv, e->work, m.num_layers,
+                                         stream)) != SG_OK)
     return st;
   trace(w, 1, stream);
   const gemm::Shape s_qkv = gemm::make_shape(Q, qkv_n, H);
@@ -297,6 +314,9 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
     ap.plane_k0 = l * 2 * nkv;
     ap.plane_v0 = l * 2 * nkv + nkv;
     ap.order = e->meta.order;
+    ap.items = e->work.items;
+    ap.num_items = e->work.num_items;
+    ap.work_counter = e->work.counters + l;
     ap.status = w.status;
     ap.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
     if ((st = attn::launch(e->kv_map, ap, R, w.max_rows_per_request, D, stream)) != SG_OK) return st;

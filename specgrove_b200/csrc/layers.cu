@@ -66,9 +66,21 @@ __global__ void tree_meta_kernel(const int64_t* __restrict__ row_offsets, const 
 // Launch order of the tree attention: requests by decreasing K/V length
 // (cache prefix + tree rows), ties by index, so the longest CTAs start first
 // and the grid's tail is short.  One CTA; R is small.
-__global__ void order_kernel(const int64_t* __restrict__ row_offsets, const int64_t* __restrict__ cache_len,
-                             int num_trees, int32_t* __restrict__ order) {
-  for (int i = threadIdx.x; i < num_trees; i += blockDim.x) {
+// Work list of the persistent tree attention.  Requests are ranked by
+// decreasing K/V length (ties by index) so the kernel's tail runs the short
+// items; each expands to its (kv head, 128-row query block) items, packed as
+// request << 16 | kv_head << 8 | block.  Also zeroes the per-layer work
+// counters the attention CTAs draw items from.  One CTA of 1024 threads.
+__global__ void __launch_bounds__(1024) attention_work_kernel(const int64_t* __restrict__ row_offsets,
+                                                              const int64_t* __restrict__ cache_len, int num_trees,
+                                                              int group, int num_kv_heads, int32_t* __restrict__ order,
+                                                              int32_t* __restrict__ items, int item_capacity,
+                                                              int32_t* __restrict__ num_items,
+                                                              int32_t* __restrict__ counters, int num_counters) {
+  __shared__ int s_scan[1024];
+  const int tid = threadIdx.x;
+  for (int i = tid; i < num_counters; i += blockDim.x) counters[i] = 0;
+  for (int i = tid; i < num_trees; i += blockDim.x) {
     const int64_t li = cache_len[i] + row_offsets[i + 1] - row_offsets[i];
     int rank = 0;
     for (int j = 0; j < num_trees; ++j) {
@@ -77,6 +89,34 @@ __global__ void order_kernel(const int64_t* __restrict__ row_offsets, const int6
     }
     order[rank] = i;
   }
+  __syncthreads();
+  auto blocks = [&](int req) -> int {  // 128-row query blocks of one kv head
+    const int64_t n = row_offsets[req + 1] - row_offsets[req];
+    if (n < 1 || n > kMaxTreeRows) return 0;  // malformed: tree_meta reports it
+    return static_cast<int>((n * group + 127) / 128);
+  };
+  const int per = (num_trees + 1023) / 1024;
+  const int c0 = min(num_trees, tid * per);
+  const int c1 = min(num_trees, c0 + per);
+  int local = 0;
+  for (int r = c0; r < c1; ++r) local += blocks(order[r]) * num_kv_heads;
+  s_scan[tid] = local;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {  // inclusive scan
+    const int v = tid >= off ? s_scan[tid - off] : 0;
+    __syncthreads();
+    s_scan[tid] += v;
+    __syncthreads();
+  }
+  int at = s_scan[tid] - local;
+  for (int r = c0; r < c1; ++r) {
+    const int req = order[r];
+    const int nb = blocks(req);
+    for (int h = 0; h < num_kv_heads; ++h)
+      for (int b = 0; b < nb; ++b, ++at)
+        if (at < item_capacity) items[at] = (req << 16) | (h << 8) | b;
+  }
+  if (tid == 1023) *num_items = min(s_scan[1023], item_capacity);
 }
 
 __global__ void embed_kernel(const int64_t* __restrict__ tokens, const __nv_bfloat16* __restrict__ embed,
@@ -276,11 +316,15 @@ __global__ void child_logprob_kernel(const __nv_bfloat16* __restrict__ h, const 
 
 }  // namespace
 
-int launch_attention_order(const int64_t* row_offsets, const int64_t* cache_len, int num_trees, int32_t* order,
-                           cudaStream_t stream) {
+int launch_attention_work(const int64_t* row_offsets, const int64_t* cache_len, int num_trees, int group,
+                          int num_kv_heads, AttentionWork work, int num_layers, cudaStream_t stream) {
   if (num_trees <= 0) return SG_OK;
-  order_kernel<<<1, 1024, 0, stream>>>(row_offsets, cache_len, num_trees, order);
-  return check_launch("order_kernel");
+  if (num_trees > 65535 || num_kv_heads > 255 || group > 127)
+    return fail(SG_ERR_UNSUPPORTED, "tree attention work list: > 65535 requests, > 255 kv heads or group > 127");
+  attention_work_kernel<<<1, 1024, 0, stream>>>(row_offsets, cache_len, num_trees, group, num_kv_heads, work.order,
+                                                work.items, work.item_capacity, work.num_items, work.counters,
+                                                num_layers);
+  return check_launch("attention_work_kernel");
 }
 
 int launch_tree_meta(const int64_t* row_offsets, const int64_t* parents, const int64_t* position_base,

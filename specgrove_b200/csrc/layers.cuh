@@ -25,8 +25,16 @@ int launch_tree_meta(const int64_t* row_offsets, const int64_t* parents, const i
                      const int64_t* request_ids, int num_trees, int num_rows, RowMeta meta, int32_t* status,
                      cudaStream_t stream);
 
-int launch_attention_order(const int64_t* row_offsets, const int64_t* cache_len, int num_trees, int32_t* order,
-                           cudaStream_t stream);
+// Persistent tree attention work list (built once per pass).
+struct AttentionWork {
+  int32_t* order;       // [R] requests by decreasing K/V length
+  int32_t* items;       // [item_capacity] request << 16 | kv_head << 8 | 128-row block
+  int item_capacity;
+  int32_t* num_items;   // [1]
+  int32_t* counters;    // [num_layers] next item of each layer's attention launch
+};
+int launch_attention_work(const int64_t* row_offsets, const int64_t* cache_len, int num_trees, int group,
+                          int num_kv_heads, AttentionWork work, int num_layers, cudaStream_t stream);
 
 int launch_embed(const int64_t* tokens, const __nv_bfloat16* embed, int64_t vocab, int hidden, int rows,
                  float* x, int32_t* status, cudaStream_t stream);
