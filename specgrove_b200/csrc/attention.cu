@@ -67,6 +67,34 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 64 bits of a 256-bit set held as four 64-bit words, starting at bit pos
+// (0 <= pos < 256; bits past 255 read as 0).  Register selects only, no
+// dynamically indexed (local-memory) array.
+__device__ __forceinline__ uint64_t bits64_at(const uint64_t (&w)[4], int pos) {
+  const int wi = pos >> 6, bo = pos & 63;
+  const uint64_t lo = wi == 0 ? w[0] : wi == 1 ? w[1] : wi == 2 ? w[2] : w[3];
+  const uint64_t hi = wi == 0 ? w[1] : wi == 1 ? w[2] : wi == 2 ? w[3] : 0ull;
+  return bo == 0 ? lo : (lo >> bo) | (hi << (64 - bo));
+}
+
+// Visibility of 64 consecutive keys of one query row: bit e is set when key
+// (kk + e) of the request's tree is visible, where negative indices are the
+// cached prefix (always visible) and tree key t < n is visible when bit t of
+// the row's ancestor-or-self set is.
+__device__ __forceinline__ uint64_t visible64(const uint64_t (&anc)[4], int64_t kk, int n) {
+  uint64_t vis = 0;
+  if (kk < 0) vis = kk <= -64 ? ~0ull : (1ull << static_cast<int>(-kk)) - 1;  // prefix keys
+  const int64_t s0 = kk < 0 ? 0 : kk;                                          // first tree key
+  const int e0 = static_cast<int>(s0 - kk);                                    // its bit
+  if (e0 < 64 && s0 < n) {
+    uint64_t t = bits64_at(anc, static_cast<int>(s0));
+    const int64_t cnt = n - s0;  // tree keys left
+    if (cnt < 64) t &= (1ull << static_cast<int>(cnt)) - 1;
+    vis |= t << e0;
+  }
+  return vis;
+}
+
 __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
@@ -442,7 +470,7 @@ template <int D, int STAGES>
 struct TmLayout {
   static constexpr int BN = 128;                          // keys per tile
   static constexpr int HK = BN / 2;                       // keys per softmax half
-  static constexpr int THREADS = 64 + 256;                // TMA, MMA, 8 softmax warps
+  static constexpr int THREADS = 96 + 256;                // K TMA, MMA, V TMA, 8 softmax warps
   static constexpr int HALVES = D / 64;                   // 64-dim swizzle blocks
   static constexpr uint32_t KV_HALF = BN * 128;           // 128 keys x 64 dims
   static constexpr uint32_t KV_BYTES = HALVES * KV_HALF;  // one K or V tile
@@ -486,9 +514,11 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
   }
   WorkItem* items = reinterpret_cast<WorkItem*>(smem + L::OFF_ITEM);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-  uint64_t* kv_full = bars;               // [STAGES]
-  uint64_t* kv_empty = kv_full + STAGES;  // [STAGES]
-  uint64_t* s_full = kv_empty + STAGES;   // S of a tile written
+  uint64_t* k_full = bars;                // [STAGES] K tile landed
+  uint64_t* k_empty = k_full + STAGES;    // [STAGES] K tile consumed by QK^T
+  uint64_t* v_full = k_empty + STAGES;    // [STAGES] V tile landed
+  uint64_t* v_empty = v_full + STAGES;    // [STAGES] V tile consumed by PV
+  uint64_t* s_full = v_empty + STAGES;    // S of a tile written
   uint64_t* s_free = s_full + 1;          // S read by every softmax thread
   uint64_t* p_full = s_free + 1;          // P (both halves) written
   uint64_t* o_done = p_full + 1;          // PV of a tile complete
@@ -503,8 +533,10 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
     // Per-tile and per-item barriers count every softmax thread.
     mbar_init(s_full, 1);
@@ -515,7 +547,7 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
     for (int i = 0; i < 4; ++i) mbar_init(&merge[i], 64);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&item_full[i], 1);
-      mbar_init(&item_empty[i], 1 + 256);
+      mbar_init(&item_empty[i], 2 + 256);  // MMA thread, V producer, softmax
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -532,6 +564,28 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
   auto give_up = [&]() {
     *abort_flag = 1;
     if (p.status != nullptr) atomicMax(p.status, static_cast<int32_t>(SG_ERR_CUDA));
+  };
+  // Producers: load the item's K (or V) tiles into their ring, tile index gt
+  // onwards (across items).
+  auto load_tiles = [&](const WorkItem& it, int64_t gt, int plane0, uint32_t off_ring, uint64_t* full,
+                        uint64_t* empty) -> bool {
+    const int plane = plane0 + it.kvh;
+    for (int j = 0; j < it.tiles; ++j, ++gt) {
+      const int s = static_cast<int>(gt % STAGES);
+      if (*abort_flag || !mbar_wait(&empty[s], static_cast<uint32_t>((gt / STAGES) & 1) ^ 1u)) {
+        give_up();
+        return false;
+      }
+      mbar_arrive_expect_tx(&full[s], L::KV_BYTES);
+      const int row = it.row0 + j * BN;
+#pragma unroll
+      for (int h = 0; h < L::HALVES; ++h)
+#pragma unroll
+        for (int rb = 0; rb < BN / kKeyTile; ++rb)  // the map's box is kKeyTile rows
+          tma_load_3d(smem + off_ring + s * L::KV_BYTES + h * L::KV_HALF + rb * kKeyTile * 128, &kv_map, h * 64,
+                      row + rb * kKeyTile, plane, &full[s]);
+    }
+    return true;
   };
   // Consumers: wait for work item `seq`, copy it, release the slot.
   auto next_item = [&](int seq, WorkItem& it) -> bool {
@@ -582,27 +636,25 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
         items[seq & 1] = it;
         mbar_arrive(&item_full[seq & 1]);
         if (it.tiles < 0) break;
-        const int plane_k = p.plane_k0 + it.kvh, plane_v = p.plane_v0 + it.kvh;
-        for (int j = 0; j < it.tiles; ++j, ++gt) {
-          const int s = static_cast<int>(gt % STAGES);
-          if (*abort_flag || !mbar_wait(&kv_empty[s], static_cast<uint32_t>((gt / STAGES) & 1) ^ 1u)) {
-            give_up();
-            break;
-          }
-          mbar_arrive_expect_tx(&kv_full[s], 2 * L::KV_BYTES);
-          const int row = it.row0 + j * BN;
-#pragma unroll
-          for (int h = 0; h < L::HALVES; ++h)
-#pragma unroll
-            for (int rb = 0; rb < BN / kKeyTile; ++rb) {  // the map's box is kKeyTile rows
-              const uint32_t off = h * L::KV_HALF + rb * kKeyTile * 128;
-              tma_load_3d(smem + L::OFF_K + s * L::KV_BYTES + off, &kv_map, h * 64, row + rb * kKeyTile, plane_k,
-                          &kv_full[s]);
-              tma_load_3d(smem + L::OFF_V + s * L::KV_BYTES + off, &kv_map, h * 64, row + rb * kKeyTile, plane_v,
-                          &kv_full[s]);
-            }
+        if (!load_tiles(it, gt, p.plane_k0, L::OFF_K, k_full, k_empty)) break;
+        gt += it.tiles;
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ V producer
+    // Follows the published items with its own ring, so K loads never queue
+    // behind a V tile whose slot PV has not released yet.
+    if (lane == 0) {
+      int64_t gt = 0;
+      for (int seq = 0;; ++seq) {
+        WorkItem it;
+        if (!next_item(seq, it)) {
+          give_up();
+          break;
         }
-        if (*abort_flag) break;
+        if (it.tiles < 0) break;
+        if (!load_tiles(it, gt, p.plane_v0, L::OFF_V, v_full, v_empty)) break;
+        gt += it.tiles;
       }
     }
   } else if (warp == 1) {
@@ -628,7 +680,7 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
           const int64_t g = gt + j;
           if (j < it.tiles) {  // S_j = Q K_j^T
             const int s = static_cast<int>(g % STAGES);
-            if (!mbar_wait(&kv_full[s], static_cast<uint32_t>((g / STAGES) & 1)) ||
+            if (!mbar_wait(&k_full[s], static_cast<uint32_t>((g / STAGES) & 1)) ||
                 (g > 0 && !mbar_wait(s_free, static_cast<uint32_t>((g - 1) & 1)))) {
               ok = false;
               break;
@@ -641,15 +693,17 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
               mma_bf16_ta(tmem + L::S_COL, tmem + L::Q_COL + ks * 8, desc_k_sw128(k_addr + koff), idesc_qk,
                           ks > 0 ? 1u : 0u);
             }
+            mma_commit(&k_empty[s]);
             mma_commit(s_full);
           }
           if (j > 0) {  // O_h += P_{j-1,h} V_{j-1,h}
-            if (!mbar_wait(p_full, static_cast<uint32_t>((g - 1) & 1))) {
+            const int s = static_cast<int>((g - 1) % STAGES);
+            if (!mbar_wait(p_full, static_cast<uint32_t>((g - 1) & 1)) ||
+                !mbar_wait(&v_full[s], static_cast<uint32_t>(((g - 1) / STAGES) & 1))) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const int s = static_cast<int>((g - 1) % STAGES);
             const uint32_t v_addr = smem_u32(smem + L::OFF_V + s * L::KV_BYTES);
 #pragma unroll
             for (int ks = 0; ks < HK / 16; ++ks)
@@ -659,7 +713,7 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
                 mma_bf16_ta(tmem + L::O_COL + h * D, tmem + L::P_COL + h * (HK / 2) + ks * 8, bdesc, idesc_pv,
                             (j > 1 || ks > 0) ? 1u : 0u);
               }
-            mma_commit(&kv_empty[s]);
+            mma_commit(&v_empty[s]);
             mma_commit(o_done);
           }
         }
@@ -670,13 +724,13 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
   } else {
     // --------------------------------------------------------------- softmax
     // Warp w serves TMEM lane quarter w % 4 (the lanes it may access) and key
-    // half hf = (w - 2) / 4 of every tile, one 64-key row per thread.  A warp
+    // half hf = (w - 3) / 4 of every tile, one 64-key row per thread.  A warp
     // whose quarter holds no query row of an item still takes every barrier
     // step of every tile (it only skips the work): parity waits are exact
     // only for a waiter at most one phase away from the barrier, so no warp
     // may skip phases and later rejoin.
     const int quarter = warp & 3;
-    const int hf = (warp - 2) >> 2;
+    const int hf = (warp - 3) >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float c2 = p.scale_log2;
@@ -733,10 +787,15 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
         tc_fence_before();
         mbar_arrive(q_full);
       }
-      uint32_t anc[layers::kAncWords];
-      const uint32_t* ap = p.anc + (it.q0 + tok) * layers::kAncWords;
-#pragma unroll
-      for (int w = 0; w < layers::kAncWords; ++w) anc[w] = ap[w];
+      uint64_t anc[4];  // the row's ancestor-or-self set (256 bits)
+      {
+        const uint4* ap = reinterpret_cast<const uint4*>(p.anc + (it.q0 + tok) * layers::kAncWords);
+        const uint4 a = ap[0], b = ap[1];
+        anc[0] = (static_cast<uint64_t>(a.y) << 32) | a.x;
+        anc[1] = (static_cast<uint64_t>(a.w) << 32) | a.z;
+        anc[2] = (static_cast<uint64_t>(b.y) << 32) | b.x;
+        anc[3] = (static_cast<uint64_t>(b.w) << 32) | b.z;
+      }
       float m_run = -INFINITY, l_run = 0.f;
       for (int j = 0; j < tiles; ++j) {
         const int64_t g = gt + j;
@@ -758,16 +817,10 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
         mbar_arrive(s_free);
         const int64_t key0 = static_cast<int64_t>(j) * BN + hf * HK;
         if (key0 + HK > it.lp) {  // this half reaches the tree keys or the end
+          const uint64_t vis = visible64(anc, key0 - it.lp, it.n);
 #pragma unroll
-          for (int e = 0; e < HK; ++e) {
-            const int64_t key = key0 + e;
-            bool vis = true;
-            if (key >= it.lp) {
-              const int k = static_cast<int>(key - it.lp);
-              vis = key < kv_total && ((anc[k >> 5] >> (k & 31)) & 1u);
-            }
-            if (!vis) sv[e] = -INFINITY;
-          }
+          for (int e = 0; e < HK; ++e)
+            if (!((vis >> e) & 1ull)) sv[e] = -INFINITY;
         }
         float mt;
         {  // pairwise max
@@ -827,8 +880,15 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
         if (key0 + HK > kv_total) {
           // Keys past the request's tail come from stale arena rows (possibly
           // NaN bit patterns); P is 0 there, but 0 * NaN is NaN in the MMA,
-          // so zero those rows of this half of the V tile before P is released.
+          // so zero those rows of this half of the V tile (once it has
+          // landed) before P is released.  The V slot's barrier is at most
+          // one phase from this wait: PV of tile g - STAGES completed (o_done
+          // of g - 1) and the slot cannot refill before PV of tile g.
           const int s = static_cast<int>(g % STAGES);
+          if (!mbar_wait(&v_full[s], static_cast<uint32_t>((g / STAGES) & 1))) {
+            ok = false;
+            break;
+          }
           for (int v = r; v < HK; v += 32 * it.active_q) {
             if (key0 + v < kv_total) continue;
             uint8_t* vrow = smem + L::OFF_V + s * L::KV_BYTES + (hf * HK + v) * 128;
