@@ -95,6 +95,13 @@ __device__ __forceinline__ uint64_t visible64(const uint64_t (&anc)[4], int64_t 
   return vis;
 }
 
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
@@ -466,7 +473,7 @@ tree_attention_tc_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
 //
 // TMEM columns (512): O_half0 [0, D), O_half1 [D, 2D), Q [2D, 2.5D) as bf16
 // pairs, P_half0 / P_half1 (32 columns each, bf16 pairs), S (128 fp32).
-template <int D, int STAGES>
+template <int D, int KST, int VST>
 struct TmLayout {
   static constexpr int BN = 128;                          // keys per tile
   static constexpr int HK = BN / 2;                       // keys per softmax half
@@ -474,12 +481,15 @@ struct TmLayout {
   static constexpr int HALVES = D / 64;                   // 64-dim swizzle blocks
   static constexpr uint32_t KV_HALF = BN * 128;           // 128 keys x 64 dims
   static constexpr uint32_t KV_BYTES = HALVES * KV_HALF;  // one K or V tile
-  static constexpr uint32_t OFF_K = 0;
-  static constexpr uint32_t OFF_V = STAGES * KV_BYTES;
-  static constexpr uint32_t OFF_RED = 2 * STAGES * KV_BYTES;  // [2 halves][2: max, sum][128] floats
+  static constexpr uint32_t OFF_K = 0;                    // KST-slot K ring
+  static constexpr uint32_t OFF_V = KST * KV_BYTES;       // VST-slot V ring
+  static constexpr uint32_t OFF_RED = (KST + VST) * KV_BYTES;  // [2 halves][2: max, sum][128] floats
   static constexpr uint32_t OFF_ITEM = OFF_RED + 4 * 128 * 4;  // [2] published work items
   static constexpr uint32_t OFF_BAR = OFF_ITEM + 128;
-  static constexpr size_t SMEM = OFF_BAR + 256;
+  // 2 * (KST + VST) ring barriers + 13 others (8 bytes each), then the TMEM
+  // base address and the abort flag.
+  static constexpr uint32_t BAR_BYTES = (2 * (KST + VST) + 13) * 8 + 8;
+  static constexpr size_t SMEM = OFF_BAR + ((BAR_BYTES + 127) / 128) * 128;
   static constexpr uint32_t O_COL = 0;                    // + half * D
   static constexpr uint32_t Q_COL = 2 * D;
   static constexpr uint32_t P_COL = Q_COL + D / 2;        // + half * HK / 2
@@ -501,10 +511,10 @@ struct WorkItem {
 };
 static_assert(sizeof(WorkItem) <= 64, "work item slot");
 
-template <int D, int STAGES>
-__global__ void __launch_bounds__(TmLayout<D, STAGES>::THREADS, 1)
+template <int D, int KST, int VST>
+__global__ void __launch_bounds__(TmLayout<D, KST, VST>::THREADS, 1)
 tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Params p) {
-  using L = TmLayout<D, STAGES>;
+  using L = TmLayout<D, KST, VST>;
   constexpr int BN = L::BN;
   constexpr int HK = L::HK;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -514,17 +524,18 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
   }
   WorkItem* items = reinterpret_cast<WorkItem*>(smem + L::OFF_ITEM);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-  uint64_t* k_full = bars;                // [STAGES] K tile landed
-  uint64_t* k_empty = k_full + STAGES;    // [STAGES] K tile consumed by QK^T
-  uint64_t* v_full = k_empty + STAGES;    // [STAGES] V tile landed
-  uint64_t* v_empty = v_full + STAGES;    // [STAGES] V tile consumed by PV
-  uint64_t* s_full = v_empty + STAGES;    // S of a tile written
+  uint64_t* k_full = bars;                // [KST] K tile landed
+  uint64_t* k_empty = k_full + KST;       // [KST] K tile consumed by QK^T
+  uint64_t* v_full = k_empty + KST;       // [VST] V tile landed
+  uint64_t* v_empty = v_full + VST;       // [VST] V tile consumed by PV
+  uint64_t* s_full = v_empty + VST;       // S of a tile written
   uint64_t* s_free = s_full + 1;          // S read by every softmax thread
   uint64_t* p_full = s_free + 1;          // P (both halves) written
   uint64_t* o_done = p_full + 1;          // PV of a tile complete
   uint64_t* q_full = o_done + 1;          // Q rows of an item in TMEM
   uint64_t* merge = q_full + 1;           // [4 quarters] per-item (max, sum) exchange
   uint64_t* item_full = merge + 4;        // [2] work item published
+  static_assert(2 * (KST + VST) + 13 == 2 * KST + 2 * VST + 4 + 1 + 4 + 2 + 2, "barrier count");
   uint64_t* item_empty = item_full + 2;   // [2] work item read by every consumer
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -532,9 +543,11 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; ++i) {
+    for (int i = 0; i < KST; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < VST; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
@@ -568,11 +581,11 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
   // Producers: load the item's K (or V) tiles into their ring, tile index gt
   // onwards (across items).
   auto load_tiles = [&](const WorkItem& it, int64_t gt, int plane0, uint32_t off_ring, uint64_t* full,
-                        uint64_t* empty) -> bool {
+                        uint64_t* empty, int stages) -> bool {
     const int plane = plane0 + it.kvh;
     for (int j = 0; j < it.tiles; ++j, ++gt) {
-      const int s = static_cast<int>(gt % STAGES);
-      if (*abort_flag || !mbar_wait(&empty[s], static_cast<uint32_t>((gt / STAGES) & 1) ^ 1u)) {
+      const int s = static_cast<int>(gt % stages);
+      if (*abort_flag || !mbar_wait(&empty[s], static_cast<uint32_t>((gt / stages) & 1) ^ 1u)) {
         give_up();
         return false;
       }
@@ -636,7 +649,7 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
         items[seq & 1] = it;
         mbar_arrive(&item_full[seq & 1]);
         if (it.tiles < 0) break;
-        if (!load_tiles(it, gt, p.plane_k0, L::OFF_K, k_full, k_empty)) break;
+        if (!load_tiles(it, gt, p.plane_k0, L::OFF_K, k_full, k_empty, KST)) break;
         gt += it.tiles;
       }
     }
@@ -653,7 +666,7 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
           break;
         }
         if (it.tiles < 0) break;
-        if (!load_tiles(it, gt, p.plane_v0, L::OFF_V, v_full, v_empty)) break;
+        if (!load_tiles(it, gt, p.plane_v0, L::OFF_V, v_full, v_empty, VST)) break;
         gt += it.tiles;
       }
     }
@@ -679,8 +692,8 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
         for (int j = 0; j <= it.tiles; ++j) {
           const int64_t g = gt + j;
           if (j < it.tiles) {  // S_j = Q K_j^T
-            const int s = static_cast<int>(g % STAGES);
-            if (!mbar_wait(&k_full[s], static_cast<uint32_t>((g / STAGES) & 1)) ||
+            const int s = static_cast<int>(g % KST);
+            if (!mbar_wait(&k_full[s], static_cast<uint32_t>((g / KST) & 1)) ||
                 (g > 0 && !mbar_wait(s_free, static_cast<uint32_t>((g - 1) & 1)))) {
               ok = false;
               break;
@@ -697,9 +710,9 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
             mma_commit(s_full);
           }
           if (j > 0) {  // O_h += P_{j-1,h} V_{j-1,h}
-            const int s = static_cast<int>((g - 1) % STAGES);
+            const int s = static_cast<int>((g - 1) % VST);
             if (!mbar_wait(p_full, static_cast<uint32_t>((g - 1) & 1)) ||
-                !mbar_wait(&v_full[s], static_cast<uint32_t>(((g - 1) / STAGES) & 1))) {
+                !mbar_wait(&v_full[s], static_cast<uint32_t>(((g - 1) / VST) & 1))) {
               ok = false;
               break;
             }
@@ -735,71 +748,108 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float c2 = p.scale_log2;
     float* red = reinterpret_cast<float*>(smem + L::OFF_RED);
-    int64_t gt = 0;
+    int gt = 0;  // tiles consumed so far (across items)
     int merges = 0;  // items this quarter was active in (merge barrier phase)
     bool ok = true;
-    for (int seq = 0; ok; ++seq) {
-      WorkItem it;
-      if (!next_item(seq, it)) {
-        ok = false;
-        break;
+    // Row of the query block this thread serves in item w (token, head).
+    auto row_of = [&](const WorkItem& w, bool& valid, int& tok, int& head) {
+      const int m_row = w.m_base + r;
+      valid = quarter < w.active_q && m_row < w.n * p.group;
+      tok = valid ? m_row / p.group : 0;
+      head = w.kvh * p.group + (valid ? m_row % p.group : 0);
+    };
+    // This thread's half of item w's Q row -> TMEM (two bf16 per column,
+    // 16 columns at a time), then arrive on q_full.  Called for the next item
+    // once S of the current item's last tile has been read, i.e. after the
+    // current item's last QK^T completed, so QK^T of the next item overlaps
+    // the current item's last exponentials, PV and epilogue.  The next item's
+    // first PV, which overwrites O, still waits for every thread's P of that
+    // item, issued only after this thread's epilogue.
+    auto stage_q = [&](const WorkItem& w) {
+      if (quarter < w.active_q) {
+        bool valid;
+        int tok, head;
+        row_of(w, valid, tok, head);
+        constexpr int QW = D / 4;  // columns per thread
+        const uint4* src = reinterpret_cast<const uint4*>(p.q + ((w.q0 + tok) * p.nq + head) * D + hf * (D / 2));
+#pragma unroll
+        for (int ch = 0; ch < QW / 16; ++ch) {
+          uint32_t qw[16];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 v = valid ? src[ch * 4 + c] : make_uint4(0u, 0u, 0u, 0u);
+            qw[4 * c + 0] = v.x;
+            qw[4 * c + 1] = v.y;
+            qw[4 * c + 2] = v.z;
+            qw[4 * c + 3] = v.w;
+          }
+          tmem_st16u(tmem + lane_base + L::Q_COL + hf * QW + ch * 16, qw);
+        }
+        tmem_wait_st();
+        prefetch_l1(p.anc + (w.q0 + tok) * layers::kAncWords);  // read when the item starts
       }
-      if (it.tiles < 0) break;
+      tc_fence_before();
+      mbar_arrive(q_full);
+    };
+    auto load_anc = [&](const WorkItem& w, uint64_t (&a4)[4]) {  // ancestor-or-self set (256 bits)
+      bool valid;
+      int tok, head;
+      row_of(w, valid, tok, head);
+      const uint4* ap = reinterpret_cast<const uint4*>(p.anc + (w.q0 + tok) * layers::kAncWords);
+      const uint4 a = ap[0], b = ap[1];
+      a4[0] = (static_cast<uint64_t>(a.y) << 32) | a.x;
+      a4[1] = (static_cast<uint64_t>(a.w) << 32) | a.z;
+      a4[2] = (static_cast<uint64_t>(b.y) << 32) | b.x;
+      a4[3] = (static_cast<uint64_t>(b.w) << 32) | b.z;
+    };
+    WorkItem it;
+    if (!next_item(0, it)) ok = false;
+    uint64_t anc[4] = {0ull, 0ull, 0ull, 0ull};
+    if (ok && it.tiles >= 0) {
+      stage_q(it);
+      if (quarter < it.active_q) load_anc(it, anc);
+    }
+    for (int seq = 0; ok && it.tiles >= 0; ++seq) {
       const int tiles = it.tiles;
+      // At the item's last tile, once its S has been read: wait for the next
+      // item and stage its Q, reading it in place (its slot is released only
+      // when this item is done, so it cannot be overwritten meanwhile).
+      auto at_last_tile = [&]() -> bool {
+        if (!mbar_wait(&item_full[(seq + 1) & 1], ((seq + 1) >> 1) & 1)) return false;
+        const WorkItem& nx = items[(seq + 1) & 1];
+        if (nx.tiles >= 0) stage_q(nx);
+        return true;
+      };
+      // Move on: copy the next item out of its slot and release the slot.
+      auto advance = [&]() {
+        it = items[(seq + 1) & 1];
+        mbar_arrive(&item_empty[(seq + 1) & 1]);
+        if (it.tiles >= 0 && quarter < it.active_q) load_anc(it, anc);
+      };
       if (quarter >= it.active_q) {
         // Idle quarter: take every barrier step of every tile (no work).
-        tc_fence_before();
-        mbar_arrive(q_full);
         for (int j = 0; j < tiles && ok; ++j) {
-          const int64_t g = gt + j;
-          if (!mbar_wait(s_full, static_cast<uint32_t>(g & 1))) ok = false;
+          const int g = gt + j;
+          if (!mbar_wait(s_full, static_cast<uint32_t>(g) & 1u)) ok = false;
           mbar_arrive(s_free);
-          if (ok && j > 0 && !mbar_wait(o_done, static_cast<uint32_t>((g - 1) & 1))) ok = false;
+          if (ok && j == tiles - 1 && !at_last_tile()) ok = false;
+          if (ok && j > 0 && !mbar_wait(o_done, static_cast<uint32_t>(g - 1) & 1u)) ok = false;
           mbar_arrive(p_full);
         }
-        if (ok && !mbar_wait(o_done, static_cast<uint32_t>((gt + tiles - 1) & 1))) ok = false;
+        if (ok && !mbar_wait(o_done, static_cast<uint32_t>(gt + tiles - 1) & 1u)) ok = false;
         gt += tiles;
+        if (ok) advance();
         continue;
       }
-      const int rows_total = it.n * p.group;
-      const int m_row = it.m_base + r;
-      const bool valid = m_row < rows_total;
-      const int tok = valid ? m_row / p.group : 0;
-      const int head = it.kvh * p.group + (valid ? m_row % p.group : 0);
-      const int64_t kv_total = it.lp + it.n;
-      {  // half of the Q row -> TMEM, two bf16 per column
-        constexpr int QW = D / 4;
-        uint32_t qw[QW];
-        const uint4* src = reinterpret_cast<const uint4*>(p.q + ((it.q0 + tok) * p.nq + head) * D + hf * (D / 2));
-#pragma unroll
-        for (int c = 0; c < QW / 4; ++c) {
-          const uint4 v = valid ? src[c] : make_uint4(0u, 0u, 0u, 0u);
-          qw[4 * c + 0] = v.x;
-          qw[4 * c + 1] = v.y;
-          qw[4 * c + 2] = v.z;
-          qw[4 * c + 3] = v.w;
-        }
-        if constexpr (QW == 32)
-          tmem_st32u(tmem + lane_base + L::Q_COL + hf * QW, qw);
-        else
-          tmem_st16u(tmem + lane_base + L::Q_COL + hf * QW, qw);
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(q_full);
-      }
-      uint64_t anc[4];  // the row's ancestor-or-self set (256 bits)
-      {
-        const uint4* ap = reinterpret_cast<const uint4*>(p.anc + (it.q0 + tok) * layers::kAncWords);
-        const uint4 a = ap[0], b = ap[1];
-        anc[0] = (static_cast<uint64_t>(a.y) << 32) | a.x;
-        anc[1] = (static_cast<uint64_t>(a.w) << 32) | a.z;
-        anc[2] = (static_cast<uint64_t>(b.y) << 32) | b.x;
-        anc[3] = (static_cast<uint64_t>(b.w) << 32) | b.z;
-      }
+      bool valid;
+      int tok, head;
+      row_of(it, valid, tok, head);
+      const int lp = static_cast<int>(it.lp);  // < capacity
+      const int kv_total = lp + it.n;
       float m_run = -INFINITY, l_run = 0.f;
       for (int j = 0; j < tiles; ++j) {
-        const int64_t g = gt + j;
-        if (!mbar_wait(s_full, static_cast<uint32_t>(g & 1))) {
+        const int g = gt + j;
+        if (!mbar_wait(s_full, static_cast<uint32_t>(g) & 1u)) {
           ok = false;
           break;
         }
@@ -815,23 +865,28 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
         }
         tc_fence_before();
         mbar_arrive(s_free);
-        const int64_t key0 = static_cast<int64_t>(j) * BN + hf * HK;
-        if (key0 + HK > it.lp) {  // this half reaches the tree keys or the end
-          const uint64_t vis = visible64(anc, key0 - it.lp, it.n);
+        if (j == tiles - 1 && !at_last_tile()) {
+          ok = false;
+          break;
+        }
+        const int key0 = j * BN + hf * HK;
+        if (key0 + HK > lp) {  // this half reaches the tree keys or the end
+          const uint64_t vis = visible64(anc, key0 - lp, it.n);
 #pragma unroll
           for (int e = 0; e < HK; ++e)
             if (!((vis >> e) & 1ull)) sv[e] = -INFINITY;
         }
         float mt;
-        {  // pairwise max
-          float t[HK / 2];
+        {  // row max of the 64 scores: three-input max tree (64 -> 22 -> 8 -> 3 -> 1)
+          float t[22];
 #pragma unroll
-          for (int e = 0; e < HK / 2; ++e) t[e] = fmaxf(sv[2 * e], sv[2 * e + 1]);
+          for (int e = 0; e < 21; ++e) t[e] = fmax3f(sv[3 * e], sv[3 * e + 1], sv[3 * e + 2]);
+          t[21] = sv[63];
+          float u[8];
 #pragma unroll
-          for (int w = HK / 4; w >= 1; w >>= 1)
-#pragma unroll
-            for (int e = 0; e < w; ++e) t[e] = fmaxf(t[e], t[e + w]);
-          mt = t[0] * c2;
+          for (int e = 0; e < 7; ++e) u[e] = fmax3f(t[3 * e], t[3 * e + 1], t[3 * e + 2]);
+          u[7] = t[21];
+          mt = fmax3f(fmax3f(u[0], u[1], u[2]), fmax3f(u[3], u[4], u[5]), fmaxf(u[6], u[7])) * c2;
         }
         // Lazy rescaling: move the reference max only when the tile max
         // exceeds it by more than 2^8 (the first tile always sets it).
@@ -860,7 +915,7 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
         }
         l_run = l_run * alpha + (((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7])));
         // P and this half's O accumulator were last used by PV of tile g-1
-        if (j > 0 && !mbar_wait(o_done, static_cast<uint32_t>((g - 1) & 1))) {
+        if (j > 0 && !mbar_wait(o_done, static_cast<uint32_t>(g - 1) & 1u)) {
           ok = false;
           break;
         }
@@ -882,10 +937,10 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
           // NaN bit patterns); P is 0 there, but 0 * NaN is NaN in the MMA,
           // so zero those rows of this half of the V tile (once it has
           // landed) before P is released.  The V slot's barrier is at most
-          // one phase from this wait: PV of tile g - STAGES completed (o_done
+          // one phase from this wait: PV of tile g - VST completed (o_done
           // of g - 1) and the slot cannot refill before PV of tile g.
-          const int s = static_cast<int>(g % STAGES);
-          if (!mbar_wait(&v_full[s], static_cast<uint32_t>((g / STAGES) & 1))) {
+          const int s = g % VST;
+          if (!mbar_wait(&v_full[s], static_cast<uint32_t>(g / VST) & 1u)) {
             ok = false;
             break;
           }
@@ -903,7 +958,7 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
         tc_fence_before();
         mbar_arrive(p_full);
       }
-      if (ok && !mbar_wait(o_done, static_cast<uint32_t>((gt + tiles - 1) & 1))) ok = false;
+      if (ok && !mbar_wait(o_done, static_cast<uint32_t>(gt + tiles - 1) & 1u)) ok = false;
       if (!ok) break;
       // Merge the two halves' (max, sum, O): each warp writes out half of the
       // O columns.  The next item's first PV overwrites O only after every
@@ -949,6 +1004,7 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
         }
       }
       gt += tiles;
+      advance();
     }
     if (!ok) give_up();
   }
@@ -975,10 +1031,10 @@ int launch_cfg(const CUtensorMap& map, const Params& p, dim3 grid, cudaStream_t 
   return launch_pdl("tree_attention_tc_kernel", kernel, grid, dim3(L::THREADS), L::SMEM, stream, map, p);
 }
 
-template <int D, int STAGES>
+template <int D, int KST, int VST>
 int launch_tm(const CUtensorMap& map, const Params& p, int num_requests, cudaStream_t stream) {
-  using L = TmLayout<D, STAGES>;
-  auto kernel = tree_attention_tm_kernel<D, STAGES>;
+  using L = TmLayout<D, KST, VST>;
+  auto kernel = tree_attention_tm_kernel<D, KST, VST>;
   static int configured = 0;
   int dev = 0;
   SG_CUDA_CHECK(cudaGetDevice(&dev));
@@ -1018,10 +1074,10 @@ int launch(const CUtensorMap& kv_map, const Params& p, int num_requests, int max
   }();
   if (impl >= 5) {
     if (head_dim == 128) {
-      if (impl == 5) return launch_tm<128, 2>(kv_map, p, num_requests, stream);
-      return launch_tm<128, 3>(kv_map, p, num_requests, stream);
+      if (impl == 5) return launch_tm<128, 3, 3>(kv_map, p, num_requests, stream);
+      return launch_tm<128, 4, 3>(kv_map, p, num_requests, stream);
     }
-    if (head_dim == 64) return launch_tm<64, 4>(kv_map, p, num_requests, stream);
+    if (head_dim == 64) return launch_tm<64, 6, 6>(kv_map, p, num_requests, stream);
   }
   if (head_dim == 128) {
     if (split == 1) return launch_cfg<128, kKeyTile, 4, 1>(kv_map, p, grid, stream);
