@@ -23,7 +23,6 @@ struct Params {
   const uint32_t* anc;       // [Q][kAncWords]
   int nq, nkv, group;
   int plane_k0, plane_v0;    // arena plane of kv head 0's K and V for this layer
-  const int32_t* order;      // [R] requests in launch order (longest first), or null
   const int32_t* items;      // persistent kernel: request << 16 | kv_head << 8 | 128-row block
   const int32_t* num_items;  // [1]
   int32_t* work_counter;     // next item; zero before the launch
@@ -31,7 +30,7 @@ struct Params {
   int32_t* status;
 };
 
-// Keys per K/V tile of the tree attention (and rows of the kv_map box).
+// Rows of the kv_map TMA box (a 128-key tile is loaded as two boxes).
 constexpr int kKeyTile = 64;
 
 // kv_map: 3-D TMA map over the whole arena (head_dim, plane rows, planes),

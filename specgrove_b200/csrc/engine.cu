@@ -313,7 +313,6 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
     ap.group = nq / nkv;
     ap.plane_k0 = l * 2 * nkv;
     ap.plane_v0 = l * 2 * nkv + nkv;
-    ap.order = e->meta.order;
     ap.items = e->work.items;
     ap.num_items = e->work.num_items;
     ap.work_counter = e->work.counters + l;
