@@ -173,6 +173,23 @@ SG_API int sg_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb,
                  int32_t epilogue, void* aux, int64_t ld_aux, int32_t* status,
                  void* stream);
 
+/*
+ * sg_gemm_bf16 with a stream-K workspace for the wave tail (no counterpart in
+ * the reference): when the tiles do not fill whole waves of one CTA per SM,
+ * the k-blocks of the last partial wave are split over all SMs and combined
+ * through fp32 partial accumulators in `workspace` (deterministic order).
+ * workspace_bytes >= sg_gemm_split_workspace_bytes(); its flag area must be
+ * zero before the first call (sg_gemm_split_workspace_init), and calls sharing
+ * a workspace must be ordered (one stream).  A null workspace or a smaller
+ * size runs sg_gemm_bf16 unchanged.
+ */
+SG_API size_t sg_gemm_split_workspace_bytes(void);
+SG_API int sg_gemm_split_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+SG_API int sg_gemm_bf16_ws(const void* A, int64_t lda, const void* B, int64_t ldb,
+                    void* C, int64_t ldc, int32_t M, int32_t N, int32_t K,
+                    int32_t epilogue, void* aux, int64_t ld_aux, int32_t* status,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------
  * The packed tree-verification pass (Qwen3 decoder shape).
  * ------------------------------------------------------------------------ */

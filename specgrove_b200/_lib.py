@@ -44,6 +44,11 @@ _SIGNATURES = {
     "sg_gemm_bf16": (ctypes.c_int, [
         c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_int32, c_int32,
         c_void_p, c_int64, c_void_p, c_void_p]),
+    "sg_gemm_split_workspace_bytes": (ctypes.c_size_t, []),
+    "sg_gemm_split_workspace_init": (ctypes.c_int, [c_void_p, ctypes.c_size_t, c_void_p]),
+    "sg_gemm_bf16_ws": (ctypes.c_int, [
+        c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_int32, c_int32,
+        c_void_p, c_int64, c_void_p, c_void_p, ctypes.c_size_t, c_void_p]),
     "sg_lm_head_sample_static": (ctypes.c_int, [
         c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, ctypes.c_float, c_void_p, c_void_p, c_uint64,
         ctypes.c_float, c_void_p, c_void_p, c_void_p]),

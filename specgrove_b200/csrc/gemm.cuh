@@ -10,6 +10,16 @@
 //               next tile's MMAs overlap this tile's epilogue.
 // Tiles are visited n-major (all M tiles of a weight panel back to back) so a
 // weight panel is read from HBM once and served from L2 to the other M tiles.
+//
+// Wave tail (stream-K): with T tiles on P CTAs, the T mod P tiles left after
+// the last full wave would leave SMs idle for a whole tile.  Their k-blocks
+// are instead split evenly over the CTAs, each taking one contiguous run of
+// (tile, k-block) iterations.  The CTA whose run holds a tile's first k-block
+// owns it: the other CTAs on that tile (at most two) write fp32 partial
+// accumulators to a workspace and count themselves done on a flag; the owner
+// adds the partials in k order (a fixed order, so results are reproducible),
+// then runs the fused epilogue and resets the flags.  All CTAs of the grid
+// (one per SM) are resident together, and every flag wait is bounded.
 #pragma once
 
 #include "sm100.cuh"
@@ -30,9 +40,20 @@ constexpr int BARRIER_BYTES = 256;
 constexpr size_t SMEM_BYTES = static_cast<size_t>(STAGES) * STAGE_BYTES + 1024 + BARRIER_BYTES;
 constexpr uint32_t IDESC = sm100::idesc_bf16_f32(BM, BN);
 
+// Stream-K plan for the tiles after the last full wave (sk_ctas == 0: none).
+struct Split {
+  int t_dp;         // tiles [0, t_dp) run whole, round-robin over the grid
+  int sk_ctas;      // CTAs [0, sk_ctas) share the k-blocks of tiles [t_dp, tiles)
+  int per, rem;     // CTA c takes per (+1 when c < rem) consecutive iterations
+  int max_slots;    // partial buffers per split tile (contributors per tile)
+  float* partials;  // [split tile][slot][BN / 4][BM] float4: column quad-major, rows contiguous
+  int* flags;       // [split tile][slot]: 128 once the contributor's threads are done
+};
+
 struct Shape {
   int M, N, K;
   int m_tiles, n_tiles, k_blocks, tiles;
+  Split sp;
 };
 
 inline Shape make_shape(int M, int N, int K) {
@@ -44,13 +65,98 @@ inline Shape make_shape(int M, int N, int K) {
   s.n_tiles = (N + BN - 1) / BN;
   s.k_blocks = K / BK;
   s.tiles = s.m_tiles * s.n_tiles;
+  s.sp = Split{s.tiles, 0, 0, 0, 0, nullptr, nullptr};
   return s;
+}
+
+// Workspace of the stream-K tail: partial accumulators and flags.  Flags
+// must be zero before the first launch (each launch leaves them zero).
+struct SplitWorkspace {
+  float* partials;
+  int* flags;
+  size_t partial_tiles;  // capacity in (tile, slot) partial buffers
+};
+
+constexpr int kMaxSlots = 2;  // contributors per split tile (each run >= half a tile)
+
+// Worst-case (tile, slot) buffers any shape needs on `sms` CTAs.
+inline size_t split_partial_tiles(int sms) { return static_cast<size_t>(sms) * kMaxSlots; }
+inline size_t split_partial_bytes(int sms) { return split_partial_tiles(sms) * BM * BN * sizeof(float); }
+
+// Plan the tail split of `s` on `sms` CTAs; leaves s.sp without a split when
+// it would not help or the workspace is missing.
+inline void plan_split(Shape& s, int sms, const SplitWorkspace* ws) {
+  s.sp = Split{s.tiles, 0, 0, 0, 0, nullptr, nullptr};
+  if (ws == nullptr || ws->partials == nullptr || ws->flags == nullptr || sms <= 0 || s.k_blocks < 2) return;
+  const int tail = s.tiles % sms;  // all tiles when there is no full wave
+  if (tail == 0) return;
+  const int64_t iters = static_cast<int64_t>(tail) * s.k_blocks;
+  const int min_run = (s.k_blocks + 1) / 2;  // keeps contributors per tile <= 2
+  const int ctas = static_cast<int>(min64(sms, iters / min_run));
+  if (ctas <= tail) return;  // no more CTAs than tiles: nothing to gain
+  if (static_cast<size_t>(tail) * kMaxSlots > ws->partial_tiles) return;
+  s.sp.t_dp = s.tiles - tail;
+  s.sp.sk_ctas = ctas;
+  s.sp.per = static_cast<int>(iters / ctas);
+  s.sp.rem = static_cast<int>(iters % ctas);
+  s.sp.max_slots = kMaxSlots;
+  s.sp.partials = ws->partials;
+  s.sp.flags = ws->flags;
 }
 
 __device__ __forceinline__ void tile_coords(const Shape& s, int tile, int& m0, int& n0) {
   m0 = (tile % s.m_tiles) * BM;
   n0 = (tile / s.m_tiles) * BN;
 }
+
+// One unit of a CTA's work: k-blocks [kb0, kb1) of a tile.
+enum SegKind { kSegWhole = 0, kSegOwner = 1, kSegContrib = 2 };
+struct Seg {
+  int tile, kb0, kb1, kind;
+  int slot;      // contributor: its partial buffer
+  int ncontrib;  // owner: partial buffers to add (slots 0 .. ncontrib-1)
+};
+
+// Walks this CTA's segments: whole tiles blockIdx.x, +gridDim.x, ... below
+// t_dp, then its run of tail iterations.  Every warp role walks the same list.
+struct SegIter {
+  int dp_next, it, end;
+  __device__ void begin(const Shape& s) {
+    dp_next = static_cast<int>(blockIdx.x);
+    const int c = static_cast<int>(blockIdx.x);
+    if (c < s.sp.sk_ctas) {
+      it = c * s.sp.per + min(c, s.sp.rem);
+      end = it + s.sp.per + (c < s.sp.rem ? 1 : 0);
+    } else {
+      it = end = 0;
+    }
+  }
+  __device__ static int cta_of(const Split& sp, int i) {  // CTA whose run holds tail iteration i
+    const int big = sp.rem * (sp.per + 1);
+    return i < big ? i / (sp.per + 1) : sp.rem + (i - big) / sp.per;
+  }
+  __device__ bool next(const Shape& s, Seg& g) {
+    if (dp_next < s.sp.t_dp) {
+      g = Seg{dp_next, 0, s.k_blocks, kSegWhole, 0, 0};
+      dp_next += static_cast<int>(gridDim.x);
+      return true;
+    }
+    if (it >= end) return false;
+    const int K = s.k_blocks;
+    const int ti = it / K, kb0 = it % K;
+    const int kb1 = min(K, kb0 + (end - it));
+    g = Seg{s.sp.t_dp + ti, kb0, kb1, kSegWhole, 0, 0};
+    if (kb0 == 0 && kb1 < K) {
+      g.kind = kSegOwner;
+      g.ncontrib = cta_of(s.sp, ti * K + K - 1) - static_cast<int>(blockIdx.x);
+    } else if (kb0 > 0) {
+      g.kind = kSegContrib;
+      g.slot = static_cast<int>(blockIdx.x) - cta_of(s.sp, ti * K) - 1;
+    }
+    it += kb1 - kb0;
+    return true;
+  }
+};
 
 // Epi must provide:
 //   struct Params;  (int32_t* status member)
@@ -107,10 +213,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < shape.tiles && !*abort_flag; tile += gridDim.x) {
+      SegIter si;
+      si.begin(shape);
+      Seg g;
+      while (!*abort_flag && si.next(shape, g)) {
         int m0, n0;
-        tile_coords(shape, tile, m0, n0);
-        for (int kb = 0; kb < shape.k_blocks; ++kb) {
+        tile_coords(shape, g.tile, m0, n0);
+        for (int kb = g.kb0; kb < g.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u)) {
             fail_wait();
             break;
@@ -131,7 +240,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int tile = blockIdx.x; tile < shape.tiles && !*abort_flag; tile += gridDim.x) {
+      SegIter si;
+      si.begin(shape);
+      Seg g;
+      while (!*abort_flag && si.next(shape, g)) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u)) {
           fail_wait();
           break;
@@ -139,7 +251,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
         bool ok = true;
-        for (int kb = 0; kb < shape.k_blocks; ++kb) {
+        for (int kb = g.kb0; kb < g.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase)) {
             fail_wait();
             ok = false;
@@ -151,7 +263,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             mma_bf16(d, desc_k_sw128(a_base + k * 32), desc_k_sw128(b_base + k * 32), IDESC,
-                     (kb | k) != 0 ? 1u : 0u);
+                     ((kb - g.kb0) | k) != 0 ? 1u : 0u);
           mma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -166,9 +278,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
     }
   } else {
     const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int r = quarter * 32 + lane;  // row within the tile
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < shape.tiles; tile += gridDim.x) {
+    SegIter si;
+    si.begin(shape);
+    Seg g;
+    while (si.next(shape, g)) {
       if (*abort_flag) break;
       if (!mbar_wait(&tfull[acc], acc_phase)) {
         fail_wait();
@@ -176,10 +292,74 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       }
       tc_fence_after();
       int m0, n0;
-      tile_coords(shape, tile, m0, n0);
+      tile_coords(shape, g.tile, m0, n0);
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      Epi::apply(ep, shape, taddr, m0 + quarter * 32 + lane, m0, n0, quarter, lane);
+      const Split& sp = shape.sp;
+      const int sk_tile = g.tile - sp.t_dp;
+      if (g.kind == kSegContrib) {
+        // Partial accumulator -> workspace (L2), then count this thread done.
+        const int fi = sk_tile * sp.max_slots + g.slot;
+        float* dst = sp.partials + static_cast<size_t>(fi) * (BM * BN);
+        // float4 of column quad j of row r at [j][r]: a warp's store is 512
+        // contiguous bytes.
+        float4* d4 = reinterpret_cast<float4*>(dst) + r;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(taddr + c * 32, v);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            __stcg(d4 + (c * 8 + q) * BM, make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]));
+        }
+        __threadfence();
+        atomicAdd(&sp.flags[fi], 1);
+      } else {
+        if (g.kind == kSegOwner) {
+          // Wait for the contributors' partials (each flag counts 128 threads).
+          bool ready = true;
+          for (int slot = 0; slot < g.ncontrib && ready; ++slot) {
+            const volatile int* f = sp.flags + sk_tile * sp.max_slots + slot;
+            uint32_t i = 0;
+            while (*f < 128 && ++i < kWaitLimit) __nanosleep(32);
+            ready = *f >= 128;
+          }
+          if (!ready) {
+            fail_wait();
+            break;
+          }
+          __threadfence();
+          // acc += partials in k order, written back to TMEM for the epilogue.
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            float v[32];
+            tmem_ld32(taddr + c * 32, v);
+            for (int slot = 0; slot < g.ncontrib; ++slot) {
+              const float4* src = reinterpret_cast<const float4*>(
+                                      sp.partials + static_cast<size_t>(sk_tile * sp.max_slots + slot) * (BM * BN)) +
+                                  r;
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const float4 pq = __ldcg(src + (c * 8 + q) * BM);
+                v[q * 4] += pq.x;
+                v[q * 4 + 1] += pq.y;
+                v[q * 4 + 2] += pq.z;
+                v[q * 4 + 3] += pq.w;
+              }
+            }
+            tmem_st32(taddr + c * 32, v);
+          }
+          tmem_wait_st();
+          // Each owner thread counts itself past the flag (128 -> 256); the
+          // last one resets it to 0 for the next launch, so no owner thread
+          // still polling can see it drop below 128.
+          for (int slot = 0; slot < g.ncontrib; ++slot) {
+            int* f = &sp.flags[sk_tile * sp.max_slots + slot];
+            if (atomicAdd(f, 1) == 255) atomicExch(f, 0);
+          }
+        }
+        Epi::apply(ep, shape, taddr, m0 + r, m0, n0, quarter, lane);
+      }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       acc ^= 1;
@@ -409,8 +589,8 @@ struct EpiLmHead {
 
 // Host launcher: persistent grid of min(tiles, SMs) CTAs.
 template <class Epi>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Shape& shape, const typename Epi::Params& ep,
-           cudaStream_t stream) {
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Shape& shape_in, const typename Epi::Params& ep,
+           cudaStream_t stream, const SplitWorkspace* split = nullptr) {
   static int configured_device_mask = 0;
   int dev = 0;
   SG_CUDA_CHECK(cudaGetDevice(&dev));
@@ -420,7 +600,10 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Shape& shape, con
     configured_device_mask |= (1 << dev);
   }
   const int sms = device_sm_count();
-  const int grid = shape.tiles < sms ? shape.tiles : sms;
+  Shape shape = shape_in;
+  plan_split(shape, sms, split);
+  int grid = shape.tiles < sms ? shape.tiles : sms;
+  if (shape.sp.sk_ctas > grid) grid = shape.sp.sk_ctas;
   if (grid <= 0) return SG_OK;
   return launch_pdl("gemm_kernel", gemm_kernel<Epi>, dim3(grid), dim3(THREADS), SMEM_BYTES, stream, ta, tb, shape,
                     ep);
