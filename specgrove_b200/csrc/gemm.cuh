@@ -37,7 +37,9 @@ constexpr int STAGE_BYTES = A_TILE + B_TILE;
 constexpr int THREADS = 192;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int BARRIER_BYTES = 256;
-constexpr size_t SMEM_BYTES = static_cast<size_t>(STAGES) * STAGE_BYTES + 1024 + BARRIER_BYTES;
+constexpr int EPI_STAGE_BYTES = 32 * 8 * 16;  // per epilogue warp: 32 rows x 8 x 16 B
+constexpr size_t SMEM_BYTES =
+    static_cast<size_t>(STAGES) * STAGE_BYTES + 1024 + BARRIER_BYTES + 4 * EPI_STAGE_BYTES;
 constexpr uint32_t IDESC = sm100::idesc_bf16_f32(BM, BN);
 
 // Stream-K plan for the tiles after the last full wave (sk_ctas == 0: none).
@@ -161,7 +163,8 @@ struct SegIter {
 // Epi must provide:
 //   struct Params;  (int32_t* status member)
 //   static __device__ void apply(const Params&, const Shape&, uint32_t taddr,
-//                                int row, int m0, int n0, int quarter, int lane);
+//                                int m0, int n0, int quarter, int lane,
+//                                uint4* stage);  // the warp's staging slice
 template <class Epi>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
@@ -172,6 +175,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_TILE;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint4* epi_stage = reinterpret_cast<uint4*>(smem + STAGES * STAGE_BYTES + BARRIER_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tfull = bars + 2 * STAGES;
@@ -358,7 +362,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
             if (atomicAdd(f, 1) == 255) atomicExch(f, 0);
           }
         }
-        Epi::apply(ep, shape, taddr, m0 + r, m0, n0, quarter, lane);
+        Epi::apply(ep, shape, taddr, m0, n0, quarter, lane, epi_stage + (warp - 2) * (EPI_STAGE_BYTES / 16));
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -375,6 +379,40 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
 }
 
 // --------------------------------------------------------------- epilogues
+//
+// Epilogue warps read TMEM one row per thread (tcgen05.ld 32x32b).  Writing
+// rows straight to row-major memory would make every warp instruction touch
+// 32 different rows; instead each warp stages 32 rows x 128 bytes in its own
+// shared-memory slice (16-byte units XOR-swizzled by row, conflict-free) and
+// reads it back transposed, so 8 lanes cover one row's 128-byte line and a
+// warp instruction moves 4 whole lines.
+
+// Row `lane`'s 16-byte unit q -> stage; unit q of row `row` <- stage.
+__device__ __forceinline__ void stage_put(uint4* st, int lane, int q, uint4 v) { st[lane * 8 + (q ^ (lane & 7))] = v; }
+__device__ __forceinline__ uint4 stage_get(const uint4* st, int row, int q) { return st[row * 8 + (q ^ (row & 7))]; }
+
+__device__ __forceinline__ uint4 f4_as_u4(float a, float b, float c, float d) {
+  return make_uint4(__float_as_uint(a), __float_as_uint(b), __float_as_uint(c), __float_as_uint(d));
+}
+
+// Stage 64 bf16 per row (8 x 16 B) and store them row-major: out + row * ld
+// + col0, columns [col0, col0 + valid) of rows [row0, row0 + 32) below M.
+__device__ __forceinline__ void store_bf16_rows(uint4* st, int lane, const uint32_t (&w)[32], __nv_bfloat16* out,
+                                                int64_t ld, int row0, int M, int col0, int valid) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) stage_put(st, lane, q, make_uint4(w[q * 4], w[q * 4 + 1], w[q * 4 + 2], w[q * 4 + 3]));
+  __syncwarp();
+  const int q = lane & 7;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int rr = i * 4 + (lane >> 3);
+    const int row = row0 + rr;
+    const uint4 v = stage_get(st, rr, q);
+    if (row < M && q * 8 < valid)
+      *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * ld + col0 + q * 8) = v;
+  }
+  __syncwarp();
+}
 
 // C (bf16, row stride ldc) = acc
 struct EpiStoreBf16 {
@@ -383,26 +421,20 @@ struct EpiStoreBf16 {
     int64_t ldo;
     int32_t* status;
   };
-  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int row, int,
-                                               int n0, int, int) {
+  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int m0, int n0,
+                                               int quarter, int lane, uint4* st) {
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      const int col = n0 + c * 32;
+    for (int c = 0; c < BN / 64; ++c) {
+      const int col = n0 + c * 64;
       if (col >= s.N) break;
-      float v[32];
-      sm100::tmem_ld32(taddr + c * 32, v);
-      if (row < s.M) {
-        uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(row) * p.ldo + col);
+      float v[64];
+      sm100::tmem_ld32_nowait(taddr + c * 64, reinterpret_cast<uint32_t*>(v));
+      sm100::tmem_ld32_nowait(taddr + c * 64 + 32, reinterpret_cast<uint32_t*>(v) + 32);
+      sm100::tmem_wait_ld();
+      uint32_t w[32];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 w;
-          w.x = sm100::pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-          w.y = sm100::pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-          w.z = sm100::pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-          w.w = sm100::pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
-          dst[q] = w;
-        }
-      }
+      for (int e = 0; e < 32; ++e) w[e] = sm100::pack_bf16x2(v[2 * e], v[2 * e + 1]);
+      store_bf16_rows(st, lane, w, p.out, p.ldo, m0 + quarter * 32, s.M, col, s.N - col);
     }
   }
 };
@@ -414,19 +446,28 @@ struct EpiStoreF32 {
     int64_t ldo;
     int32_t* status;
   };
-  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int row, int,
-                                               int n0, int, int) {
+  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int m0, int n0,
+                                               int quarter, int lane, uint4* st) {
+    const int row0 = m0 + quarter * 32;
+    const int q = lane & 7;
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       const int col = n0 + c * 32;
       if (col >= s.N) break;
       float v[32];
       sm100::tmem_ld32(taddr + c * 32, v);
-      if (row < s.M) {
-        float4* dst = reinterpret_cast<float4*>(p.out + static_cast<int64_t>(row) * p.ldo + col);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) dst[q] = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+      for (int k = 0; k < 8; ++k) stage_put(st, lane, k, f4_as_u4(v[k * 4], v[k * 4 + 1], v[k * 4 + 2], v[k * 4 + 3]));
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int rr = i * 4 + (lane >> 3);
+        const int row = row0 + rr;
+        const uint4 u = stage_get(st, rr, q);
+        if (row < s.M)
+          *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(row) * p.ldo + col + q * 4) = u;
       }
+      __syncwarp();
     }
   }
 };
@@ -440,42 +481,46 @@ struct EpiResidual {
     int64_t ldb;
     int32_t* status;
   };
-  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int row, int,
-                                               int n0, int, int) {
+  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int m0, int n0,
+                                               int quarter, int lane, uint4* st) {
+    const int row0 = m0 + quarter * 32;
+    const int q = lane & 7;
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       const int col = n0 + c * 32;
       if (col >= s.N) break;
       float v[32];
       sm100::tmem_ld32(taddr + c * 32, v);
-      if (row < s.M) {
-        float4* xr = reinterpret_cast<float4*>(p.x + static_cast<int64_t>(row) * p.ldx + col);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float4 x = xr[q];
-          x.x += v[q * 4];
-          x.y += v[q * 4 + 1];
-          x.z += v[q * 4 + 2];
-          x.w += v[q * 4 + 3];
-          xr[q] = x;
-          v[q * 4] = x.x;
-          v[q * 4 + 1] = x.y;
-          v[q * 4 + 2] = x.z;
-          v[q * 4 + 3] = x.w;
-        }
-        if (p.x_bf16 != nullptr) {
-          uint4* dst = reinterpret_cast<uint4*>(p.x_bf16 + static_cast<int64_t>(row) * p.ldb + col);
+      for (int k = 0; k < 8; ++k) stage_put(st, lane, k, f4_as_u4(v[k * 4], v[k * 4 + 1], v[k * 4 + 2], v[k * 4 + 3]));
+      __syncwarp();
+      // Lane (i, lane / 8, q) handles 4 columns of row i * 4 + lane / 8: the
+      // x loads of all 8 passes go out first, then the adds and stores.
+      float4 xv[8];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 w;
-            w.x = sm100::pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-            w.y = sm100::pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-            w.z = sm100::pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-            w.w = sm100::pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
-            dst[q] = w;
-          }
+      for (int i = 0; i < 8; ++i) {
+        const int row = row0 + i * 4 + (lane >> 3);
+        xv[i] = row < s.M ? *reinterpret_cast<const float4*>(p.x + static_cast<int64_t>(row) * p.ldx + col + q * 4)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int rr = i * 4 + (lane >> 3);
+        const int row = row0 + rr;
+        const uint4 a = stage_get(st, rr, q);
+        float4 x = xv[i];
+        x.x += __uint_as_float(a.x);
+        x.y += __uint_as_float(a.y);
+        x.z += __uint_as_float(a.z);
+        x.w += __uint_as_float(a.w);
+        if (row < s.M) {
+          *reinterpret_cast<float4*>(p.x + static_cast<int64_t>(row) * p.ldx + col + q * 4) = x;
+          if (p.x_bf16 != nullptr)
+            *reinterpret_cast<uint2*>(p.x_bf16 + static_cast<int64_t>(row) * p.ldb + col + q * 4) =
+                make_uint2(sm100::pack_bf16x2(x.x, x.y), sm100::pack_bf16x2(x.z, x.w));
         }
       }
+      __syncwarp();
     }
   }
 };
@@ -489,32 +534,26 @@ struct EpiSwiGlu {
     int64_t ldo;
     int32_t* status;
   };
-  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int row, int,
-                                               int n0, int, int) {
+  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int m0, int n0,
+                                               int quarter, int lane, uint4* st) {
+    if (n0 >= s.N) return;
 #pragma unroll 1
-    for (int c = 0; c < BN / 64; ++c) {
-      float g[32], u[32];
-      sm100::tmem_ld32(taddr + c * 32, g);
-      sm100::tmem_ld32(taddr + BN / 2 + c * 32, u);
-      const int col = n0 / 2 + c * 32;
-      if (row < s.M && n0 < s.N) {
-        uint4* dst = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(row) * p.ldo + col);
+    for (int c = 0; c < BN / 128; ++c) {  // 64 output columns per pass
+      uint32_t w[32];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float h[8];
+      for (int h = 0; h < 2; ++h) {
+        float g[32], u[32];
+        sm100::tmem_ld32_nowait(taddr + c * 64 + h * 32, reinterpret_cast<uint32_t*>(g));
+        sm100::tmem_ld32_nowait(taddr + BN / 2 + c * 64 + h * 32, reinterpret_cast<uint32_t*>(u));
+        sm100::tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float gv = g[q * 8 + e];
-            h[e] = gv / (1.0f + __expf(-gv)) * u[q * 8 + e];
-          }
-          uint4 w;
-          w.x = sm100::pack_bf16x2(h[0], h[1]);
-          w.y = sm100::pack_bf16x2(h[2], h[3]);
-          w.z = sm100::pack_bf16x2(h[4], h[5]);
-          w.w = sm100::pack_bf16x2(h[6], h[7]);
-          dst[q] = w;
+        for (int e = 0; e < 16; ++e) {
+          const float g0 = g[2 * e], g1 = g[2 * e + 1];
+          w[h * 16 + e] = sm100::pack_bf16x2(g0 / (1.0f + __expf(-g0)) * u[2 * e],
+                                             g1 / (1.0f + __expf(-g1)) * u[2 * e + 1]);
         }
       }
+      store_bf16_rows(st, lane, w, p.out, p.ldo, m0 + quarter * 32, s.M, n0 / 2 + c * 64, 64);
     }
   }
 };
@@ -538,8 +577,9 @@ struct EpiLmHead {
     float inv_temp;
     int32_t* status;
   };
-  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int row, int,
-                                               int n0, int, int) {
+  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int m0, int n0,
+                                               int quarter, int lane, uint4*) {
+    const int row = m0 + quarter * 32 + lane;
     const bool rv = row < s.M;
     const uint32_t node = rv ? static_cast<uint32_t>(p.row_local[row]) : 0u;
     const uint64_t req = rv ? static_cast<uint64_t>(p.row_request[row]) : 0ull;
