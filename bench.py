@@ -57,24 +57,51 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device_index: int):
-        self.device_index = device_index
+        self.gpu_id = self._smi_id(device_index)
         self.proc = None
         self.path = None
+
+    @staticmethod
+    def _smi_id(device_index: int) -> str:
+        """nvidia-smi --id for a torch device: its UUID (immune to
+        CUDA_VISIBLE_DEVICES remapping), else the visible-device mapping."""
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [v.strip() for v in visible.split(",") if v.strip()]
+        fallback = ids[device_index] if device_index < len(ids) else str(device_index)
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            if not uuid:
+                return fallback
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            probe = subprocess.run(["nvidia-smi", f"--id={uuid}", "--query-gpu=index", "--format=csv,noheader"],
+                                   capture_output=True, text=True, timeout=10)
+            return uuid if probe.returncode == 0 and probe.stdout.strip() else fallback
+        except Exception:  # no device properties or no nvidia-smi: keep the index mapping
+            return fallback
+
+    def _cmd(self, loop: bool):
+        cmd = ["nvidia-smi", f"--id={self.gpu_id}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"]
+        return cmd + ["-lms", "50"] if loop else cmd
 
     def __enter__(self):
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            self.proc = subprocess.Popen(self._cmd(True), stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            # one more sample taken at the end of the timed region, so short
+            # runs report at least one reading
+            try:
+                out = subprocess.run(self._cmd(False), capture_output=True, text=True, timeout=10).stdout
+                with open(self.path, "a") as f:
+                    f.write(out)
+            except (OSError, subprocess.SubprocessError):
+                pass
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
