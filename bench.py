@@ -40,6 +40,11 @@ sys.path.insert(0, str(ROOT))
 
 KV_BYTES_PER_TOKEN = 36 * 8 * 128 * 2 * 2  # layers x kv heads x head_dim x bf16 x {K,V}
 
+# DRAM bytes (read + write) of one layer's tree-attention launch on the
+# configuration-4 wave, from an ncu capture of that launch
+# (dram__bytes_read.sum 736.3 MB + dram__bytes_write.sum 15.5 MB).
+NCU_ATTENTION_TRAFFIC_CFG4 = 736.310016e6 + 15.491584e6
+
 
 def peaks():
     path = ROOT / "MEASURED_PEAKS.json"
@@ -344,8 +349,9 @@ def run_verify(args, world, rank):
                    "requests_per_gpu": wl.R, "rows_per_gpu": wl.rows, "global_batch_rows": wl.rows * world,
                    "verify_pass_us_per_row": ms * 1000 / wl.rows, "temperature": 1.0,
                    "parallelism": f"dp{world}", "l2": "inputs larger than L2 (16.4 GB weights, ~24 GB KV/step)"},
-        "roofline": {"bound": "hbm", "kernel": "tree_attention_kernel (layer 0)", "achieved": attn_gbs,
-                     "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": attn_gbs / hbm, "traffic": None,
+        "roofline": {"bound": "hbm", "kernel": "tree_attention_tm_kernel (layer 0)", "achieved": attn_gbs,
+                     "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": attn_gbs / hbm,
+                     "traffic": NCU_ATTENTION_TRAFFIC_CFG4 if wl.name.startswith("config4") else None,
                      "algorithmic_bytes_per_launch": attn_bytes, "launch_ms": attn_ms,
                      "pass": {"bound": "tensor", "achieved": pass_tflops, "peak": tc_sus, "unit": "TFLOP/s",
                               "frac": pass_tflops / tc_sus, "algorithmic_flops_per_step": flops,
