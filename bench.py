@@ -44,6 +44,9 @@ KV_BYTES_PER_TOKEN = 36 * 8 * 128 * 2 * 2  # layers x kv heads x head_dim x bf16
 # configuration-4 wave, from an ncu capture of that launch
 # (dram__bytes_read.sum 736.3 MB + dram__bytes_write.sum 15.5 MB).
 NCU_ATTENTION_TRAFFIC_CFG4 = 736.310016e6 + 15.491584e6
+# Same for one gate/up + SwiGLU GEMM launch on the configuration-4 rows
+# (dram__bytes_read.sum 218.3 MB + dram__bytes_write.sum 40.3 MB).
+NCU_SWIGLU_TRAFFIC_CFG4 = 218.3e6 + 40.3e6
 
 
 def peaks():
@@ -336,6 +339,10 @@ def run_verify(args, world, rank):
     attn_gbs = attn_bytes / (attn_ms / 1000) / 1e9
     flops = wl.pass_flops()
     pass_tflops = flops / (ms / 1000) / 1e12
+    gu_ms = stages["L0 gate/up gemm"]
+    gu_flops = 2.0 * wl.rows * (2 * wl.shape.intermediate) * wl.shape.hidden
+    gu_tflops = gu_flops / (gu_ms / 1000) / 1e12
+    cfg4 = wl.name.startswith("config4")
     e2e = e2e_verify(wl, args, world)
     cpu = cpu_baseline_verify(wl) if (rank == 0 and world == 1 and not args.no_cpu) else None
     clk = clocks.summary()
@@ -349,10 +356,18 @@ def run_verify(args, world, rank):
                    "requests_per_gpu": wl.R, "rows_per_gpu": wl.rows, "global_batch_rows": wl.rows * world,
                    "verify_pass_us_per_row": ms * 1000 / wl.rows, "temperature": 1.0,
                    "parallelism": f"dp{world}", "l2": "inputs larger than L2 (16.4 GB weights, ~24 GB KV/step)"},
-        "roofline": {"bound": "hbm", "kernel": "tree_attention_tm_kernel (layer 0)", "achieved": attn_gbs,
-                     "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s", "frac": attn_gbs / hbm,
-                     "traffic": NCU_ATTENTION_TRAFFIC_CFG4 if wl.name.startswith("config4") else None,
-                     "algorithmic_bytes_per_launch": attn_bytes, "launch_ms": attn_ms,
+        # dominant kernel by time: the gate/up GEMM with the SwiGLU epilogue
+        # (timed inside the step, so against the sustained bf16 peak)
+        "roofline": {"bound": "tensor", "kernel": "gemm_kernel<EpiSwiGlu> (layer 0 gate/up)",
+                     "achieved": gu_tflops, "peak": tc_sus, "peak_kind": peak_kind + " sustained",
+                     "unit": "TFLOP/s", "frac": gu_tflops / tc_sus,
+                     "traffic": NCU_SWIGLU_TRAFFIC_CFG4 if cfg4 else None,
+                     "algorithmic_flops_per_launch": gu_flops, "launch_ms": gu_ms,
+                     "attention": {"bound": "hbm", "kernel": "tree_attention_tm_kernel (layer 0)",
+                                   "achieved": attn_gbs, "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
+                                   "frac": attn_gbs / hbm,
+                                   "traffic": NCU_ATTENTION_TRAFFIC_CFG4 if cfg4 else None,
+                                   "algorithmic_bytes_per_launch": attn_bytes, "launch_ms": attn_ms},
                      "pass": {"bound": "tensor", "achieved": pass_tflops, "peak": tc_sus, "unit": "TFLOP/s",
                               "frac": pass_tflops / tc_sus, "algorithmic_flops_per_step": flops,
                               "peak_kind": peak_kind + " sustained"}},
