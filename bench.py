@@ -45,8 +45,8 @@ KV_BYTES_PER_TOKEN = 36 * 8 * 128 * 2 * 2  # layers x kv heads x head_dim x bf16
 # (dram__bytes_read.sum 736.3 MB + dram__bytes_write.sum 15.5 MB).
 NCU_ATTENTION_TRAFFIC_CFG4 = 736.310016e6 + 15.491584e6
 # Same for one gate/up + SwiGLU GEMM launch on the configuration-4 rows
-# (dram__bytes_read.sum 218.3 MB + dram__bytes_write.sum 40.3 MB).
-NCU_SWIGLU_TRAFFIC_CFG4 = 218.3e6 + 40.3e6
+# (dram__bytes_read.sum 218.2 MB + dram__bytes_write.sum 41.1 MB).
+NCU_SWIGLU_TRAFFIC_CFG4 = 218.232576e6 + 41.149184e6
 
 
 def peaks():
