@@ -476,7 +476,14 @@ def run_b200(args, world, rank):
     commit_ms = [e[1].elapsed_time(e[2]) for e in ev]
     visited = (outs[..., wl.D] + 1).double()        # scan rule: accepted + exit row
     accept_bytes = float(visited.sum()) / K * wl.vocab * 4
-    commit_bytes = float(visited.sum()) / K * KV_BYTES_PER_TOKEN
+    # kept tokens x 147,456 B, read and written (the reference's append copies
+    # every kept row); here the root row and rows already at their final
+    # position never move, so the bytes actually moved are fewer
+    commit_bytes = float(visited.sum()) / K * KV_BYTES_PER_TOKEN * 2
+    moved = outs[..., :wl.D] >= 0
+    depth_idx = torch.arange(1, wl.D + 1, device=outs.device).expand_as(moved)
+    moved_rows = float((moved & (outs[..., :wl.D] != depth_idx)).sum()) / K
+    moved_bytes = moved_rows * KV_BYTES_PER_TOKEN * 2
     accept_gbs = accept_bytes / (statistics.mean(accept_ms) / 1000) / 1e9
     commit_gbs = commit_bytes / (statistics.mean(commit_ms) / 1000) / 1e9
     # e2e through the public API with host buffers: probabilities and tree
@@ -496,7 +503,8 @@ def run_b200(args, world, rank):
                      "algorithmic_bytes_per_launch": accept_bytes,
                      "launch_ms": statistics.mean(accept_ms),
                      "commit": {"achieved": commit_gbs, "frac": commit_gbs / hbm,
-                                "bytes_per_launch": commit_bytes, "launch_ms": statistics.mean(commit_ms)}},
+                                "bytes_per_launch": commit_bytes, "moved_bytes_per_launch": moved_bytes,
+                                "launch_ms": statistics.mean(commit_ms)}},
         "cpu_baseline": cpu, "clocks": clk, "e2e": e2e, "gpu_launches": launches,
     }
     return line

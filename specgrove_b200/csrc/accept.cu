@@ -2,9 +2,11 @@
 //
 // One thread-block cluster walks one request tree top-down.  At each visited
 // node the cluster's CTAs split the node's probability row, reduce it to exact
-// 64.64 fixed-point masses per 128-token block, exchange their slice totals
-// through distributed shared memory, and the CTA whose slice holds the
-// inverse-CDF threshold locates the token with one 128-token rescan.  The walk
+// 64.64 fixed-point masses per 1024-token block (a warp per block, 32 tokens
+// per lane; probabilities below 1 take a one-word fixed-point path), exchange
+// their slice totals through distributed shared memory, and the CTA whose
+// slice holds the inverse-CDF threshold locates the token with one
+// 1024-token rescan in index order.  The walk
 // then follows the matching child edge (warp ballot over the tree's nodes).
 //
 // Semantics follow the reference kernels
@@ -27,8 +29,8 @@ namespace {
 
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-constexpr int kBlockElems = 128;  // one warp x float4
-constexpr int kUnroll = 8;
+constexpr int kBlockElems = 1024;  // one warp x 8 float4 per lane
+constexpr int kVecs = kBlockElems / 128;  // float4 loads per lane per block
 constexpr int kMaxChildren = 256;
 
 struct AcceptParams {
@@ -53,6 +55,28 @@ struct AcceptParams {
 
 __device__ __forceinline__ void report(int32_t* status, int code) {
   if (status != nullptr) atomicMax(status, code);
+}
+
+// General path for a float4 with a value >= 1, negative or not finite (rare
+// in probability rows), kept out of line so the common path stays short.
+__device__ __noinline__ void accumulate4_general(Mass& big, uint4 v, uint32_t* bad) {
+  big = mass_add(big, mass_from_bits(v.x, bad));
+  big = mass_add(big, mass_from_bits(v.y, bad));
+  big = mass_add(big, mass_from_bits(v.z, bad));
+  big = mass_add(big, mass_from_bits(v.w, bad));
+}
+
+// Exact masses of four fp32 values into (lo, carry) — all four below 1.0 —
+// or into `big` through the general path.
+__device__ __forceinline__ void accumulate4(uint64_t& lo, uint32_t& carry, Mass& big, uint4 v, uint32_t* bad) {
+  if (__builtin_expect(max(max(v.x, v.y), max(v.z, v.w)) < 0x3f800000u, 1)) {
+    add_with_carry(lo, carry, mass_lo_f64(v.x));
+    add_with_carry(lo, carry, mass_lo_f64(v.y));
+    add_with_carry(lo, carry, mass_lo_f64(v.z));
+    add_with_carry(lo, carry, mass_lo_f64(v.w));
+  } else {
+    accumulate4_general(big, v, bad);
+  }
 }
 
 __device__ __forceinline__ Mass warp_sum(Mass v) {
@@ -231,26 +255,22 @@ __global__ void __launch_bounds__(kThreads, 1) accept_probs_kernel(const AcceptP
       }
     }
 
-    // ---- full-row pass: exact mass of every 128-token block of this slice.
-    for (int base = warp; base < nb; base += kWarps * kUnroll) {
-      uint4 v[kUnroll];
+    // ---- full-row pass: exact mass of every 1024-token block of this slice
+    // (lane l reads float4 l of each 512-byte segment, so every load
+    // instruction is one contiguous 512 bytes; 8 loads per lane in flight).
+    for (int b = warp; b < nb; b += kWarps) {
+      uint4 v[kVecs];
 #pragma unroll
-      for (int k = 0; k < kUnroll; ++k) {
-        const int b = base + k * kWarps;
-        if (b < nb) v[k] = load4(row, (slice_first + b) * kBlockElems + lane * 4, V, p.aligned4);
-      }
+      for (int k = 0; k < kVecs; ++k)
+        v[k] = load4(row, (slice_first + b) * kBlockElems + k * 128 + lane * 4, V, p.aligned4);
+      uint64_t lo = 0ull;
+      uint32_t carry = 0u;
+      Mass big = mass_zero();
 #pragma unroll
-      for (int k = 0; k < kUnroll; ++k) {
-        const int b = base + k * kWarps;
-        if (b < nb) {
-          Mass s = mass_from_bits(v[k].x, &bad_prob);
-          s = mass_add(s, mass_from_bits(v[k].y, &bad_prob));
-          s = mass_add(s, mass_from_bits(v[k].z, &bad_prob));
-          s = mass_add(s, mass_from_bits(v[k].w, &bad_prob));
-          s = warp_sum(s);
-          if (lane == 0) blk[b] = s;
-        }
-      }
+      for (int k = 0; k < kVecs; ++k) accumulate4(lo, carry, big, v[k], &bad_prob);
+      Mass s = mass_add(Mass{lo, carry}, big);
+      s = warp_sum(s);
+      if (lane == 0) blk[b] = s;
     }
     __syncthreads();
     if (sparse && tid == 0) {
@@ -326,30 +346,43 @@ __global__ void __launch_bounds__(kThreads, 1) accept_probs_kernel(const AcceptP
       }
       __syncthreads();
       if (warp == 0) {
+        // Rescan the crossing block in index order: lane l owns tokens
+        // [first, first + 32) with first = block start + 32 l.
         const int b = s_cross_block;
         const Mass resid = s_cross_residual;
-        const int64_t first = (slice_first + b) * kBlockElems + lane * 4;
-        const uint4 v = load4(row, first, V, p.aligned4);
-        uint32_t e[4] = {v.x, v.y, v.z, v.w};
-        Mass m[4];
-        uint32_t bad = 0u;
-        Mass lane_sum = mass_zero();
+        const int64_t first = (slice_first + b) * kBlockElems + lane * (kBlockElems / 32);
+        uint32_t e[kBlockElems / 32];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          m[k] = mass_from_bits(e[k], &bad);
-          if (sparse) {
-            for (int c = 0; c < s_child_count; ++c)
-              if (s_child_tok[c] == first + k) m[k] = mass_zero();
-          }
-          lane_sum = mass_add(lane_sum, m[k]);
+        for (int k = 0; k < kBlockElems / 128; ++k) {
+          const uint4 v = load4(row, first + k * 4, V, p.aligned4);
+          e[4 * k] = v.x;
+          e[4 * k + 1] = v.y;
+          e[4 * k + 2] = v.z;
+          e[4 * k + 3] = v.w;
         }
+        uint32_t bad = 0u;
+        if (sparse) {  // children are excluded from the exit draw
+          for (int c = 0; c < s_child_count; ++c) {
+            const int64_t off = s_child_tok[c] - first;
+#pragma unroll
+            for (int k = 0; k < kBlockElems / 32; ++k)
+              if (off == k) e[k] = 0u;
+          }
+        }
+        uint64_t lo = 0ull;
+        uint32_t carry = 0u;
+        Mass big = mass_zero();
+#pragma unroll
+        for (int k = 0; k < kBlockElems / 128; ++k)
+          accumulate4(lo, carry, big, make_uint4(e[4 * k], e[4 * k + 1], e[4 * k + 2], e[4 * k + 3]), &bad);
+        const Mass lane_sum = mass_add(Mass{lo, carry}, big);
         const Mass li = warp_inclusive_scan(lane_sum, lane);
         Mass run = mass_sub(li, lane_sum);
         int found = -1;
         if (!mass_lt(resid, run) && mass_lt(resid, li)) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            run = mass_add(run, m[k]);
+          for (int k = 0; k < kBlockElems / 32; ++k) {
+            mass_accumulate(run, e[k], &bad);
             if (found < 0 && mass_lt(resid, run)) found = k;
           }
         }
@@ -358,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1) accept_probs_kernel(const AcceptP
           const int src = __ffs(who) - 1;
           const int fk = __shfl_sync(0xffffffffu, found, src);
           if (lane == 0) {
-            const int token = static_cast<int>((slice_first + b) * kBlockElems + src * 4 + fk);
+            const int token = static_cast<int>((slice_first + b) * kBlockElems + src * (kBlockElems / 32) + fk);
 #pragma unroll
             for (int r = 0; r < CLUSTER; ++r) *cluster.map_shared_rank(&s_selected, r) = token;
           }

@@ -157,6 +157,52 @@ __host__ __device__ __forceinline__ Mass mass_from_bits(uint32_t bits, uint32_t*
   return r;
 }
 
+// floor(p * 2^64) of a non-negative fp32 p below 1.0 (bit pattern below
+// 0x3f800000): the low word of its 64.64 mass, whose high word is zero.  Equal
+// to mass_from_bits on every such input (checked exhaustively).
+__host__ __device__ __forceinline__ uint64_t mass_lo_below_one(uint32_t bits) {
+  const uint32_t e = bits >> 23;  // 0 .. 126
+  const uint32_t m = (bits & 0x7fffffu) | (e != 0u ? 0x800000u : 0u);
+  const int s = static_cast<int>(e != 0u ? e : 1u) - 86;  // mass = m * 2^s
+  if (s >= 0) return static_cast<uint64_t>(m) << s;       // s <= 40
+  const int r = -s;
+  return r < 32 ? static_cast<uint64_t>(m >> r) : 0ull;   // m < 2^24
+}
+
+#ifdef __CUDACC__
+// Same value on the device in four instructions: the fp32 bits shifted left
+// by 29 plus 960 << 52 are exactly the fp64 bit pattern of p * 2^64 (the
+// exponent rebased from 127 to 1023 + 64; fp32 denormals land below 1), and
+// the truncating conversion to an unsigned 64-bit integer is the floor.
+// Equal to mass_lo_below_one on every input below 1.0 (checked exhaustively).
+__device__ __forceinline__ uint64_t mass_lo_f64(uint32_t bits) {
+  const uint64_t d = (static_cast<uint64_t>(bits) << 29) + 0x3C00000000000000ull;
+  return __double2ull_rz(__longlong_as_double(static_cast<long long>(d)));
+}
+
+// (lo, carry) += v as one carry chain.
+__device__ __forceinline__ void add_with_carry(uint64_t& lo, uint32_t& carry, uint64_t v) {
+  asm("add.cc.u64 %0, %0, %2;\n\taddc.u32 %1, %1, 0;" : "+l"(lo), "+r"(carry) : "l"(v));
+}
+#endif
+
+// Exact running sum of fp32 masses: probabilities below 1 take the one-word
+// path (low word plus a carry count in the high word); anything else goes
+// through mass_from_bits.
+__host__ __device__ __forceinline__ void mass_accumulate(Mass& acc, uint32_t bits, uint32_t* bad) {
+  if (bits < 0x3f800000u) {
+#ifdef __CUDA_ARCH__
+    const uint64_t v = mass_lo_f64(bits);
+#else
+    const uint64_t v = mass_lo_below_one(bits);
+#endif
+    acc.lo += v;
+    acc.hi += (acc.lo < v) ? 1ull : 0ull;
+  } else {
+    acc = mass_add(acc, mass_from_bits(bits, bad));
+  }
+}
+
 __host__ __device__ __forceinline__ uint64_t mul_hi64(uint64_t a, uint64_t b) {
 #ifdef __CUDA_ARCH__
   return __umul64hi(a, b);

@@ -137,71 +137,53 @@ namespace sg {
 namespace {
 
 constexpr int kMaxKeep = 64;
+constexpr int kAcceptedThreads = 256;
 
-__global__ void __launch_bounds__(kCommitThreads)
-kv_commit_accepted_kernel(unsigned char* arena, int64_t plane_rows, int64_t num_planes,
-                          int64_t row_bytes, int64_t capacity, const int64_t* __restrict__ slots,
+// One thread per (tree, plane, 16- or 4-byte column).  Kept row r of a tree
+// is node out[r-1] of its tree (row 0, the root, is node 0), which the verify
+// pass wrote at len + node; it moves to len + r.  Nodes on the accepted path
+// increase with depth, so node_r >= r: walking r upward, a thread never
+// overwrites a row it still has to read (a destination len + r equal to a
+// later source len + node_r' would need node_r' = r < r'), and no staging is
+// needed.  Rows already in place (node_r == r, always the root) are skipped.
+__global__ void __launch_bounds__(kAcceptedThreads)
+kv_commit_accepted_kernel(unsigned char* arena, int64_t plane_rows, int64_t num_planes, int64_t row_bytes,
+                          int64_t capacity, const int64_t* __restrict__ slots,
                           const int64_t* __restrict__ lengths_in, int64_t* __restrict__ lengths_out,
-                          const int64_t* __restrict__ accept_out, int32_t max_depth,
-                          int planes_per_cta, bool vec16, int32_t* status) {
-  __shared__ __align__(16) unsigned char stage[kStageBytes];
-  __shared__ int64_t s_src[kMaxKeep];
-  __shared__ int s_kept;
-  const int t = blockIdx.x;
-  const int64_t plane0 = static_cast<int64_t>(blockIdx.y) * planes_per_cta;
-  const int nplanes = static_cast<int>(min64(planes_per_cta, num_planes - plane0));
+                          const int64_t* __restrict__ accept_out, int32_t max_depth, bool vec16,
+                          int32_t* status) {
+  const int t = blockIdx.y;
   const int64_t* out = accept_out + static_cast<int64_t>(t) * (max_depth + 2);
   const int64_t slot = slots[t];
   const int64_t len = lengths_in[t];
-  if (threadIdx.x == 0) {
-    int64_t count = out[max_depth];
-    int kept = static_cast<int>(count) + 1;
-    bool ok = count >= 0 && count <= max_depth && kept <= kMaxKeep && len >= 0 &&
-              len + kept <= capacity && slot >= 0 && (slot + 1) * capacity <= plane_rows;
-    if (!ok) {
-      if (status != nullptr) atomicMax(status, static_cast<int32_t>(SG_ERR_CAPACITY));
-      kept = 0;
-    }
-    s_kept = kept;
-    if (blockIdx.y == 0) lengths_out[t] = len + kept;
+  const int64_t count = out[max_depth];
+  int kept = static_cast<int>(count) + 1;
+  const bool ok = count >= 0 && count <= max_depth && kept <= kMaxKeep && len >= 0 && len + kept <= capacity &&
+                  slot >= 0 && (slot + 1) * capacity <= plane_rows;
+  if (!ok) kept = 0;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (!ok && status != nullptr) atomicMax(status, static_cast<int32_t>(SG_ERR_CAPACITY));
+    lengths_out[t] = len + kept;
   }
-  __syncthreads();
-  const int kept = s_kept;
-  if (threadIdx.x < kept) {
-    const int64_t node = threadIdx.x == 0 ? 0 : out[threadIdx.x - 1];
-    s_src[threadIdx.x] = slot * capacity + len + node;
-  }
-  __syncthreads();
-  if (kept == 0 || nplanes <= 0) return;
+  if (kept <= 1) return;
   const int unit = vec16 ? 16 : 4;
-  const int units_per_row = static_cast<int>(row_bytes / unit);
-  const int64_t dst0 = slot * capacity + len;
-  const int total_units = nplanes * kept * units_per_row;
-  for (int i = threadIdx.x; i < total_units; i += kCommitThreads) {
-    const int u = i % units_per_row;
-    const int rest = i / units_per_row;
-    const int r = rest % kept;
-    const int pl = rest / kept;
-    const int64_t s = s_src[r];
-    const unsigned char* from = arena + ((plane0 + pl) * plane_rows + s) * row_bytes + static_cast<int64_t>(u) * unit;
-    unsigned char* to = stage + static_cast<int64_t>(i) * unit;
+  const int64_t units_per_row = row_bytes / unit;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * kAcceptedThreads + threadIdx.x;
+  if (i >= num_planes * units_per_row) return;
+  const int64_t plane = i / units_per_row;
+  const int64_t u = i % units_per_row;
+  unsigned char* col = arena + (plane * plane_rows + slot * capacity + len) * row_bytes + u * unit;
+  for (int r = 1; r < kept; ++r) {
+    const int64_t node = out[r - 1];
+    if (node == r) continue;
+    if (node < r || len + node >= capacity) {  // not a root path in this slot's tail
+      if (status != nullptr) atomicMax(status, static_cast<int32_t>(SG_ERR_TREE));
+      return;
+    }
     if (vec16)
-      *reinterpret_cast<uint4*>(to) = *reinterpret_cast<const uint4*>(from);
+      *reinterpret_cast<uint4*>(col + r * row_bytes) = *reinterpret_cast<const uint4*>(col + node * row_bytes);
     else
-      *reinterpret_cast<uint32_t*>(to) = *reinterpret_cast<const uint32_t*>(from);
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < total_units; i += kCommitThreads) {
-    const int u = i % units_per_row;
-    const int rest = i / units_per_row;
-    const int r = rest % kept;
-    const int pl = rest / kept;
-    unsigned char* to = arena + ((plane0 + pl) * plane_rows + dst0 + r) * row_bytes + static_cast<int64_t>(u) * unit;
-    const unsigned char* from = stage + static_cast<int64_t>(i) * unit;
-    if (vec16)
-      *reinterpret_cast<uint4*>(to) = *reinterpret_cast<const uint4*>(from);
-    else
-      *reinterpret_cast<uint32_t*>(to) = *reinterpret_cast<const uint32_t*>(from);
+      *reinterpret_cast<uint32_t*>(col + r * row_bytes) = *reinterpret_cast<const uint32_t*>(col + node * row_bytes);
   }
 }
 
@@ -224,16 +206,14 @@ extern "C" int sg_kv_commit_accepted(void* arena, int64_t plane_rows, int64_t nu
     return fail(SG_ERR_INVALID_ARGUMENT, "sg_kv_commit_accepted: bad sizes");
   if (max_depth + 1 > kMaxKeep)
     return fail(SG_ERR_UNSUPPORTED, "sg_kv_commit_accepted: max_depth above 63");
-  const int64_t per_plane = static_cast<int64_t>(max_depth + 1) * row_bytes;
-  if (per_plane > kStageBytes) return fail(SG_ERR_UNSUPPORTED, "sg_kv_commit_accepted: rows too large");
   const bool vec16 = (row_bytes % 16 == 0) && (reinterpret_cast<uintptr_t>(arena) % 16 == 0);
-  int64_t planes_per_cta = kStageBytes / per_plane;
-  if (planes_per_cta > num_planes) planes_per_cta = num_planes;
-  const int64_t grid_y = (num_planes + planes_per_cta - 1) / planes_per_cta;
-  if (grid_y > 65535) return fail(SG_ERR_UNSUPPORTED, "sg_kv_commit_accepted: too many planes");
-  dim3 grid(static_cast<unsigned>(num_trees), static_cast<unsigned>(grid_y), 1);
-  kv_commit_accepted_kernel<<<grid, kCommitThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  const int64_t columns = num_planes * (row_bytes / (vec16 ? 16 : 4));
+  const int64_t grid_x = (columns + kAcceptedThreads - 1) / kAcceptedThreads;
+  if (grid_x > 0x7fffffff || num_trees > 65535)
+    return fail(SG_ERR_UNSUPPORTED, "sg_kv_commit_accepted: more than 65535 trees or too many columns");
+  dim3 grid(static_cast<unsigned>(grid_x), static_cast<unsigned>(num_trees), 1);
+  kv_commit_accepted_kernel<<<grid, kAcceptedThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<unsigned char*>(arena), plane_rows, num_planes, row_bytes, capacity, slots, lengths_in,
-      lengths_out, accept_out, max_depth, static_cast<int>(planes_per_cta), vec16, status);
+      lengths_out, accept_out, max_depth, vec16, status);
   return check_launch("kv_commit_accepted_kernel");
 }
