@@ -187,7 +187,7 @@ def sum_over_ranks(value: float, world: int) -> float:
 class AcceptWorkload:
     name = "acceptance_sweep: 64 trees / 4096 nodes / V=151936 fp32 probs + KV commit 36x8x128 bf16"
 
-    def __init__(self, rank: int, capacity: int = 320):
+    def __init__(self, rank: int):
         from specgrove_b200 import workloads
         from specgrove_b200.arena import PersistentKVArena
         from specgrove_b200.sampling import PackedTrees
@@ -196,14 +196,17 @@ class AcceptWorkload:
         self.D = self.trees.max_depth
         self.T = self.trees.count
         self.vocab = self.probs.shape[1]
-        self.arena = PersistentKVArena(36, 8, 128, self.T, capacity, dtype=torch.bfloat16)
         rng = np.random.default_rng(rank)
         self.lengths0 = rng.integers(64, 257, size=self.T)
+        # a node's tree row sits at length + node in its slot's tail
+        capacity = int(self.lengths0.max()) + self.trees.max_nodes
+        self.arena = PersistentKVArena(36, 8, 128, self.T, capacity, dtype=torch.bfloat16)
         self.slots = torch.arange(self.T, dtype=torch.long, device="cuda")
         self.len_in = torch.from_numpy(self.lengths0.astype(np.int64)).cuda()
         self.len_out = torch.empty_like(self.len_in)
         self.request_ids = torch.arange(self.T, dtype=torch.long, device="cuda") + 1000 * rank
         self.status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        torch.cuda.empty_cache()   # release the generator's temporaries
 
     def step(self, seed: int, out: torch.Tensor, events=None):
         from specgrove_b200 import _lib
