@@ -145,6 +145,10 @@ SG_API int sg_kv_commit(void* dst, int64_t dst_plane_rows, const void* src,
  * slots, lengths_in, lengths_out  [num_trees] int64 (lengths_out != lengths_in)
  * accept_out   [num_trees, max_depth + 2] output of sg_tree_accept_probs /
  *              sg_tree_follow; max_depth <= 63.
+ * status       a count that overflows the slot sets SG_ERR_CAPACITY; a path
+ *              that is not a root path inside the slot's tail (node < depth,
+ *              or beyond the capacity) sets SG_ERR_TREE and that tree's rows
+ *              are left unmoved.
  */
 SG_API int sg_kv_commit_accepted(void* arena, int64_t plane_rows, int64_t num_planes,
                           int64_t row_bytes, int64_t capacity, const int64_t* slots,

@@ -1,13 +1,19 @@
 // Tree-sampling acceptance over packed fp32 probability rows (sm_100a).
 //
-// One thread-block cluster walks one request tree top-down.  At each visited
-// node the cluster's CTAs split the node's probability row, reduce it to exact
-// 64.64 fixed-point masses per 1024-token block (a warp per block, 32 tokens
-// per lane; probabilities below 1 take a one-word fixed-point path), exchange
-// their slice totals through distributed shared memory, and the CTA whose
-// slice holds the inverse-CDF threshold locates the token with one
-// 1024-token rescan in index order.  The walk
-// then follows the matching child edge (warp ballot over the tree's nodes).
+// One thread-block cluster (up to 8 CTAs) walks one request tree top-down;
+// the cluster size is the largest for which every tree's cluster is resident
+// at once.  At each visited node the cluster's CTAs split the node's
+// probability row into 1024-token blocks.  Each CTA streams its slice through
+// a ring of 4 KB shared-memory slots filled by bulk asynchronous copies
+// (cp.async.bulk completing on an mbarrier, no multicast); the warp that owns
+// a slot waits for it, reduces the block to an exact 64.64 fixed-point mass
+// and refills the slot, so a CTA keeps 48 KB of the row in flight without
+// holding it in registers.  Block masses are double-buffered by pass, so one
+// cluster barrier per visited node suffices: after it, warp 0 of every CTA
+// reads the slice totals and the owning CTA's block masses through
+// distributed shared memory, finds the crossing block, rescans it in index
+// order (lane sums, then the crossing lane's 32 tokens spread over the warp)
+// and reaches the same token and child as every other CTA of the cluster.
 //
 // Semantics follow the reference kernels
 //   fused_tree_sampling.py:538-627 (scan rule: token = first index whose
@@ -20,18 +26,32 @@
 // decision is independent of the reduction order.
 #include <cooperative_groups.h>
 
+#include <cstdlib>
+#include <mutex>
+
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace sg {
 namespace {
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
+constexpr int kMinCtasPerSm = 4;
 constexpr int kBlockElems = 1024;  // one warp x 8 float4 per lane
-constexpr int kVecs = kBlockElems / 128;  // float4 loads per lane per block
+constexpr int kBlockBytes = kBlockElems * 4;
+constexpr int kVecs = kBlockElems / 128;  // float4 per lane per block
+constexpr int kSlots = 12;                // ring of 4 KB slots per CTA (48 KB), 3 per warp
 constexpr int kMaxChildren = 256;
+constexpr int kMaxCluster = 8;
+// Block i of a slice goes to slot i % kSlots and is reduced by warp
+// i % kWarps.  With kSlots a multiple of kWarps every slot has one owner
+// warp, which both waits for each of its fills and issues the next one, so a
+// slot's barrier is never more than the one awaited phase ahead of its
+// waiter (a parity wait cannot tell phase k from phase k - 2).
+static_assert(kSlots % kWarps == 0, "each ring slot must belong to exactly one warp");
 
 struct AcceptParams {
   const float* probs;
@@ -49,7 +69,7 @@ struct AcceptParams {
   const int64_t* request_ids;
   int64_t* out;
   int32_t* status;
-  int32_t blocks_per_cta;  // 128-token blocks per CTA slice
+  int32_t blocks_per_cta;  // 1024-token blocks per CTA slice
   bool aligned4;           // rows 16-byte aligned and vocab % 4 == 0
 };
 
@@ -116,8 +136,130 @@ __device__ __forceinline__ uint4 load4(const float* row, int64_t index, int64_t 
   return r;
 }
 
-template <int CLUSTER>
-__global__ void __launch_bounds__(kThreads, 1) accept_probs_kernel(const AcceptParams p) {
+__device__ __forceinline__ Mass shfl_mass(Mass v, int src) {
+  Mass r;
+  r.lo = __shfl_sync(0xffffffffu, v.lo, src);
+  r.hi = __shfl_sync(0xffffffffu, v.hi, src);
+  return r;
+}
+
+// Bulk asynchronous copy of `bytes` (multiple of 16, both addresses 16-byte
+// aligned) from global memory into this CTA's shared memory, completing on
+// `bar` (no multicast).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          sm100::smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(sm100::smem_u32(bar))
+      : "memory");
+}
+
+// Fill ring slot `slot` with block `b` of `row` (blocks past the end of the
+// row are never issued; the row's last block may be short).
+__device__ __forceinline__ void fill_slot(float* ring, uint64_t* full, int slot, const float* row,
+                                          int64_t b, int64_t vocab) {
+  const int64_t base = b * kBlockElems;
+  const uint32_t bytes = static_cast<uint32_t>(min64(kBlockElems, vocab - base) * 4);
+  sm100::mbar_arrive_expect_tx(&full[slot], bytes);
+  bulk_load(ring + slot * kBlockElems, row + base, bytes, &full[slot]);
+}
+
+// Exact mass of block `gb` (global block index) of `row` read from a ring
+// slot: lane l holds float4 l of each 512-byte segment.
+__device__ __forceinline__ Mass slot_mass(const float* slot, int64_t gb, int64_t vocab, int lane, uint32_t* bad) {
+  const float4* src = reinterpret_cast<const float4*>(slot);
+  const int64_t base = gb * kBlockElems;
+  // Four independent carry chains (float4 k goes to chain k % 4) keep the
+  // dependent adds per lane short.
+  constexpr int kChains = 4;
+  uint64_t lo[kChains] = {};
+  uint32_t carry[kChains] = {};
+  Mass big = mass_zero();
+#pragma unroll
+  for (int k = 0; k < kVecs; ++k) {
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (base + k * 128 + lane * 4 < vocab) {  // vocab % 4 == 0 on this path
+      const float4 f = src[k * 32 + lane];
+      v = make_uint4(__float_as_uint(f.x), __float_as_uint(f.y), __float_as_uint(f.z), __float_as_uint(f.w));
+    }
+    accumulate4(lo[k % kChains], carry[k % kChains], big, v, bad);
+  }
+  Mass sum = big;
+#pragma unroll
+  for (int c = 0; c < kChains; ++c) sum = mass_add(sum, Mass{lo[c], carry[c]});
+  return warp_sum(sum);
+}
+
+// The same mass read straight from global memory (rows that are not 16-byte
+// aligned or whose vocabulary is not a multiple of 4).
+__device__ __forceinline__ Mass global_mass(const float* row, int64_t gb, int64_t vocab, bool aligned4, int lane,
+                                            uint32_t* bad) {
+  uint4 v[kVecs];
+#pragma unroll
+  for (int k = 0; k < kVecs; ++k) v[k] = load4(row, gb * kBlockElems + k * 128 + lane * 4, vocab, aligned4);
+  uint64_t lo = 0ull;
+  uint32_t carry = 0u;
+  Mass big = mass_zero();
+#pragma unroll
+  for (int k = 0; k < kVecs; ++k) accumulate4(lo, carry, big, v[k], bad);
+  return warp_sum(mass_add(Mass{lo, carry}, big));
+}
+
+// Warp-wide: the token of block `gb` of `row` at which the running mass of
+// the block first exceeds `resid` (resid < the block's mass), or -1.  Lane l
+// owns the 32 consecutive tokens from gb * 1024 + 32 l; children of a
+// sparse-exit node count as zero.  A scan of the lane sums picks the lane
+// that holds the crossing, whose 32 values are then spread one per lane for a
+// second scan, so no lane walks its tokens serially.
+__device__ __forceinline__ int crossing_token(const float* row, int64_t gb, int64_t vocab, bool aligned4, Mass resid,
+                                              bool sparse, const int* child_tok, int child_count, int lane,
+                                              uint32_t* bad) {
+  const int64_t first = gb * kBlockElems + lane * (kBlockElems / 32);
+  uint32_t e[kBlockElems / 32];
+#pragma unroll
+  for (int k = 0; k < kBlockElems / 128; ++k) {
+    const uint4 v = load4(row, first + k * 4, vocab, aligned4);
+    e[4 * k] = v.x;
+    e[4 * k + 1] = v.y;
+    e[4 * k + 2] = v.z;
+    e[4 * k + 3] = v.w;
+  }
+  if (sparse) {  // children are excluded from the exit draw
+    for (int c = 0; c < child_count; ++c) {
+      const int64_t off = child_tok[c] - first;
+#pragma unroll
+      for (int k = 0; k < kBlockElems / 32; ++k)
+        if (off == k) e[k] = 0u;
+    }
+  }
+  uint64_t lo = 0ull;
+  uint32_t carry = 0u;
+  Mass big = mass_zero();
+#pragma unroll
+  for (int k = 0; k < kBlockElems / 128; ++k)
+    accumulate4(lo, carry, big, make_uint4(e[4 * k], e[4 * k + 1], e[4 * k + 2], e[4 * k + 3]), bad);
+  const Mass lane_sum = mass_add(Mass{lo, carry}, big);
+  const Mass li = warp_inclusive_scan(lane_sum, lane);
+  const Mass le = mass_sub(li, lane_sum);
+  const unsigned hit = __ballot_sync(0xffffffffu, !mass_lt(resid, le) && mass_lt(resid, li));
+  if (hit == 0u) return -1;
+  const int L = __ffs(hit) - 1;
+  const Mass resid2 = mass_sub(resid, shfl_mass(le, L));
+  // Lane j takes token j of lane L's run.
+  uint32_t mine = 0u;
+#pragma unroll
+  for (int k = 0; k < kBlockElems / 32; ++k) {
+    const uint32_t v = __shfl_sync(0xffffffffu, e[k], L);
+    if (k == lane) mine = v;
+  }
+  const Mass ti = warp_inclusive_scan(mass_from_bits(mine, bad), lane);
+  const unsigned hit2 = __ballot_sync(0xffffffffu, mass_lt(resid2, ti));
+  if (hit2 == 0u) return -1;
+  return static_cast<int>(first - lane * (kBlockElems / 32)) + L * (kBlockElems / 32) + (__ffs(hit2) - 1);
+}
+
+template <int CLUSTER, bool BULK>
+__global__ void __launch_bounds__(kThreads, kMinCtasPerSm) accept_probs_kernel(const AcceptParams p) {
   cg::cluster_group cluster = cg::this_cluster();
   const unsigned crank = cluster.block_rank();
   const int tree = static_cast<int>(blockIdx.x) / CLUSTER;
@@ -125,20 +267,27 @@ __global__ void __launch_bounds__(kThreads, 1) accept_probs_kernel(const AcceptP
   const int lane = tid & 31;
   const int warp = tid >> 5;
 
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  Mass* blk = reinterpret_cast<Mass*>(smem_raw);                        // [blocks_per_cta]
-  int* s_parent = reinterpret_cast<int*>(blk + p.blocks_per_cta);       // [max_nodes]
-  int* s_token = s_parent + p.max_nodes;                                // [max_nodes]
+  // Dynamic shared memory: [ring: kSlots x 4 KB (BULK only)]
+  // [block masses: 2 x blocks_per_cta] [parents: max_nodes] [tokens: max_nodes]
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  float* ring = reinterpret_cast<float*>(smem_raw);
+  Mass* blk = reinterpret_cast<Mass*>(smem_raw + (BULK ? kSlots * kBlockBytes : 0));
+  int* s_parent = reinterpret_cast<int*>(blk + 2 * p.blocks_per_cta);
+  int* s_token = s_parent + p.max_nodes;
 
-  __shared__ Mass s_cta_total;
-  __shared__ Mass s_warp[kWarps];
-  __shared__ int s_selected;       // written into every CTA by the owner
+  __shared__ __align__(8) uint64_t s_full[kSlots];
+  __shared__ Mass s_total[2];  // this CTA's slice total, by pass parity
   __shared__ int s_bad_tree;
   __shared__ int s_child_count;
   __shared__ int s_child_node[kMaxChildren];
   __shared__ int s_child_tok[kMaxChildren];
-  __shared__ int s_cross_block;
-  __shared__ Mass s_cross_residual;
+  __shared__ int s_sel_token;
+  __shared__ int s_sel_child;
+
+  if (BULK && tid == 0) {
+    for (int s = 0; s < kSlots; ++s) sm100::mbar_init(&s_full[s], 1);
+    sm100::fence_barrier_init();
+  }
 
   const int64_t row0 = p.row_offsets[tree];
   const int n = static_cast<int>(p.row_offsets[tree + 1] - row0);
@@ -181,7 +330,9 @@ __global__ void __launch_bounds__(kThreads, 1) accept_probs_kernel(const AcceptP
 
   int cur = 0;
   int accepted = 0;
+  int pass = 0;  // full-row passes so far (identical in every CTA of the cluster)
   uint32_t bad_prob = 0u;
+  bool wait_failed = false;
   for (int depth = 0; depth <= D; ++depth) {
     const float* row = p.probs + (row0 + cur) * V;
     double u_main, u_exit;
@@ -255,185 +406,155 @@ __global__ void __launch_bounds__(kThreads, 1) accept_probs_kernel(const AcceptP
       }
     }
 
-    // ---- full-row pass: exact mass of every 1024-token block of this slice
-    // (lane l reads float4 l of each 512-byte segment, so every load
-    // instruction is one contiguous 512 bytes; 8 loads per lane in flight).
-    for (int b = warp; b < nb; b += kWarps) {
-      uint4 v[kVecs];
-#pragma unroll
-      for (int k = 0; k < kVecs; ++k)
-        v[k] = load4(row, (slice_first + b) * kBlockElems + k * 128 + lane * 4, V, p.aligned4);
-      uint64_t lo = 0ull;
-      uint32_t carry = 0u;
-      Mass big = mass_zero();
-#pragma unroll
-      for (int k = 0; k < kVecs; ++k) accumulate4(lo, carry, big, v[k], &bad_prob);
-      Mass s = mass_add(Mass{lo, carry}, big);
-      s = warp_sum(s);
-      if (lane == 0) blk[b] = s;
+    // ---- full-row pass: exact mass of every 1024-token block of this slice.
+    const int buf = pass & 1;
+    Mass* mb = blk + buf * p.blocks_per_cta;
+    if (BULK) {
+      // Slot s receives blocks s, s + kSlots, ... of the slice: `fills` per
+      // pass, so the phase of its barrier for block i of pass `pass` is
+      // (pass * fills + i / kSlots) & 1.  Every slot is idle here (each
+      // earlier fill was consumed before the block-wide barrier that ended
+      // the previous pass).  Slot s is only ever awaited and refilled by
+      // warp s % kWarps, which consumes fill k before it issues fill k + 1.
+      if (tid == 0)
+        for (int s = 0; s < kSlots && s < nb; ++s) fill_slot(ring, s_full, s, row, slice_first + s, V);
+      for (int i = warp; i < nb; i += kWarps) {
+        const int s = i % kSlots;
+        const int fills = (nb - s + kSlots - 1) / kSlots;
+        const uint32_t parity = static_cast<uint32_t>(pass * fills + i / kSlots) & 1u;
+        if (!sm100::mbar_wait(&s_full[s], parity)) wait_failed = true;
+        const Mass m = slot_mass(ring + s * kBlockElems, slice_first + i, V, lane, &bad_prob);
+        if (lane == 0) mb[i] = m;
+        __syncwarp();
+        if (lane == 0 && i + kSlots < nb) {
+          sm100::fence_proxy_async_smem();  // this warp's reads of the slot precede the refill
+          fill_slot(ring, s_full, s, row, slice_first + i + kSlots, V);
+        }
+      }
+    } else {
+      for (int i = warp; i < nb; i += kWarps) {
+        const Mass m = global_mass(row, slice_first + i, V, p.aligned4, lane, &bad_prob);
+        if (lane == 0) mb[i] = m;
+      }
     }
+    ++pass;
     __syncthreads();
-    if (sparse && tid == 0) {
-      // Remove the children's mass from their blocks (exact subtraction).
-      uint32_t bad = 0u;
-      for (int c = 0; c < s_child_count; ++c) {
-        const int64_t tok = s_child_tok[c];
-        const int64_t b = tok / kBlockElems - slice_first;
-        if (b >= 0 && b < nb) {
-          const float v = __ldg(row + tok);
-          blk[b] = mass_sub(blk[b], mass_from_bits(__float_as_uint(v), &bad));
-        }
-      }
-    }
-    __syncthreads();
-    // CTA total.
-    {
-      Mass s = mass_zero();
-      for (int b = tid; b < nb; b += kThreads) s = mass_add(s, blk[b]);
-      s = warp_sum(s);
-      if (lane == 0) s_warp[warp] = s;
-      __syncthreads();
-      if (warp == 0) {
-        Mass t = (lane < kWarps) ? s_warp[lane] : mass_zero();
-        t = warp_sum(t);
-        if (lane == 0) s_cta_total = t;
-      }
-      if (tid == 0) s_selected = -1;
-    }
-    cluster.sync();
-
-    // Grand total and this CTA's exclusive prefix (identical in every CTA).
-    Mass total = mass_zero(), prefix = mass_zero(), mine = mass_zero();
-#pragma unroll
-    for (int r = 0; r < CLUSTER; ++r) {
-      const Mass* remote = cluster.map_shared_rank(&s_cta_total, r);
-      const Mass t = *remote;
-      if (r < static_cast<int>(crank)) prefix = mass_add(prefix, t);
-      if (r == static_cast<int>(crank)) mine = t;
-      total = mass_add(total, t);
-    }
-    const Mass thr = mass_scale(sparse ? u_exit : u_main, total);
-    const bool owner = !mass_is_zero(total) && !mass_lt(thr, prefix) &&
-                       mass_lt(thr, mass_add(prefix, mine));
-    if (owner) {
-      // Find the crossing block: contiguous runs of blocks per thread.
-      const Mass local = mass_sub(thr, prefix);
-      const int per = (nb + kThreads - 1) / kThreads;
-      const int b0 = min(nb, tid * per), b1 = min(nb, b0 + per);
-      Mass s = mass_zero();
-      for (int b = b0; b < b1; ++b) s = mass_add(s, blk[b]);
-      Mass incl = warp_inclusive_scan(s, lane);
-      if (lane == 31) s_warp[warp] = incl;
-      __syncthreads();
-      if (warp == 0) {
-        Mass w = (lane < kWarps) ? s_warp[lane] : mass_zero();
-        Mass wi = warp_inclusive_scan(w, lane);
-        if (lane < kWarps) s_warp[lane] = mass_sub(wi, w);  // exclusive
-      }
-      __syncthreads();
-      const Mass excl = mass_add(s_warp[warp], mass_sub(incl, s));
-      if (b0 < b1 && !mass_lt(local, excl) && mass_lt(local, mass_add(excl, s))) {
-        Mass run = excl;
-        for (int b = b0; b < b1; ++b) {
-          const Mass next = mass_add(run, blk[b]);
-          if (mass_lt(local, next)) {
-            s_cross_block = b;
-            s_cross_residual = mass_sub(local, run);
-            break;
-          }
-          run = next;
-        }
-      }
-      __syncthreads();
-      if (warp == 0) {
-        // Rescan the crossing block in index order: lane l owns tokens
-        // [first, first + 32) with first = block start + 32 l.
-        const int b = s_cross_block;
-        const Mass resid = s_cross_residual;
-        const int64_t first = (slice_first + b) * kBlockElems + lane * (kBlockElems / 32);
-        uint32_t e[kBlockElems / 32];
-#pragma unroll
-        for (int k = 0; k < kBlockElems / 128; ++k) {
-          const uint4 v = load4(row, first + k * 4, V, p.aligned4);
-          e[4 * k] = v.x;
-          e[4 * k + 1] = v.y;
-          e[4 * k + 2] = v.z;
-          e[4 * k + 3] = v.w;
-        }
+    if (sparse) {
+      if (tid == 0) {
+        // Remove the children's mass from their blocks (exact subtraction).
         uint32_t bad = 0u;
-        if (sparse) {  // children are excluded from the exit draw
-          for (int c = 0; c < s_child_count; ++c) {
-            const int64_t off = s_child_tok[c] - first;
-#pragma unroll
-            for (int k = 0; k < kBlockElems / 32; ++k)
-              if (off == k) e[k] = 0u;
-          }
-        }
-        uint64_t lo = 0ull;
-        uint32_t carry = 0u;
-        Mass big = mass_zero();
-#pragma unroll
-        for (int k = 0; k < kBlockElems / 128; ++k)
-          accumulate4(lo, carry, big, make_uint4(e[4 * k], e[4 * k + 1], e[4 * k + 2], e[4 * k + 3]), &bad);
-        const Mass lane_sum = mass_add(Mass{lo, carry}, big);
-        const Mass li = warp_inclusive_scan(lane_sum, lane);
-        Mass run = mass_sub(li, lane_sum);
-        int found = -1;
-        if (!mass_lt(resid, run) && mass_lt(resid, li)) {
-#pragma unroll
-          for (int k = 0; k < kBlockElems / 32; ++k) {
-            mass_accumulate(run, e[k], &bad);
-            if (found < 0 && mass_lt(resid, run)) found = k;
-          }
-        }
-        const unsigned who = __ballot_sync(0xffffffffu, found >= 0);
-        if (who != 0u) {
-          const int src = __ffs(who) - 1;
-          const int fk = __shfl_sync(0xffffffffu, found, src);
-          if (lane == 0) {
-            const int token = static_cast<int>((slice_first + b) * kBlockElems + src * (kBlockElems / 32) + fk);
-#pragma unroll
-            for (int r = 0; r < CLUSTER; ++r) *cluster.map_shared_rank(&s_selected, r) = token;
+        for (int c = 0; c < s_child_count; ++c) {
+          const int64_t tok = s_child_tok[c];
+          const int64_t b = tok / kBlockElems - slice_first;
+          if (b >= 0 && b < nb) {
+            const float v = __ldg(row + tok);
+            mb[b] = mass_sub(mb[b], mass_from_bits(__float_as_uint(v), &bad));
           }
         }
       }
+      __syncthreads();
     }
+    // CTA total (warp 0; at most a few dozen blocks per slice).
+    if (warp == 0) {
+      Mass s = mass_zero();
+      for (int b = lane; b < nb; b += 32) s = mass_add(s, mb[b]);
+      s = warp_sum(s);
+      if (lane == 0) s_total[buf] = s;
+    }
+    // The one cluster barrier of this node: every slice total and block mass
+    // of this pass is visible cluster-wide after it.  Buffers of parity `buf`
+    // are rewritten two passes later, after the next barrier, which no CTA
+    // passes before every CTA has finished reading them below.
     cluster.sync();
 
-    int token = s_selected;
-    if (token < 0) {
-      // Zero total (or a final boundary): reference fallbacks.
+    if (warp == 0) {
+      // Slice totals -> grand total, owning CTA, threshold inside its slice.
+      const Mass t = (lane < CLUSTER) ? *cluster.map_shared_rank(&s_total[buf], lane) : mass_zero();
+      const Mass incl = warp_inclusive_scan(t, lane);
+      const Mass total = shfl_mass(incl, CLUSTER - 1);
+      const Mass thr = mass_scale(sparse ? u_exit : u_main, total);
+      int token = -1;
+      const unsigned own = __ballot_sync(0xffffffffu, lane < CLUSTER && mass_lt(thr, incl));
+      if (!mass_is_zero(total) && own != 0u) {
+        const int owner = __ffs(own) - 1;
+        const Mass local = mass_sub(thr, shfl_mass(mass_sub(incl, t), owner));
+        // The owner's block masses (distributed shared memory): lane l sums a
+        // contiguous run, a warp scan locates the run and then the block that
+        // holds the threshold.
+        const Mass* ob = cluster.map_shared_rank(blk + buf * p.blocks_per_cta, owner);
+        const int64_t o_first = static_cast<int64_t>(owner) * p.blocks_per_cta;
+        const int o_nb = static_cast<int>(max64(0, min64(p.blocks_per_cta, nblk_total - o_first)));
+        const int per = (o_nb + 31) / 32;
+        const int b0 = min(o_nb, lane * per), b1 = min(o_nb, b0 + per);
+        Mass run_sum = mass_zero();
+        for (int b = b0; b < b1; ++b) run_sum = mass_add(run_sum, ob[b]);
+        const Mass run_incl = warp_inclusive_scan(run_sum, lane);
+        const Mass run_excl = mass_sub(run_incl, run_sum);
+        const bool mine = b0 < b1 && !mass_lt(local, run_excl) && mass_lt(local, run_incl);
+        int cb = -1;
+        Mass resid = mass_zero();
+        if (mine) {
+          Mass run = run_excl;
+          for (int b = b0; b < b1; ++b) {
+            const Mass next = mass_add(run, ob[b]);
+            if (mass_lt(local, next)) {
+              cb = b;
+              resid = mass_sub(local, run);
+              break;
+            }
+            run = next;
+          }
+        }
+        const unsigned who = __ballot_sync(0xffffffffu, mine && cb >= 0);
+        if (who != 0u) {
+          const int src_lane = __ffs(who) - 1;
+          cb = __shfl_sync(0xffffffffu, cb, src_lane);
+          resid = shfl_mass(resid, src_lane);
+          uint32_t bad = 0u;
+          token = crossing_token(row, o_first + cb, V, p.aligned4, resid, sparse, s_child_tok, s_child_count,
+                                 lane, &bad);
+        }
+      }
+      if (token < 0) {
+        // Zero total (or a final boundary): reference fallbacks.
+        if (!sparse) {
+          token = static_cast<int>(V - 1);
+        } else {
+          for (int64_t t2 = V - 1; t2 >= 0; --t2) {
+            bool is_child = false;
+            for (int c = 0; c < s_child_count; ++c) is_child = is_child || (s_child_tok[c] == t2);
+            if (!is_child) {
+              token = static_cast<int>(t2);
+              break;
+            }
+          }
+        }
+      }
+      int child = -1;
       if (!sparse) {
-        token = static_cast<int>(V - 1);
-      } else {
-        for (int64_t t = V - 1; t >= 0; --t) {
-          bool is_child = false;
-          for (int c = 0; c < s_child_count; ++c) is_child = is_child || (s_child_tok[c] == t);
-          if (!is_child) {
-            token = static_cast<int>(t);
+        // First node with (parent, token) == (cur, token).
+        for (int base = 1; base < n; base += 32) {
+          const int j = base + lane;
+          const bool hit = (j < n) && s_parent[j] == cur && s_token[j] == token;
+          const unsigned mask = __ballot_sync(0xffffffffu, hit);
+          if (mask != 0u) {
+            child = base + __ffs(mask) - 1;
             break;
           }
         }
       }
-    }
-    int child = -1;
-    if (!sparse) {
-      // First node with (parent, token) == (cur, token).
-      for (int base = 1; base < n; base += 32) {
-        const int j = base + lane;
-        const bool hit = (j < n) && s_parent[j] == cur && s_token[j] == token;
-        const unsigned mask = __ballot_sync(0xffffffffu, hit);
-        if (mask != 0u) {
-          child = base + __ffs(mask) - 1;
-          break;
-        }
+      if (lane == 0) {
+        s_sel_token = token;
+        s_sel_child = child;
       }
     }
+    __syncthreads();
+    const int token = s_sel_token;
+    const int child = s_sel_child;
     if (child >= 0 && depth < D) {
       if (crank == 0 && tid == 0) out[accepted] = child;
       ++accepted;
       cur = child;
-      __syncthreads();
       continue;
     }
     if (crank == 0 && tid == 0) {
@@ -443,6 +564,8 @@ __global__ void __launch_bounds__(kThreads, 1) accept_probs_kernel(const AcceptP
     break;
   }
   if (bad_prob) report(p.status, SG_ERR_PROBABILITY);
+  if (wait_failed) report(p.status, SG_ERR_CUDA);
+  // No CTA leaves while another may still read its shared memory.
   cluster.sync();
 }
 
@@ -488,9 +611,9 @@ __global__ void follow_kernel(const int64_t* __restrict__ posterior, const int64
   }
 }
 
-template <int CLUSTER>
+template <int CLUSTER, bool BULK>
 int launch_accept(const AcceptParams& p, size_t smem, cudaStream_t stream) {
-  auto kernel = accept_probs_kernel<CLUSTER>;
+  auto kernel = accept_probs_kernel<CLUSTER, BULK>;
   SG_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(smem)));
   cudaLaunchConfig_t cfg = {};
@@ -507,6 +630,66 @@ int launch_accept(const AcceptParams& p, size_t smem, cudaStream_t stream) {
   cfg.numAttrs = 1;
   SG_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, p));
   return check_launch("accept_probs_kernel");
+}
+
+template <bool BULK>
+int launch_accept_cluster(int cluster, const AcceptParams& p, size_t smem, cudaStream_t s) {
+  switch (cluster) {
+    case 1: return launch_accept<1, BULK>(p, smem, s);
+    case 2: return launch_accept<2, BULK>(p, smem, s);
+    case 4: return launch_accept<4, BULK>(p, smem, s);
+    default: return launch_accept<8, BULK>(p, smem, s);
+  }
+}
+
+// Resident CTAs per SM of the kernel variant for `cluster` with `smem` bytes
+// of dynamic shared memory (cached per variant and size).
+template <bool BULK>
+int resident_ctas(int cluster, size_t smem) {
+  static std::mutex mu;
+  static size_t cached_smem[kMaxCluster + 1] = {};
+  static int cached_occ[kMaxCluster + 1] = {};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (cached_smem[cluster] == smem) return cached_occ[cluster];
+  }
+  int occ = 0;
+  cudaError_t err = cudaSuccess;
+  auto query = [&](auto kernel) {
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (err == cudaSuccess) err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kThreads, smem);
+  };
+  switch (cluster) {
+    case 1: query(accept_probs_kernel<1, BULK>); break;
+    case 2: query(accept_probs_kernel<2, BULK>); break;
+    case 4: query(accept_probs_kernel<4, BULK>); break;
+    default: query(accept_probs_kernel<8, BULK>); break;
+  }
+  if (err != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cached_smem[cluster] = smem;
+  cached_occ[cluster] = occ;
+  return occ;
+}
+
+size_t accept_smem(int cluster, int64_t nblk, int32_t max_nodes, bool bulk) {
+  const int64_t per_cta = (nblk + cluster - 1) / cluster;
+  return (bulk ? static_cast<size_t>(kSlots) * kBlockBytes : 0) + static_cast<size_t>(per_cta) * 2 * sizeof(Mass) +
+         static_cast<size_t>(max_nodes) * 8;
+}
+
+// SG_ACCEPT_CLUSTER=1|2|4|8 fixes the cluster size (launch-shape sweeps).
+int accept_cluster_override() {
+  static const int value = [] {
+    const char* env = std::getenv("SG_ACCEPT_CLUSTER");
+    if (env == nullptr) return 0;
+    const int v = std::atoi(env);
+    return (v == 1 || v == 2 || v == 4 || v == 8) ? v : 0;
+  }();
+  return value;
 }
 
 }  // namespace
@@ -535,8 +718,6 @@ extern "C" int sg_tree_accept_probs(const float* probs, int64_t vocab, const int
   }
   const int sms = device_sm_count();
   if (sms <= 0) return fail(SG_ERR_CUDA, "sg_tree_accept_probs: no CUDA device");
-  int cluster = 1;
-  while (cluster < 8 && static_cast<int64_t>(num_trees) * cluster * 2 <= sms) cluster *= 2;
   const int64_t nblk = (vocab + kBlockElems - 1) / kBlockElems;
   AcceptParams p;
   p.probs = probs;
@@ -555,21 +736,36 @@ extern "C" int sg_tree_accept_probs(const float* probs, int64_t vocab, const int
   p.out = out;
   p.status = status;
   p.aligned4 = (vocab % 4 == 0) && (reinterpret_cast<uintptr_t>(probs) % 16 == 0);
-  size_t smem = 0;
-  for (;;) {
-    p.blocks_per_cta = static_cast<int32_t>((nblk + cluster - 1) / cluster);
-    smem = static_cast<size_t>(p.blocks_per_cta) * sizeof(Mass) + static_cast<size_t>(max_nodes) * 8;
-    if (smem <= 160 * 1024 || cluster == 8) break;
+  const bool bulk = p.aligned4;
+  // Cluster size: the largest power of two up to 8 (and up to the number of
+  // blocks in a row) for which every tree's cluster is resident at once, so
+  // that a visited row is split over as many SMs as the batch allows.
+  int cluster = 1;
+  const int forced = accept_cluster_override();
+  if (forced > 0) {
+    cluster = forced;
+  } else {
+    for (int c = kMaxCluster; c >= 1; c >>= 1) {
+      if (c > 1 && c > nblk) continue;
+      const size_t sm = accept_smem(c, nblk, max_nodes, bulk);
+      if (sm > 200 * 1024) break;  // smaller clusters need even more
+      const int occ = bulk ? resident_ctas<true>(c, sm) : resident_ctas<false>(c, sm);
+      if (c == 1 || static_cast<int64_t>(num_trees) * c <= static_cast<int64_t>(sms) * occ) {
+        cluster = c;
+        break;
+      }
+    }
+  }
+  // Large vocabularies need more CTAs per row to fit the block masses.
+  size_t smem = accept_smem(cluster, nblk, max_nodes, bulk);
+  while (smem > 200 * 1024 && cluster < kMaxCluster) {
     cluster *= 2;
+    smem = accept_smem(cluster, nblk, max_nodes, bulk);
   }
-  if (smem > 200 * 1024) return fail(SG_ERR_UNSUPPORTED, "sg_tree_accept_probs: vocabulary too large");
+  if (smem > 200 * 1024) return fail(SG_ERR_UNSUPPORTED, "sg_tree_accept_probs: vocabulary or tree too large");
+  p.blocks_per_cta = static_cast<int32_t>((nblk + cluster - 1) / cluster);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (cluster) {
-    case 1: return launch_accept<1>(p, smem, s);
-    case 2: return launch_accept<2>(p, smem, s);
-    case 4: return launch_accept<4>(p, smem, s);
-    default: return launch_accept<8>(p, smem, s);
-  }
+  return bulk ? launch_accept_cluster<true>(cluster, p, smem, s) : launch_accept_cluster<false>(cluster, p, smem, s);
 }
 
 extern "C" int sg_tree_follow(const int64_t* posterior, const int64_t* row_offsets, const int64_t* parents,

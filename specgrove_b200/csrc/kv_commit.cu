@@ -139,24 +139,36 @@ namespace {
 constexpr int kMaxKeep = 64;
 constexpr int kAcceptedThreads = 256;
 
-// One thread per (tree, plane, 16- or 4-byte column).  Kept row r of a tree
-// is node out[r-1] of its tree (row 0, the root, is node 0), which the verify
-// pass wrote at len + node; it moves to len + r.  Nodes on the accepted path
-// increase with depth, so node_r >= r: walking r upward, a thread never
-// overwrites a row it still has to read (a destination len + r equal to a
-// later source len + node_r' would need node_r' = r < r'), and no staging is
-// needed.  Rows already in place (node_r == r, always the root) are skipped.
+constexpr int kCopyChunk = 4;     // rows a thread loads before it stores them
+constexpr int kColsPerThread = 4; // 16- or 4-byte columns per thread
+
+// One thread per (tree, kColsPerThread columns of the plane space), so one
+// tree needs only a few CTAs and a whole wave fits on the GPU.  Kept row r of
+// a tree is node out[r-1] of its tree (row 0, the root, is node 0), which
+// the verify pass wrote at len + node; it moves to len + r.  The CTA stages
+// the tree's path in shared memory and checks it once (node_r >= r, inside
+// the slot's tail) before anything moves, so a bad path changes nothing.  A
+// thread then copies its columns kCopyChunk rows at a time: all loads of a
+// chunk are issued before its stores, so the row reads overlap.  In place
+// this is safe because node_r >= r: a chunk writes rows below the first row
+// of the next chunk, whose sources node_r' >= r' lie above them, and within a
+// chunk every source is read before any destination is written.  Rows
+// already in place (node_r == r, always the root) are skipped.
 __global__ void __launch_bounds__(kAcceptedThreads)
 kv_commit_accepted_kernel(unsigned char* arena, int64_t plane_rows, int64_t num_planes, int64_t row_bytes,
                           int64_t capacity, const int64_t* __restrict__ slots,
                           const int64_t* __restrict__ lengths_in, int64_t* __restrict__ lengths_out,
                           const int64_t* __restrict__ accept_out, int32_t max_depth, bool vec16,
                           int32_t* status) {
+  __shared__ int s_node[kMaxKeep];
+  __shared__ int s_bad;
   const int t = blockIdx.y;
   const int64_t* out = accept_out + static_cast<int64_t>(t) * (max_depth + 2);
   const int64_t slot = slots[t];
   const int64_t len = lengths_in[t];
   const int64_t count = out[max_depth];
+  // path nodes, loaded alongside the count (validated below)
+  const int64_t node_raw = (threadIdx.x < kMaxKeep - 1 && threadIdx.x < max_depth) ? out[threadIdx.x] : 0;
   int kept = static_cast<int>(count) + 1;
   const bool ok = count >= 0 && count <= max_depth && kept <= kMaxKeep && len >= 0 && len + kept <= capacity &&
                   slot >= 0 && (slot + 1) * capacity <= plane_rows;
@@ -166,24 +178,71 @@ kv_commit_accepted_kernel(unsigned char* arena, int64_t plane_rows, int64_t num_
     lengths_out[t] = len + kept;
   }
   if (kept <= 1) return;
+  if (threadIdx.x == 0) s_bad = 0;
+  __syncthreads();
+  if (threadIdx.x < kept - 1) {
+    const int r = threadIdx.x + 1;
+    const bool good = node_raw >= r && len + node_raw < capacity;  // a root path in this slot's tail
+    s_node[r - 1] = good ? static_cast<int>(node_raw) : r;
+    if (!good) s_bad = 1;
+  }
+  __syncthreads();
+  if (s_bad) {
+    if (blockIdx.x == 0 && threadIdx.x == 0 && status != nullptr)
+      atomicMax(status, static_cast<int32_t>(SG_ERR_TREE));
+    return;
+  }
   const int unit = vec16 ? 16 : 4;
   const int64_t units_per_row = row_bytes / unit;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * kAcceptedThreads + threadIdx.x;
-  if (i >= num_planes * units_per_row) return;
-  const int64_t plane = i / units_per_row;
-  const int64_t u = i % units_per_row;
-  unsigned char* col = arena + (plane * plane_rows + slot * capacity + len) * row_bytes + u * unit;
-  for (int r = 1; r < kept; ++r) {
-    const int64_t node = out[r - 1];
-    if (node == r) continue;
-    if (node < r || len + node >= capacity) {  // not a root path in this slot's tail
-      if (status != nullptr) atomicMax(status, static_cast<int32_t>(SG_ERR_TREE));
-      return;
+  const int64_t columns = num_planes * units_per_row;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kAcceptedThreads;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kAcceptedThreads + threadIdx.x;
+  unsigned char* colp[kColsPerThread];
+#pragma unroll
+  for (int j = 0; j < kColsPerThread; ++j) {
+    const int64_t c = c0 + j * stride;
+    const int64_t plane = c / units_per_row;
+    const int64_t u = c % units_per_row;
+    colp[j] = (c < columns) ? arena + (plane * plane_rows + slot * capacity + len) * row_bytes + u * unit : nullptr;
+  }
+  for (int r0 = 1; r0 < kept; r0 += kCopyChunk) {
+    if (vec16) {
+      uint4 v[kColsPerThread][kCopyChunk];
+#pragma unroll
+      for (int j = 0; j < kColsPerThread; ++j)
+#pragma unroll
+        for (int k = 0; k < kCopyChunk; ++k) {
+          const int r = r0 + k;
+          if (colp[j] != nullptr && r < kept && s_node[r - 1] != r)
+            v[j][k] = *reinterpret_cast<const uint4*>(colp[j] + static_cast<int64_t>(s_node[r - 1]) * row_bytes);
+        }
+#pragma unroll
+      for (int j = 0; j < kColsPerThread; ++j)
+#pragma unroll
+        for (int k = 0; k < kCopyChunk; ++k) {
+          const int r = r0 + k;
+          if (colp[j] != nullptr && r < kept && s_node[r - 1] != r)
+            *reinterpret_cast<uint4*>(colp[j] + r * row_bytes) = v[j][k];
+        }
+    } else {
+      uint32_t v[kColsPerThread][kCopyChunk];
+#pragma unroll
+      for (int j = 0; j < kColsPerThread; ++j)
+#pragma unroll
+        for (int k = 0; k < kCopyChunk; ++k) {
+          const int r = r0 + k;
+          if (colp[j] != nullptr && r < kept && s_node[r - 1] != r)
+            v[j][k] = *reinterpret_cast<const uint32_t*>(colp[j] + static_cast<int64_t>(s_node[r - 1]) * row_bytes);
+        }
+#pragma unroll
+      for (int j = 0; j < kColsPerThread; ++j)
+#pragma unroll
+        for (int k = 0; k < kCopyChunk; ++k) {
+          const int r = r0 + k;
+          if (colp[j] != nullptr && r < kept && s_node[r - 1] != r)
+            *reinterpret_cast<uint32_t*>(colp[j] + r * row_bytes) = v[j][k];
+        }
     }
-    if (vec16)
-      *reinterpret_cast<uint4*>(col + r * row_bytes) = *reinterpret_cast<const uint4*>(col + node * row_bytes);
-    else
-      *reinterpret_cast<uint32_t*>(col + r * row_bytes) = *reinterpret_cast<const uint32_t*>(col + node * row_bytes);
   }
 }
 
@@ -208,7 +267,8 @@ extern "C" int sg_kv_commit_accepted(void* arena, int64_t plane_rows, int64_t nu
     return fail(SG_ERR_UNSUPPORTED, "sg_kv_commit_accepted: max_depth above 63");
   const bool vec16 = (row_bytes % 16 == 0) && (reinterpret_cast<uintptr_t>(arena) % 16 == 0);
   const int64_t columns = num_planes * (row_bytes / (vec16 ? 16 : 4));
-  const int64_t grid_x = (columns + kAcceptedThreads - 1) / kAcceptedThreads;
+  const int64_t per_cta = static_cast<int64_t>(kAcceptedThreads) * kColsPerThread;
+  const int64_t grid_x = (columns + per_cta - 1) / per_cta;
   if (grid_x > 0x7fffffff || num_trees > 65535)
     return fail(SG_ERR_UNSUPPORTED, "sg_kv_commit_accepted: more than 65535 trees or too many columns");
   dim3 grid(static_cast<unsigned>(grid_x), static_cast<unsigned>(num_trees), 1);
