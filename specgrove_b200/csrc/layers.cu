@@ -140,10 +140,24 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ 
   const int row = blockIdx.x;
   const float4* xr = reinterpret_cast<const float4*>(x + static_cast<int64_t>(row) * hidden);
   const int n4 = hidden / 4;
+  // Rows of up to kKeep float4 per thread stay in registers between the sum of
+  // squares and the scaling, so the row is read once.
+  constexpr int kKeep = 8;
+  const bool keep = n4 <= kKeep * static_cast<int>(blockDim.x);
+  float4 kept[kKeep];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
-    const float4 v = xr[i];
-    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  if (keep) {
+#pragma unroll
+    for (int k = 0; k < kKeep; ++k) {
+      const int i = threadIdx.x + k * blockDim.x;
+      kept[k] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      ss += kept[k].x * kept[k].x + kept[k].y * kept[k].y + kept[k].z * kept[k].z + kept[k].w * kept[k].w;
+    }
+  } else {
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+      const float4 v = xr[i];
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
   }
   __shared__ float red[8];
 #pragma unroll
@@ -160,8 +174,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ 
   const float rstd = rsqrtf(red[0] / static_cast<float>(hidden) + eps);
   const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(w);
   uint2* o = reinterpret_cast<uint2*>(out + static_cast<int64_t>(row) * hidden);
-  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
-    const float4 v = xr[i];
+  auto scale = [&](int i, float4 v) {
     const float2 wa = __bfloat1622float2(w2[2 * i]);
     const float2 wb = __bfloat1622float2(w2[2 * i + 1]);
     __nv_bfloat162 a = __floats2bfloat162_rn(v.x * rstd * wa.x, v.y * rstd * wa.y);
@@ -170,6 +183,15 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ 
     packed.x = *reinterpret_cast<uint32_t*>(&a);
     packed.y = *reinterpret_cast<uint32_t*>(&b);
     o[i] = packed;
+  };
+  if (keep) {
+#pragma unroll
+    for (int k = 0; k < kKeep; ++k) {
+      const int i = threadIdx.x + k * blockDim.x;
+      if (i < n4) scale(i, kept[k]);
+    }
+  } else {
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) scale(i, xr[i]);
   }
 }
 
@@ -238,6 +260,112 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(const QkvPost p) {
   }
 #pragma unroll
   for (int i = 0; i < PER; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(v[i]);
+}
+
+// The same operation with one CTA per packed row.  The row's D/2 rotary
+// angles (cos, sin) and both norm weight vectors are staged in shared memory
+// once, so the angles are not recomputed for each of the row's heads.  A
+// group of D/8 threads owns one head, each thread 8 consecutive dims moved as
+// 16-byte vectors; the rotary partner of dim d (< D/2) is dim d + D/2, held
+// by the thread D/16 lanes away in the same group, and the norm's sum of
+// squares is reduced inside the group.  Every lane takes every shuffle (value
+// heads and idle lanes compute and then discard), so control flow stays
+// uniform across a warp whose groups hold different head types.
+template <int D>
+__global__ void __launch_bounds__(256) qkv_post_row_kernel(const QkvPost p) {
+  constexpr int G = D / 8;      // threads per head
+  constexpr int HALF_G = G / 2; // partner distance in lanes
+  constexpr int HALF = D / 2;
+  pdl_trigger();
+  __shared__ float s_cos[HALF], s_sin[HALF], s_qw[D], s_kw[D];
+  __shared__ int64_t s_arena_row;
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  for (int i = tid; i < D; i += blockDim.x) {  // weights are not produced by a predecessor
+    s_qw[i] = __bfloat162float(p.q_norm[i]);
+    s_kw[i] = __bfloat162float(p.k_norm[i]);
+  }
+  pdl_wait();
+  if (tid < HALF) {
+    const float angle = static_cast<float>(p.position[row]) * p.inv_freq[tid];
+    float sn, cs;
+    sincosf(angle, &sn, &cs);
+    s_cos[tid] = cs;
+    s_sin[tid] = sn;
+  }
+  if (tid == 0) {
+    int64_t ar = -1;  // -1: row of a rejected tree, no K/V write
+    const int t = p.tree[row];
+    if (t >= 0) {
+      const int64_t a = p.slots[t] * p.capacity + p.cache_len[t] + p.local[row];
+      if (a < 0 || a >= p.plane_rows || p.cache_len[t] + p.local[row] >= p.capacity) {
+        report(p.status, SG_ERR_CAPACITY);
+      } else {
+        ar = a;
+      }
+    }
+    s_arena_row = ar;
+  }
+  __syncthreads();
+  const int heads = p.nq + 2 * p.nkv;
+  const int64_t arena_row = s_arena_row;
+  const int j = tid % G;            // 8-dim chunk of the head
+  const bool high = j >= HALF_G;    // dims >= D/2
+  const int d0 = 8 * j;
+  const int dl = 8 * (j % HALF_G);  // angle index of this chunk's dims
+  const int iters = (heads * G + static_cast<int>(blockDim.x) - 1) / static_cast<int>(blockDim.x);
+  for (int it = 0; it < iters; ++it) {
+    const int head = (it * static_cast<int>(blockDim.x) + tid) / G;
+    const bool valid = head < heads;
+    float v[8];
+    if (valid) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(p.qkv + static_cast<int64_t>(row) * heads * D +
+                                                        static_cast<int64_t>(head) * D + d0);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h2[e]);
+        v[2 * e] = f.x;
+        v[2 * e + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = 0.f;
+    }
+    const bool is_q = head < p.nq;
+    const bool is_k = !is_q && head < p.nq + p.nkv;
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+#pragma unroll
+    for (int d = HALF_G; d >= 1; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
+    const float rstd = rsqrtf(ss / static_cast<float>(D) + p.eps);
+    const float* w = is_q ? s_qw : s_kw;
+    float r[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float x = v[e] * rstd * w[d0 + e];
+      const float partner = __shfl_xor_sync(0xffffffffu, x, HALF_G);
+      const float c = s_cos[dl + e], sn = s_sin[dl + e];
+      // rotate_half: out_d = x_d cos - x_{d+H} sin,  out_{d+H} = x_{d+H} cos + x_d sin
+      r[e] = high ? x * c + partner * sn : x * c - partner * sn;
+    }
+    if (!valid) continue;
+    const bool qk = is_q || is_k;
+    uint4 packed;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&packed);
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      o2[e] = __floats2bfloat162_rn(qk ? r[2 * e] : v[2 * e], qk ? r[2 * e + 1] : v[2 * e + 1]);
+    if (is_q) {
+      *reinterpret_cast<uint4*>(p.q_out + static_cast<int64_t>(row) * p.nq * D + static_cast<int64_t>(head) * D +
+                                d0) = packed;
+    } else if (arena_row >= 0) {
+      const int kvh = is_k ? head - p.nq : head - p.nq - p.nkv;
+      __nv_bfloat16* plane = (is_k ? p.k_plane0 : p.v_plane0) + static_cast<int64_t>(kvh) * p.plane_stride;
+      *reinterpret_cast<uint4*>(plane + arena_row * D + d0) = packed;
+    }
+  }
 }
 
 // lse and Gumbel-max token of every row from the per-vocab-tile partials
@@ -354,6 +482,13 @@ int launch_rmsnorm(const float* x, const __nv_bfloat16* weight, int hidden, int 
 
 int launch_qkv_post(const QkvPost& p, cudaStream_t stream) {
   if (p.rows <= 0) return SG_OK;
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  const bool vec = a16(p.qkv) && a16(p.q_out) && a16(p.k_plane0) && a16(p.v_plane0) &&
+                   (p.plane_stride * 2) % 16 == 0;
+  if (vec && p.head_dim == 128)
+    return launch_pdl("qkv_post_row_kernel", qkv_post_row_kernel<128>, dim3(p.rows), dim3(256), 0, stream, p);
+  if (vec && p.head_dim == 64)
+    return launch_pdl("qkv_post_row_kernel", qkv_post_row_kernel<64>, dim3(p.rows), dim3(256), 0, stream, p);
   const int64_t warps = static_cast<int64_t>(p.rows) * (p.nq + 2 * p.nkv);
   const unsigned grid = static_cast<unsigned>((warps + 7) / 8);
   if (p.head_dim == 128)
