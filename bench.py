@@ -47,6 +47,9 @@ NCU_ATTENTION_TRAFFIC_CFG4 = 736.310016e6 + 15.491584e6
 # Same for one gate/up + SwiGLU GEMM launch on the configuration-4 rows
 # (dram__bytes_read.sum 218.2 MB + dram__bytes_write.sum 41.1 MB).
 NCU_SWIGLU_TRAFFIC_CFG4 = 218.232576e6 + 41.149184e6
+# Same for one acceptance launch of the configuration-2 sweep
+# (dram__bytes_read.sum 53.6 MB + dram__bytes_write.sum 0.81 MB).
+NCU_ACCEPT_TRAFFIC_CFG2 = 53.622528e6 + 0.811264e6
 
 
 def peaks():
@@ -515,7 +518,8 @@ def run_b200(args, world, rank):
                          "(acceptance + commit), flush excluded",
                    "ms_per_step_with_flush": ms_with_flush},
         "roofline": {"bound": "hbm", "kernel": "accept_probs_kernel", "achieved": accept_gbs, "peak": hbm,
-                     "peak_kind": peak_kind, "unit": "GB/s", "frac": accept_gbs / hbm, "traffic": None,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": accept_gbs / hbm,
+                     "traffic": NCU_ACCEPT_TRAFFIC_CFG2,
                      "algorithmic_bytes_per_launch": accept_bytes,
                      "launch_ms": statistics.mean(accept_ms),
                      "commit": {"achieved": commit_gbs, "frac": commit_gbs / hbm,
