@@ -53,6 +53,10 @@ struct Engine {
   layers::RowMeta meta;
   layers::AttentionWork work;
   int vocab_tiles;
+  // Stream-K workspace for GEMMs with fewer tiles than SMs (small waves):
+  // their k-blocks are spread over up to twice as many CTAs.
+  gemm::SplitWorkspace split = {nullptr, nullptr, 0};
+  int sms = 0;
 };
 
 template <typename T>
@@ -75,7 +79,7 @@ int attention_item_capacity(const sg_model_desc& m, int rows) {
   return m.num_kv_heads * ((rows * G + 127) / 128 + rows);
 }
 
-size_t workspace_size(const sg_model_desc& m, int rows) {
+size_t workspace_size(const sg_model_desc& m, int rows, int sms) {
   const size_t H = m.hidden, D = m.head_dim, I = m.intermediate;
   const size_t qkv = (m.num_q_heads + 2 * m.num_kv_heads) * D;
   const size_t vt = (m.vocab + gemm::BN - 1) / gemm::BN;
@@ -95,6 +99,8 @@ size_t workspace_size(const sg_model_desc& m, int rows) {
   s += rows * 4 + 256;                        // attention order (R <= rows)
   s += attention_item_capacity(m, rows) * 4 + 256;  // attention work list
   s += (m.num_layers + 1) * 4 + 256;          // item count, per-layer work counters
+  s += gemm::split_partial_bytes(sms) + 256;  // stream-K partial accumulators
+  s += gemm::split_partial_tiles(sms) * sizeof(int) + 256;  // stream-K flags
   return s + 4096;
 }
 
@@ -163,7 +169,9 @@ extern "C" int sg_engine_create(const sg_model_desc* model, const sg_arena_desc*
       return st;
   }
 
-  e->workspace_bytes = workspace_size(m, max_rows);
+  e->sms = device_sm_count();
+  if (e->sms <= 0) return fail(SG_ERR_CUDA, "sg_engine_create: no CUDA device");
+  e->workspace_bytes = workspace_size(m, max_rows, e->sms);
   SG_CUDA_CHECK(cudaMalloc(&e->workspace, e->workspace_bytes));
   uint8_t* cur = static_cast<uint8_t*>(e->workspace);
   e->x = carve<float>(cur, static_cast<size_t>(max_rows) * H);
@@ -187,9 +195,17 @@ extern "C" int sg_engine_create(const sg_model_desc* model, const sg_arena_desc*
   e->work.items = carve<int32_t>(cur, e->work.item_capacity);
   e->work.num_items = carve<int32_t>(cur, 1);
   e->work.counters = carve<int32_t>(cur, m.num_layers);
+  e->split.partial_tiles = gemm::split_partial_tiles(e->sms);
+  e->split.partials = carve<float>(cur, e->split.partial_tiles * gemm::BM * gemm::BN);
+  e->split.flags = carve<int>(cur, e->split.partial_tiles);
   if (static_cast<size_t>(cur - static_cast<uint8_t*>(e->workspace)) > e->workspace_bytes) {
     cudaFree(e->workspace);
     return fail(SG_ERR_WORKSPACE, "sg_engine_create: workspace layout overflow");
+  }
+  // Split flags start at zero; every split GEMM leaves them at zero.
+  if (cudaMemset(e->split.flags, 0, e->split.partial_tiles * sizeof(int)) != cudaSuccess) {
+    cudaFree(e->workspace);
+    return fail(SG_ERR_CUDA, "sg_engine_create: cudaMemset of the split flags failed");
   }
   if ((st = make_tmap_2d_bf16(&e->xn_map, e->xn, H, max_rows, H * 2, gemm::BK, gemm::BM)) != SG_OK) return st;
   if ((st = make_tmap_2d_bf16(&e->attn_map, e->attn, qw, max_rows, qw * 2, gemm::BK, gemm::BM)) != SG_OK) return st;
@@ -256,6 +272,12 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
   const gemm::Shape s_o = gemm::make_shape(Q, H, qw);
   const gemm::Shape s_gu = gemm::make_shape(Q, 2 * I, H);
   const gemm::Shape s_down = gemm::make_shape(Q, H, I);
+  // Shapes with at most half a wave of tiles (few packed rows) give each
+  // tile's k-blocks to two CTAs; everything else runs whole tiles, which
+  // measured faster (a tile split across CTA runs makes its owner wait).
+  auto small_wave = [&](const gemm::Shape& sh) -> const gemm::SplitWorkspace* {
+    return 2 * sh.tiles <= e->sms ? &e->split : nullptr;
+  };
   for (int l = 0; l < m.num_layers; ++l) {
     const void* const* lw = &e->layer_ptrs[static_cast<size_t>(l) * W_COUNT];
     const LayerMaps& lm = e->maps[l];
@@ -267,7 +289,7 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
       return st;
     if (l == 0) trace(w, 2, stream);
     gemm::EpiStoreBf16::Params pq{e->qkv, qkv_n, w.status};
-    if ((st = gemm::launch<gemm::EpiStoreBf16>(e->xn_map, lm.qkv, s_qkv, pq, stream)) != SG_OK) return st;
+    if ((st = gemm::launch<gemm::EpiStoreBf16>(e->xn_map, lm.qkv, s_qkv, pq, stream, small_wave(s_qkv))) != SG_OK) return st;
     if (l == 0) trace(w, 3, stream);
 
     layers::QkvPost qp;
@@ -322,17 +344,17 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
     if (l == 0) trace(w, 5, stream);
 
     gemm::EpiResidual::Params po{e->x, H, nullptr, 0, w.status};
-    if ((st = gemm::launch<gemm::EpiResidual>(e->attn_map, lm.o, s_o, po, stream)) != SG_OK) return st;
+    if ((st = gemm::launch<gemm::EpiResidual>(e->attn_map, lm.o, s_o, po, stream, small_wave(s_o))) != SG_OK) return st;
     if (l == 0) trace(w, 6, stream);
     if ((st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(lw[W_POST_NORM]), H, Q, m.rms_eps,
                                      e->xn, stream)) != SG_OK)
       return st;
     if (l == 0) trace(w, 7, stream);
     gemm::EpiSwiGlu::Params pg{e->h, I, w.status};
-    if ((st = gemm::launch<gemm::EpiSwiGlu>(e->xn_map, lm.gate_up, s_gu, pg, stream)) != SG_OK) return st;
+    if ((st = gemm::launch<gemm::EpiSwiGlu>(e->xn_map, lm.gate_up, s_gu, pg, stream, small_wave(s_gu))) != SG_OK) return st;
     if (l == 0) trace(w, 8, stream);
     gemm::EpiResidual::Params pd{e->x, H, nullptr, 0, w.status};
-    if ((st = gemm::launch<gemm::EpiResidual>(e->h_map, lm.down, s_down, pd, stream)) != SG_OK) return st;
+    if ((st = gemm::launch<gemm::EpiResidual>(e->h_map, lm.down, s_down, pd, stream, small_wave(s_down))) != SG_OK) return st;
     if (l == 0) trace(w, 9, stream);
   }
   trace(w, 10, stream);
