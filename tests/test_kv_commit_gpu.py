@@ -128,3 +128,35 @@ def test_commit_from_accept_output_matches_oracle(cuda_lib):
     assert int(status) == 0
     np.testing.assert_array_equal(arena.storage.view(torch.int16).cpu().numpy().reshape(expected.shape), expected)
     assert len_out.cpu().tolist() == [int(l) + len(k) for l, k in zip(lengths, keeps)]
+
+
+def test_commit_rejects_a_non_root_path_without_moving_rows(cuda_lib):
+    """A path whose node at depth r lies below r (not a root path of the
+    slot's tail) is reported as SG_ERR_TREE and leaves that tree's rows as
+    they were; the other trees of the launch commit normally."""
+    from specgrove_b200 import _lib
+    from specgrove_b200._lib import SG_ERR_TREE, ptr, stream_ptr
+    layers, heads, dim, slots, cap, D = 2, 4, 128, 4, 64, 4
+    arena = PersistentKVArena(layers, heads, dim, slots, cap, dtype=torch.bfloat16)
+    arena.storage.copy_(torch.randn(arena.storage.shape, dtype=torch.bfloat16, device="cuda"))
+    before = arena.storage.view(torch.int16).cpu().numpy().reshape(layers * 2 * heads, slots * cap, dim).copy()
+    out = np.full((2, D + 2), -1, np.int64)
+    out[0, :3] = [3, 1, 5]          # depth 2 holds node 1 < 2: not a root path
+    out[0, D], out[0, D + 1] = 3, 9
+    out[1, :2] = [2, 4]             # a valid path in slot 1
+    out[1, D], out[1, D + 1] = 2, 9
+    lengths = np.array([10, 20], np.int64)
+    expected = before.copy()
+    base = 1 * cap + 20
+    oracle.kv_commit(expected, expected, [base + r for r in (0, 2, 4)], [base + i for i in range(3)])
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int64)).cuda()
+    len_out = torch.empty(2, dtype=torch.long, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st = _lib.load().sg_kv_commit_accepted(
+        ptr(arena.storage), arena.plane_rows, arena.num_planes, arena.row_bytes, cap, ptr(dev([0, 1])),
+        ptr(dev(lengths)), ptr(len_out), ptr(dev(out)), 2, D, ptr(status), stream_ptr())
+    assert st == 0
+    torch.cuda.synchronize()
+    assert int(status) == SG_ERR_TREE
+    got = arena.storage.view(torch.int16).cpu().numpy().reshape(expected.shape)
+    np.testing.assert_array_equal(got, expected)
