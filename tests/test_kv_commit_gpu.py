@@ -150,11 +150,13 @@ def test_commit_rejects_a_non_root_path_without_moving_rows(cuda_lib):
     base = 1 * cap + 20
     oracle.kv_commit(expected, expected, [base + r for r in (0, 2, 4)], [base + i for i in range(3)])
     dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.int64)).cuda()
+    # device arrays stay bound until the kernel has run
+    slots_d, len_in, out_d = dev([0, 1]), dev(lengths), dev(out)
     len_out = torch.empty(2, dtype=torch.long, device="cuda")
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     st = _lib.load().sg_kv_commit_accepted(
-        ptr(arena.storage), arena.plane_rows, arena.num_planes, arena.row_bytes, cap, ptr(dev([0, 1])),
-        ptr(dev(lengths)), ptr(len_out), ptr(dev(out)), 2, D, ptr(status), stream_ptr())
+        ptr(arena.storage), arena.plane_rows, arena.num_planes, arena.row_bytes, cap, ptr(slots_d),
+        ptr(len_in), ptr(len_out), ptr(out_d), 2, D, ptr(status), stream_ptr())
     assert st == 0
     torch.cuda.synchronize()
     assert int(status) == SG_ERR_TREE
