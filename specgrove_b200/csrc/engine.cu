@@ -97,6 +97,8 @@ size_t workspace_size(const sg_model_desc& m, int rows, int sms) {
   s += rows * 4 * 3 + 3 * 256;                // position, tree, local
   s += rows * 8 + 256;                        // request id
   s += rows * 4 + 256;                        // attention order (R <= rows)
+  s += rows * (D / 2) * 8 + 256;              // per-pass rotary table (cos, sin)
+  s += rows * 8 + 256;                        // per-pass K/V arena row
   s += attention_item_capacity(m, rows) * 4 + 256;  // attention work list
   s += (m.num_layers + 1) * 4 + 256;          // item count, per-layer work counters
   s += gemm::split_partial_bytes(sms) + 256;  // stream-K partial accumulators
@@ -190,6 +192,8 @@ extern "C" int sg_engine_create(const sg_model_desc* model, const sg_arena_desc*
   e->meta.local = carve<int32_t>(cur, max_rows);
   e->meta.request_id = carve<int64_t>(cur, max_rows);
   e->meta.order = carve<int32_t>(cur, max_rows);
+  e->meta.rope = carve<float2>(cur, static_cast<size_t>(max_rows) * (D / 2));
+  e->meta.arena_row = carve<int64_t>(cur, max_rows);
   e->work.order = e->meta.order;
   e->work.item_capacity = attention_item_capacity(m, max_rows);
   e->work.items = carve<int32_t>(cur, e->work.item_capacity);
@@ -260,6 +264,9 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
   if ((st = layers::launch_tree_meta(w.row_offsets, w.parents, w.position_base, w.request_ids, R, Q, e->meta, w.status,
                                      stream)) != SG_OK)
     return st;
+  if ((st = layers::launch_row_rope(e->meta, m.inv_freq, D, Q, w.slots, w.cache_lengths, e->arena.capacity,
+                                    plane_rows, w.status, stream)) != SG_OK)
+    return st;
   if ((st = layers::launch_embed(w.tokens, static_cast<const __nv_bfloat16*>(m.embed), m.vocab, H, Q, e->x, w.status,
                                  stream)) != SG_OK)
     return st;
@@ -308,6 +315,8 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
     qp.plane_stride = plane_stride;
     qp.capacity = e->arena.capacity;
     qp.plane_rows = plane_rows;
+    qp.rope = e->meta.rope;
+    qp.arena_row = e->meta.arena_row;
     qp.nq = nq;
     qp.nkv = nkv;
     qp.head_dim = D;

@@ -262,57 +262,75 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(const QkvPost p) {
   for (int i = 0; i < PER; ++i) dst[lane + 32 * i] = __float2bfloat16_rn(v[i]);
 }
 
-// The same operation with one CTA per packed row.  The row's D/2 rotary
-// angles (cos, sin) and both norm weight vectors are staged in shared memory
-// once, so the angles are not recomputed for each of the row's heads.  A
-// group of D/8 threads owns one head, each thread 8 consecutive dims moved as
-// 16-byte vectors; the rotary partner of dim d (< D/2) is dim d + D/2, held
-// by the thread D/16 lanes away in the same group, and the norm's sum of
-// squares is reduced inside the group.  Every lane takes every shuffle (value
-// heads and idle lanes compute and then discard), so control flow stays
-// uniform across a warp whose groups hold different head types.
+// Rotary table and K/V arena row of every packed row, once per pass (the
+// angles and the arena row do not change from layer to layer).  One CTA of
+// D/2 threads per row; thread 0 also resolves the row's arena row, -1 for a
+// row of a rejected tree or one that would overflow its slot (reported).
+__global__ void row_rope_kernel(const int32_t* __restrict__ position, const int32_t* __restrict__ tree,
+                                const int32_t* __restrict__ local, const float* __restrict__ inv_freq,
+                                const int64_t* __restrict__ slots, const int64_t* __restrict__ cache_len,
+                                int64_t capacity, int64_t plane_rows, int half, float2* __restrict__ rope,
+                                int64_t* __restrict__ arena_row, int32_t* status) {
+  const int row = blockIdx.x;
+  const int d = threadIdx.x;
+  if (d < half) {
+    const float angle = static_cast<float>(position[row]) * inv_freq[d];
+    float sn, cs;
+    sincosf(angle, &sn, &cs);
+    rope[static_cast<int64_t>(row) * half + d] = make_float2(cs, sn);
+  }
+  if (d == 0) {
+    int64_t ar = -1;
+    const int t = tree[row];
+    if (t >= 0) {
+      const int64_t a = slots[t] * capacity + cache_len[t] + local[row];
+      if (a < 0 || a >= plane_rows || cache_len[t] + local[row] >= capacity)
+        report(status, SG_ERR_CAPACITY);
+      else
+        ar = a;
+    }
+    arena_row[row] = ar;
+  }
+}
+
+// The same operation as qkv_post_kernel with one CTA per packed row, reading
+// the pass's rotary table and arena rows.  A group of D/8 threads owns one
+// head, each thread 8 consecutive dims moved as 16-byte vectors, with its 8
+// (cos, sin) pairs and norm weights in registers; the rotary partner of dim
+// d (< D/2) is dim d + D/2, held by the thread D/16 lanes away in the same
+// group, and the norm's sum of squares is reduced inside the group.  Every
+// lane takes every shuffle (value heads and idle lanes compute and then
+// discard), so control flow stays uniform across a warp whose groups hold
+// different head types, and no block-wide barrier is needed.
 template <int D>
 __global__ void __launch_bounds__(256) qkv_post_row_kernel(const QkvPost p) {
   constexpr int G = D / 8;      // threads per head
   constexpr int HALF_G = G / 2; // partner distance in lanes
   constexpr int HALF = D / 2;
   pdl_trigger();
-  __shared__ float s_cos[HALF], s_sin[HALF], s_qw[D], s_kw[D];
-  __shared__ int64_t s_arena_row;
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
-  for (int i = tid; i < D; i += blockDim.x) {  // weights are not produced by a predecessor
-    s_qw[i] = __bfloat162float(p.q_norm[i]);
-    s_kw[i] = __bfloat162float(p.k_norm[i]);
-  }
-  pdl_wait();
-  if (tid < HALF) {
-    const float angle = static_cast<float>(p.position[row]) * p.inv_freq[tid];
-    float sn, cs;
-    sincosf(angle, &sn, &cs);
-    s_cos[tid] = cs;
-    s_sin[tid] = sn;
-  }
-  if (tid == 0) {
-    int64_t ar = -1;  // -1: row of a rejected tree, no K/V write
-    const int t = p.tree[row];
-    if (t >= 0) {
-      const int64_t a = p.slots[t] * p.capacity + p.cache_len[t] + p.local[row];
-      if (a < 0 || a >= p.plane_rows || p.cache_len[t] + p.local[row] >= p.capacity) {
-        report(p.status, SG_ERR_CAPACITY);
-      } else {
-        ar = a;
-      }
-    }
-    s_arena_row = ar;
-  }
-  __syncthreads();
-  const int heads = p.nq + 2 * p.nkv;
-  const int64_t arena_row = s_arena_row;
   const int j = tid % G;            // 8-dim chunk of the head
   const bool high = j >= HALF_G;    // dims >= D/2
   const int d0 = 8 * j;
   const int dl = 8 * (j % HALF_G);  // angle index of this chunk's dims
+  float qw[8], kw[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {  // weights are not produced by a predecessor
+    qw[e] = __bfloat162float(p.q_norm[d0 + e]);
+    kw[e] = __bfloat162float(p.k_norm[d0 + e]);
+  }
+  pdl_wait();
+  float cs[8], sn[8];
+  const float2* rr = p.rope + static_cast<int64_t>(row) * HALF + dl;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float2 t = rr[e];
+    cs[e] = t.x;
+    sn[e] = t.y;
+  }
+  const int64_t arena_row = p.arena_row[row];
+  const int heads = p.nq + 2 * p.nkv;
   const int iters = (heads * G + static_cast<int>(blockDim.x) - 1) / static_cast<int>(blockDim.x);
   for (int it = 0; it < iters; ++it) {
     const int head = (it * static_cast<int>(blockDim.x) + tid) / G;
@@ -340,15 +358,13 @@ __global__ void __launch_bounds__(256) qkv_post_row_kernel(const QkvPost p) {
 #pragma unroll
     for (int d = HALF_G; d >= 1; d >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, d);
     const float rstd = rsqrtf(ss / static_cast<float>(D) + p.eps);
-    const float* w = is_q ? s_qw : s_kw;
     float r[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const float x = v[e] * rstd * w[d0 + e];
+      const float x = v[e] * rstd * (is_q ? qw[e] : kw[e]);
       const float partner = __shfl_xor_sync(0xffffffffu, x, HALF_G);
-      const float c = s_cos[dl + e], sn = s_sin[dl + e];
       // rotate_half: out_d = x_d cos - x_{d+H} sin,  out_{d+H} = x_{d+H} cos + x_d sin
-      r[e] = high ? x * c + partner * sn : x * c - partner * sn;
+      r[e] = high ? x * cs[e] + partner * sn[e] : x * cs[e] - partner * sn[e];
     }
     if (!valid) continue;
     const bool qk = is_q || is_k;
@@ -466,6 +482,16 @@ int launch_tree_meta(const int64_t* row_offsets, const int64_t* parents, const i
   return check_launch("tree_meta_kernel");
 }
 
+int launch_row_rope(const RowMeta& meta, const float* inv_freq, int head_dim, int rows, const int64_t* slots,
+                    const int64_t* cache_len, int64_t capacity, int64_t plane_rows, int32_t* status,
+                    cudaStream_t stream) {
+  if (rows <= 0) return SG_OK;
+  const int half = head_dim / 2;
+  row_rope_kernel<<<rows, half, 0, stream>>>(meta.position, meta.tree, meta.local, inv_freq, slots, cache_len,
+                                             capacity, plane_rows, half, meta.rope, meta.arena_row, status);
+  return check_launch("row_rope_kernel");
+}
+
 int launch_embed(const int64_t* tokens, const __nv_bfloat16* embed, int64_t vocab, int hidden, int rows, float* x,
                  int32_t* status, cudaStream_t stream) {
   if (rows <= 0) return SG_OK;
@@ -483,8 +509,8 @@ int launch_rmsnorm(const float* x, const __nv_bfloat16* weight, int hidden, int 
 int launch_qkv_post(const QkvPost& p, cudaStream_t stream) {
   if (p.rows <= 0) return SG_OK;
   auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
-  const bool vec = a16(p.qkv) && a16(p.q_out) && a16(p.k_plane0) && a16(p.v_plane0) &&
-                   (p.plane_stride * 2) % 16 == 0;
+  const bool vec = p.rope != nullptr && p.arena_row != nullptr && a16(p.qkv) && a16(p.q_out) &&
+                   a16(p.k_plane0) && a16(p.v_plane0) && (p.plane_stride * 2) % 16 == 0;
   if (vec && p.head_dim == 128)
     return launch_pdl("qkv_post_row_kernel", qkv_post_row_kernel<128>, dim3(p.rows), dim3(256), 0, stream, p);
   if (vec && p.head_dim == 64)

@@ -19,7 +19,15 @@ struct RowMeta {
   int32_t* local;       // [Q] local node index
   int64_t* request_id;  // [Q] Philox key of the row's request
   int32_t* order;       // [R] requests by decreasing K/V length (attention launch order)
+  float2* rope;         // [Q][D/2] (cos, sin) of the row's rotary angles, once per pass
+  int64_t* arena_row;   // [Q] arena row of the row's K/V (-1: rejected tree or overflow)
 };
+
+// Per-pass rotary table and K/V arena row of every packed row (the same in
+// every layer): rope[q][d] = sincos(position[q] * inv_freq[d]).
+int launch_row_rope(const RowMeta& meta, const float* inv_freq, int head_dim, int rows, const int64_t* slots,
+                    const int64_t* cache_len, int64_t capacity, int64_t plane_rows, int32_t* status,
+                    cudaStream_t stream);
 
 int launch_tree_meta(const int64_t* row_offsets, const int64_t* parents, const int64_t* position_base,
                      const int64_t* request_ids, int num_trees, int num_rows, RowMeta meta, int32_t* status,
@@ -58,6 +66,8 @@ struct QkvPost {
   int64_t plane_stride;         // elements between consecutive kv heads' planes
   int64_t capacity;             // rows per slot
   int64_t plane_rows;           // rows per plane (slots * capacity)
+  const float2* rope;           // [Q][D/2] per-pass rotary table (launch_row_rope), or null
+  const int64_t* arena_row;     // [Q] per-pass K/V arena row (launch_row_rope), or null
   int nq, nkv, head_dim, rows;
   float eps;
   int32_t* status;
