@@ -20,47 +20,57 @@ __device__ __forceinline__ void report(int32_t* status, int code) {
 
 // One thread per tree: parents precede children, so one ordered pass gives
 // depth and the ancestor-or-self bitset of every node.
-__global__ void tree_meta_kernel(const int64_t* __restrict__ row_offsets, const int64_t* __restrict__ parents,
-                                 const int64_t* __restrict__ position_base, const int64_t* __restrict__ request_ids,
-                                 int num_trees, int num_rows, RowMeta meta, int32_t* status) {
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+__global__ void __launch_bounds__(kMaxTreeRows) tree_meta_kernel(
+    const int64_t* __restrict__ row_offsets, const int64_t* __restrict__ parents,
+    const int64_t* __restrict__ position_base, const int64_t* __restrict__ request_ids, int num_trees, int num_rows,
+    RowMeta meta, int32_t* status) {
+  // One CTA per tree, one thread per node: each node builds its own
+  // ancestor-or-self bitset and depth by walking its parent chain in shared
+  // memory, so no node waits for another.  A parent outside [0, j) is
+  // reported and treated as the root, as is a root whose parent is not -1.
+  __shared__ int s_parent[kMaxTreeRows];
+  const int t = blockIdx.x;
   if (t >= num_trees) return;
   const int64_t r0 = row_offsets[t];
   const int64_t r1 = row_offsets[t + 1];
   const int n = static_cast<int>(r1 - r0);
   if (r0 < 0 || r1 > num_rows || n < 1 || n > kMaxTreeRows) {
-    report(status, SG_ERR_TREE);
+    if (threadIdx.x == 0) report(status, SG_ERR_TREE);
     return;
   }
-  const int64_t base = position_base[t];
-  const int64_t rid = request_ids != nullptr ? request_ids[t] : t;
-  int depth[kMaxTreeRows];
-  for (int j = 0; j < n; ++j) {
-    const int64_t q = r0 + j;
-    const int64_t par = parents[q];
-    uint32_t* anc = meta.anc + q * kAncWords;
+  const int j = threadIdx.x;
+  if (j < n) {
+    const int64_t par = parents[r0 + j];
+    int p = 0;
     if (j == 0) {
       if (par != -1) report(status, SG_ERR_TREE);
-      depth[0] = 0;
-#pragma unroll
-      for (int w = 0; w < kAncWords; ++w) anc[w] = 0u;
+      p = -1;
+    } else if (par < 0 || par >= j) {
+      report(status, SG_ERR_TREE);
     } else {
-      int p = static_cast<int>(par);
-      if (par < 0 || par >= j) {
-        report(status, SG_ERR_TREE);
-        p = 0;
-      }
-      depth[j] = depth[p] + 1;
-      const uint32_t* pa = meta.anc + (r0 + p) * kAncWords;
-#pragma unroll
-      for (int w = 0; w < kAncWords; ++w) anc[w] = pa[w];
+      p = static_cast<int>(par);
     }
-    anc[j >> 5] |= 1u << (j & 31);
-    meta.position[q] = static_cast<int32_t>(base + depth[j]);
-    meta.tree[q] = t;
-    meta.local[q] = j;
-    meta.request_id[q] = rid;
+    s_parent[j] = p;
   }
+  __syncthreads();
+  if (j >= n) return;
+  uint32_t bits[kAncWords];
+#pragma unroll
+  for (int w = 0; w < kAncWords; ++w) bits[w] = 0u;
+  int depth = 0;
+  for (int a = j; a > 0; a = s_parent[a]) {  // parents are strictly smaller: the walk ends at the root
+    bits[a >> 5] |= 1u << (a & 31);
+    ++depth;
+  }
+  bits[0] |= 1u;  // the root
+  const int64_t q = r0 + j;
+  uint32_t* anc = meta.anc + q * kAncWords;
+#pragma unroll
+  for (int w = 0; w < kAncWords; ++w) anc[w] = bits[w];
+  meta.position[q] = static_cast<int32_t>(position_base[t] + depth);
+  meta.tree[q] = t;
+  meta.local[q] = j;
+  meta.request_id[q] = request_ids != nullptr ? request_ids[t] : t;
 }
 
 // Launch order of the tree attention: requests by decreasing K/V length
@@ -477,8 +487,8 @@ int launch_tree_meta(const int64_t* row_offsets, const int64_t* parents, const i
   if (num_trees <= 0) return SG_OK;
   // rows not claimed by a valid tree keep tree = -1 and are skipped downstream
   SG_CUDA_CHECK(cudaMemsetAsync(meta.tree, 0xff, static_cast<size_t>(num_rows) * sizeof(int32_t), stream));
-  tree_meta_kernel<<<(num_trees + 63) / 64, 64, 0, stream>>>(row_offsets, parents, position_base, request_ids,
-                                                               num_trees, num_rows, meta, status);
+  tree_meta_kernel<<<num_trees, kMaxTreeRows, 0, stream>>>(row_offsets, parents, position_base, request_ids,
+                                                             num_trees, num_rows, meta, status);
   return check_launch("tree_meta_kernel");
 }
 
