@@ -156,6 +156,33 @@ SG_API int sg_kv_commit_accepted(void* arena, int64_t plane_rows, int64_t num_pl
                           const int64_t* accept_out, int32_t num_trees,
                           int32_t max_depth, int32_t* status, void* stream);
 
+/*
+ * Shared-budget tier allocation for the next wave (host function: every
+ * pointer is a HOST pointer; no device work).  Replaces the reference's
+ * exact-row allocator _allocate_global_tree_budgets
+ * (continuous_tree_block_decode.py:706-795) with its wave-cost model
+ * _global_wave_cost (:619-641), given the per-request weights the decoder
+ * derives from progress and age (:751-760; across data-parallel ranks their
+ * global terms come from the per-wave score allgather).
+ *
+ * weights      [num_requests] fp64 >= 0
+ * options      [num_options] tier sizes in draft nodes, strictly increasing,
+ *              >= 1; a tier of b nodes takes b + 1 rows
+ * utilities    [num_requests, num_options] fp64 >= 1 (draft expected tokens)
+ * row_budget   rows of the wave; >= num_requests * (options[0] + 1)
+ * cost model   fixed_row_equivalent > 0 with curve_points == 0 (cost = fixed +
+ *              rows), or fixed_row_equivalent = NaN with a piecewise-linear
+ *              curve of curve_points (rows, cost) points, rows increasing,
+ *              cost positive and non-decreasing
+ * allocation   [num_requests] out: the chosen tier (an entry of options)
+ * Returns SG_ERR_INVALID_ARGUMENT for a malformed problem.  Results are
+ * bit-identical to the reference's (same fp64 evaluation order and tie rules).
+ */
+SG_API int sg_allocate_tiers(int32_t num_requests, const double* weights, int32_t num_options,
+                             const int32_t* options, const double* utilities, int32_t row_budget,
+                             double fixed_row_equivalent, const int32_t* curve_rows, const double* curve_cost,
+                             int32_t curve_points, int32_t* allocation);
+
 /* Epilogues of sg_gemm_bf16. */
 enum sg_gemm_epilogue {
   SG_EPI_STORE_BF16 = 0, /* C bf16 [M, ldc] = acc */
@@ -243,7 +270,11 @@ typedef struct {
   const int64_t* position_base;  /* [R] rotary position of the root row */
   const int64_t* request_ids;    /* [R] Philox key per request (NULL: index) */
   uint64_t seed;
-  float temperature;
+  float temperature;             /* > 0: sample softmax(logits / T); 0: greedy,
+                                    the argmax of the bf16-rounded logits
+                                    (first maximum), the reference's T = 0
+                                    verifier tree_verify_greedy_block,
+                                    continuous_tree_block_decode.py:45-71 */
   int32_t commit;                /* 1: move accepted rows' KV to L_i.. */
   int64_t* accept_out;           /* [R, max_depth + 2] reference layout */
   int64_t* lengths_out;          /* [R] L_i + accepted + 1 (commit) */
@@ -277,13 +308,42 @@ SG_API size_t sg_engine_workspace_bytes(void* engine);
  * One packed tree-verification step, enqueued on `stream` with no host
  * synchronisation (capturable in a CUDA graph): target forward over the
  * packed rows with request-isolated tree attention reading the arena, new
- * K/V written at each request's arena tail, LM head fused with online
- * softmax and Gumbel-max sampling (one posterior draw per row: the law of
- * sampling.py:903-950), tree walk into accept_out, optional commit.
- * Replaces continuous_tree_block_decode.py:1748-2129 (pack, target,
- * select_commit stages).
+ * K/V written at each request's arena tail, LM head fused with softmax and
+ * sampling (one posterior draw per row from softmax(logits / T): the law of
+ * sampling.py:903-950; greedy argmax at T = 0), tree walk into accept_out,
+ * optional commit.  Replaces continuous_tree_block_decode.py:1748-2129
+ * (pack, target, select_commit stages).
  */
 SG_API int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stream);
+
+/*
+ * Final RMSNorm + LM head fused with softmax and sampling over caller-given
+ * residual rows: the computation of sg_verify_pass's sampling stage, and the
+ * fused form of the reference's lazy-projection verifier input (hidden states
+ * plus the LM-head module instead of logits,
+ * continuous_tree_block_decode.py:1795-1808, 1933-1964).
+ *
+ * x            fp32 [rows, hidden] residual rows (e.g. sg_wave_desc.hidden_out),
+ *              16-byte aligned
+ * final_norm   bf16 [hidden], 4-byte aligned;  lm_head bf16 [vocab, hidden],
+ *              16-byte aligned;  hidden % 64 == 0, vocab % 32 == 0
+ * row_node     int32 [rows], row_request int64 [rows]: the Philox key of each
+ *              row's draw (seed, request, node), as in the pass
+ * temperature  > 0 samples softmax(logits / T); 0 is greedy (argmax of the
+ *              bf16-rounded logits, first maximum)
+ * lse          fp32 [rows] log-normaliser of logits / T (T = 1 when greedy);
+ *              posterior int64 [rows] the drawn token
+ * workspace    256-byte aligned device buffer of at least
+ *              sg_lm_head_sample_workspace_bytes(rows, hidden, vocab) bytes,
+ *              used by this call only (calls sharing one must be ordered)
+ * If the GEMM gives up a bounded wait, every row gets posterior -1 and lse
+ * NaN.  Misaligned pointers return SG_ERR_INVALID_ARGUMENT before any launch.
+ */
+SG_API size_t sg_lm_head_sample_workspace_bytes(int32_t rows, int32_t hidden, int32_t vocab);
+SG_API int sg_lm_head_sample(const float* x, const void* final_norm, const void* lm_head, int32_t rows,
+                             int32_t hidden, int32_t vocab, float rms_eps, const int32_t* row_node,
+                             const int64_t* row_request, uint64_t seed, float temperature, float* lse,
+                             int64_t* posterior, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Fused LM-head sampling that allocates no device memory.  No counterpart in
@@ -292,23 +352,25 @@ SG_API int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stream);
  * allocator, or a foreign-language caller whose FFI only passes in buffers
  * it allocated itself.
  *
- * Same computation and output as the sampling stage of sg_verify_pass:
- * final RMSNorm of the residual rows x (fp32 [rows, hidden], e.g. the
- * pass's hidden_out) with final_norm (bf16 [hidden]), LM head (bf16
- * [vocab, hidden]) fused with online softmax and Gumbel-max sampling keyed
- * by (seed, row_request[r], row_node[r]), then lse[r] and posterior[r].
+ * Same arguments (minus the workspace), computation and output as
+ * sg_lm_head_sample, including the alignment rules and the posterior = -1 /
+ * lse = NaN answer to a GEMM that gave up a bounded wait.
  *
- * Its scratch (normalised rows and per-vocab-tile partials,
- * rows * (2 * hidden + 16 * ceil(vocab / 256)) bytes plus alignment) lives in
- * one library-owned device array of SG_LM_HEAD_STATIC_SCRATCH_BYTES, present
- * on every GPU that loads the library until the process exits; larger
- * requests fail with SG_ERR_WORKSPACE.  The first call on each device looks
- * up the array's device address (cudaGetSymbolAddress) and caches it; make
- * that first call before any stream capture.  All calls share the array:
- * calls whose executions overlap on the GPU (other streams, other host
- * threads) race and must be serialised by the caller.  Nothing needs
- * clearing between calls: every scratch value read is written earlier in the
- * same call.
+ * Its scratch (a status word, the normalised rows and per-vocab-tile
+ * partials: sg_lm_head_sample_workspace_bytes(rows, hidden, vocab) bytes,
+ * about rows * (2 * hidden + 16 * ceil(vocab / 256)) + 512) lives in one
+ * library-owned device array of SG_LM_HEAD_STATIC_SCRATCH_BYTES, present on
+ * every GPU that loads the library until the process exits; larger requests
+ * fail with SG_ERR_WORKSPACE (e.g. 473 rows fit at hidden 4096, vocab
+ * 151936).  The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress) and caches it; make that first call before
+ * any stream capture.  The cached address belongs to the CUDA context of
+ * that first call: after cudaDeviceReset in the same process it is stale,
+ * and this entry point must not be used on that device again.  All calls
+ * share the array: calls whose executions overlap on the GPU (other streams,
+ * other host threads) race and must be serialised by the caller.  The status
+ * word is cleared at the start of every call; every other scratch value read
+ * is written earlier in the same call.
  */
 #define SG_LM_HEAD_STATIC_SCRATCH_BYTES (8u << 20)
 SG_API int sg_lm_head_sample_static(const float* x, const void* final_norm, const void* lm_head,

@@ -1,12 +1,12 @@
 """Shared-budget tier allocation across data-parallel ranks.
 
-Host-side planning that chooses each request's tree tier for the next wave.
-It restates the reference's exact-row allocator
-(continuous_tree_block_decode.py:560-568 ``_draft_tree_expected_tokens``,
-:619-641 ``_global_wave_cost``, :706-795 ``_allocate_global_tree_budgets``):
-a multiple-choice knapsack solved by dynamic programming over exact row
-counts, maximising weighted draft-side expected tokens divided by the wave
-cost, with causal critical-path weights
+Host-side planning that chooses each request's tree tier for the next wave,
+the role of the reference's exact-row allocator
+(continuous_tree_block_decode.py:706-795, with the draft utility of :560-568
+and the wave-cost model of :619-641).  The knapsack itself is native code in
+the library (``sg_allocate_tiers``, include/specgrove_b200.h): one tier per
+request, maximising weighted draft expected tokens divided by the measured
+wave cost, with the critical-path weights
 ``1 + c * ((leading_progress - generated) / max_new_tokens + age / max_age)``.
 
 With requests sharded over GPUs, the weights' global terms (the leading
@@ -19,83 +19,70 @@ exchanged.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 from typing import Sequence
 
+import numpy as np
 import torch
+
+from . import _lib
 
 
 def draft_tree_expected_tokens(prefix_log_masses: Sequence[float]) -> float:
-    """1 + sum of draft prefix masses of the non-root nodes (:560-568)."""
-    value = 1.0 + sum(math.exp(m) for m in prefix_log_masses[1:])
-    if not math.isfinite(value) or value < 1.0:
-        raise FloatingPointError("Invalid draft-tree expected-token utility")
-    return value
-
-
-def wave_cost(rows: int, fixed_row_equivalent: float | None,
-              row_cost_curve: Sequence[tuple[int, float]] | None) -> float:
-    """Piecewise-linear measured wave cost, or fixed + rows (:619-641)."""
-    if rows < 1:
-        raise ValueError("A Target wave must contain at least one row")
-    if row_cost_curve is None:
-        if fixed_row_equivalent is None or not math.isfinite(fixed_row_equivalent) or fixed_row_equivalent <= 0:
-            raise ValueError("Missing global Target cost model")
-        return fixed_row_equivalent + rows
-    curve = tuple(row_cost_curve)
-    if rows <= curve[0][0]:
-        return curve[0][1]
-    for (lr, lc), (rr, rc) in zip(curve, curve[1:]):
-        if rows <= rr:
-            return lc + (rows - lr) / (rr - lr) * (rc - lc)
-    return curve[-1][1]
+    """Expected accepted tokens of a draft tree plus its bonus: one plus the
+    draft probability mass of every non-root node's prefix."""
+    masses = [math.exp(float(v)) for v in list(prefix_log_masses)[1:]]
+    total = 1.0 + math.fsum(masses)
+    if not (math.isfinite(total) and total >= 1.0):
+        raise FloatingPointError("draft expected-token utility is not a finite value >= 1")
+    return total
 
 
 def critical_path_weights(progress: Sequence[int], ages: Sequence[int], criticality_weight: float,
                           max_new_tokens: int, leading_progress: int | None = None,
                           maximum_age: int | None = None) -> list[float]:
-    """Per-request weights; global terms default to this request set's."""
+    """Per-request weights; the global terms default to this request set's
+    own leading progress and oldest age."""
     lead = max(progress) if leading_progress is None else leading_progress
-    oldest = max(ages) if maximum_age is None else maximum_age
-    return [1.0 + criticality_weight * ((lead - g) / max_new_tokens + a / max(1, oldest))
-            for g, a in zip(progress, ages)]
+    oldest = max(1, max(ages) if maximum_age is None else maximum_age)
+    weights = []
+    for generated, age in zip(progress, ages):
+        lag = (lead - generated) / max_new_tokens
+        weights.append(1.0 + criticality_weight * (lag + age / oldest))
+    return weights
 
 
 def allocate_tree_budgets(weights: Sequence[float], budget_options: Sequence[int],
                           utilities: Sequence[Sequence[float]], *, row_budget: int,
                           fixed_row_equivalent: float | None = None,
                           row_cost_curve: Sequence[tuple[int, float]] | None = None) -> tuple[int, ...]:
-    """Exact-row DP (:765-795): for every reachable row count keep the best
-    weighted reward (ties -> lexicographically smaller allocation); pick the
-    row count maximising reward / wave cost (ties -> fewer rows, larger trees)."""
-    options = tuple(int(v) for v in budget_options)
-    if (not weights or tuple(sorted(set(options))) != options or options[0] < 1
-            or row_budget < len(weights) * (options[0] + 1)
-            or (fixed_row_equivalent is None) == (row_cost_curve is None)
-            or len(utilities) != len(weights) or any(len(u) != len(options) for u in utilities)):
-        raise ValueError("Invalid global tree-budget allocation problem")
-    frontier: dict[int, tuple[float, tuple[int, ...]]] = {0: (0.0, ())}
-    for weight, values in zip(weights, utilities):
-        updated: dict[int, tuple[float, tuple[int, ...]]] = {}
-        for used, (reward, alloc) in frontier.items():
-            for budget, utility in zip(options, values):
-                rows = used + budget + 1
-                if rows > row_budget:
-                    continue
-                cand = (reward + weight * utility, alloc + (budget,))
-                prev = updated.get(rows)
-                if (prev is None or cand[0] > prev[0] + 1e-12
-                        or (abs(cand[0] - prev[0]) <= 1e-12 and cand[1] < prev[1])):
-                    updated[rows] = cand
-        frontier = updated
-    if not frontier:
-        raise RuntimeError("Global tree-budget allocator found no feasible wave")
-    _, (_, allocation) = max(
-        frontier.items(),
-        key=lambda item: (item[1][0] / wave_cost(item[0], fixed_row_equivalent, row_cost_curve), -item[0],
-                          tuple(-v for v in item[1][1])))
-    return allocation
+    """One tier per request from ``budget_options`` (draft nodes; a tier of b
+    nodes takes b + 1 rows) under ``row_budget`` rows, through the native
+    exact-row knapsack.  Exactly one cost model: ``fixed_row_equivalent``
+    (cost = fixed + rows) or ``row_cost_curve`` [(rows, cost), ...]."""
+    R, T = len(weights), len(budget_options)
+    util = np.asarray(utilities, dtype=np.float64)
+    if R < 1 or util.shape != (R, T) or (fixed_row_equivalent is None) == (row_cost_curve is None):
+        raise ValueError("tier allocation needs one weight and one utility per option for every request, "
+                         "and exactly one cost model")
+    w = np.ascontiguousarray(weights, dtype=np.float64)
+    opts = np.ascontiguousarray(budget_options, dtype=np.int32)
+    util = np.ascontiguousarray(util)
+    curve = list(row_cost_curve or [])
+    c_rows = np.ascontiguousarray([int(r) for r, _ in curve] or [0], dtype=np.int32)
+    c_cost = np.ascontiguousarray([float(c) for _, c in curve] or [0.0], dtype=np.float64)
+    fixed = math.nan if fixed_row_equivalent is None else float(fixed_row_equivalent)
+    out = np.zeros(R, dtype=np.int32)
+    lib = _lib.load()
+    st = lib.sg_allocate_tiers(R, w.ctypes.data, T, opts.ctypes.data, util.ctypes.data, int(row_budget), fixed,
+                               c_rows.ctypes.data, c_cost.ctypes.data, len(curve), out.ctypes.data)
+    if st == _lib.SG_ERR_INVALID_ARGUMENT:
+        raise ValueError(lib.sg_last_error().decode())
+    if st != _lib.SG_OK:
+        raise RuntimeError(lib.sg_last_error().decode())
+    return tuple(int(v) for v in out)
 
 
 @dataclass

@@ -46,6 +46,10 @@ inline int check_launch(const char* kernel) {
 
 int device_sm_count();
 
+// Largest CUDA device index + 1 that the per-device caches of this library
+// (kernel attributes, static scratch addresses) handle.
+constexpr int kMaxDevices = 64;
+
 // ---------------------------------------------------------------------------
 // Programmatic dependent launch.  A kernel launched with launch_pdl may start
 // while the previous kernel in the stream is still finishing: it triggers its

@@ -246,7 +246,10 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
     return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: null wave array");
   if (w.commit && w.lengths_out == nullptr)
     return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: commit needs lengths_out");
-  if (!(w.temperature > 0.f)) return fail(SG_ERR_UNSUPPORTED, "sg_verify_pass: temperature must be positive");
+  if (!(w.temperature >= 0.f) || w.temperature == INFINITY)
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: temperature must be finite and >= 0 (0 = greedy)");
+  const bool greedy = w.temperature == 0.f;
+  const float inv_temp = greedy ? 1.0f : 1.0f / w.temperature;
   int dev = 0;
   SG_CUDA_CHECK(cudaGetDevice(&dev));
   if (dev != e->device) return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: engine belongs to another device");
@@ -380,7 +383,8 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
   pl.row_local = e->meta.local;
   pl.row_request = e->meta.request_id;
   pl.seed = w.seed;
-  pl.inv_temp = 1.0f / w.temperature;
+  pl.inv_temp = inv_temp;
+  pl.greedy = greedy ? 1 : 0;
   pl.status = w.status;
   if ((st = gemm::launch<gemm::EpiLmHead>(e->xn_map, e->lm_map, gemm::make_shape(Q, m.vocab, H), pl, stream)) !=
       SG_OK)
@@ -388,10 +392,11 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
   trace(w, 12, stream);
   float* lse = w.lse != nullptr ? w.lse : e->lse_ws;
   int64_t* posterior = w.posterior != nullptr ? w.posterior : e->posterior_ws;
-  if ((st = layers::launch_lm_combine(e->partials, e->vocab_tiles, Q, lse, posterior, stream)) != SG_OK) return st;
+  if ((st = layers::launch_lm_combine(e->partials, e->vocab_tiles, Q, lse, posterior, nullptr, stream)) != SG_OK)
+    return st;
   if (w.child_logprob != nullptr &&
       (st = layers::launch_child_logprob(e->xn, static_cast<const __nv_bfloat16*>(m.lm_head), H, m.vocab, w.tokens, w.parents,
-                                         w.row_offsets, e->meta.tree, e->meta.local, lse, 1.0f / w.temperature, Q,
+                                         w.row_offsets, e->meta.tree, e->meta.local, lse, inv_temp, Q,
                                          w.child_logprob, stream)) != SG_OK)
     return st;
   trace(w, 13, stream);

@@ -559,14 +559,53 @@ struct EpiSwiGlu {
 };
 
 
-// LM head fused with online softmax and Gumbel-max sampling: full-vocabulary
-// logits never reach HBM.  Per (row, 256-column vocab tile) the epilogue
-// writes {tile max, sum exp(l - max), best l + Gumbel noise, its column};
-// a combine kernel turns the tiles into lse[row] and the row's posterior
-// token.  argmax_j (l_j + G_j) with G_j = -log(-log U_j) is an exact draw from
-// softmax(l); U_j comes from Philox4x32-10 keyed by the seed with counter
-// (column / 4, node, request lo, 0x80000000 | request hi), a stream disjoint
-// from the acceptance walk's (whose 4th counter word is 0).
+// LM head fused with softmax and sampling: full-vocabulary logits never reach
+// HBM.  Per (row, 256-column vocab tile) the epilogue writes
+// {tile max m_t, tile mass S_t = sum exp(x - m_t), tile key, tile column};
+// lm_combine_kernel turns the tiles into lse[row] and the row's posterior
+// token (the column of the largest key).  x = logit / T.
+//
+// Sampled rows (T > 0) use a two-level exact draw of softmax(x):
+//   1. a Gumbel race over the tiles: key_t = m_t + log S_t + G_t, G_t =
+//      -log E_t, E_t ~ Exp(1); argmax_t key_t picks tile t with probability
+//      S_t e^{m_t} / sum_s S_s e^{m_s} (Gumbel-max over the tile masses);
+//   2. inside the tile, column j = the first whose running sum of
+//      exp(x - m_t) exceeds U * S_t (inverse CDF), drawn whether or not the
+//      tile wins, so no second pass over the vocabulary is needed.
+// P(j) = (S_t e^{m_t} / Z) (e^{x_j - m_t} / S_t) = e^{x_j} / Z: the law of
+// softmax(x), the law of the reference's per-row multinomial
+// (sampling.py:29-42, 903-950).  Both draws come from one Philox4x32-10 call
+// keyed by the seed with counter (tile, node, request lo, 0x80000000 |
+// request hi), a stream disjoint from the acceptance walk's (whose 4th
+// counter word is 0): words (x, y) give E_t from 64 bits, word z the 24-bit
+// uniform U.  E_t keeps full fp32 relative precision near 0, where the
+// winning keys come from (exp_variate), so near-ties between tiles resolve
+// to within fp32 rounding of the keys, ~1e-6.
+// Greedy rows (T = 0, the reference's argmax verifier over bf16 logits,
+// continuous_tree_block_decode.py:45-71, 1809-1811): key = bf16(logit),
+// column = first maximum, mass terms at T = 1 (lse of the raw logits).
+__host__ __device__ __forceinline__ float exp_variate(uint64_t w) {
+  // V = (2k + 1) / 2^53 with k = w >> 12, a uniform in (0, 1); E = -ln(1 - V).
+  // Below 1/2, E = -log1p(-V); above, 1 - V = (2k' + 1) / 2^53 with
+  // k' = 2^52 - 1 - k exactly, and E = -ln(1 - V).  Both operands are exact
+  // up to one fp32 rounding of the odd integer.
+  const uint64_t k = w >> 12;
+  const bool low = (k >> 51) == 0ull;
+  const uint64_t kk = low ? k : ((1ull << 52) - 1ull) - k;
+#ifdef __CUDA_ARCH__
+  const float v = __ull2float_rn(2ull * kk + 1ull) * 0x1p-53f;
+#else
+  const float v = static_cast<float>(2ull * kk + 1ull) * 0x1p-53f;
+#endif
+  return low ? -log1pf(-v) : -logf(v);
+}
+
+__device__ __forceinline__ float lm_tile_weight(float v, float inv_temp, float m) {
+  return __expf(__fsub_rn(__fmul_rn(v, inv_temp), m));
+}
+
+__device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
 struct EpiLmHead {
   struct Params {
     float4* partials;          // [rows, n_tiles]
@@ -574,56 +613,105 @@ struct EpiLmHead {
     const int32_t* row_local;  // [rows] node index within the tree
     const int64_t* row_request;// [rows] request key
     uint64_t seed;
-    float inv_temp;
+    float inv_temp;            // 1 / T (1 for greedy rows)
+    int greedy;                // 1: argmax of bf16 logits
     int32_t* status;
   };
   static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int m0, int n0,
                                                int quarter, int lane, uint4*) {
+    constexpr int kChunks = BN / 32;
     const int row = m0 + quarter * 32 + lane;
     const bool rv = row < s.M;
-    const uint32_t node = rv ? static_cast<uint32_t>(p.row_local[row]) : 0u;
-    const uint64_t req = rv ? static_cast<uint64_t>(p.row_request[row]) : 0ull;
-    const uint32_t k0 = static_cast<uint32_t>(p.seed), k1 = static_cast<uint32_t>(p.seed >> 32);
-    float m = -INFINITY, sum = 0.f, best = -INFINITY;
-    int bidx = n0;
+    const int nch = min(BN, s.N - n0) / 32;  // N % 32 == 0; uniform over the CTA
+    // pass 1: tile max of x = logit / T (greedy: first maximum of bf16(logit))
+    float m = -INFINITY, gbest = -INFINITY;
+    int gcol = n0;
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      const int col0 = n0 + c * 32;
-      if (col0 >= s.N) break;
+    for (int c = 0; c < nch; ++c) {
       float v[32];
       sm100::tmem_ld32(taddr + c * 32, v);
-      float cm = -INFINITY;
+      if (p.greedy) {
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        v[e] *= p.inv_temp;
-        cm = fmaxf(cm, v[e]);
-      }
-      const float mn = fmaxf(m, cm);
-      float add = 0.f;
-#pragma unroll
-      for (int e = 0; e < 32; ++e) add += __expf(v[e] - mn);
-      sum = sum * __expf(m - mn) + add;
-      m = mn;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const U32x4 r = philox4x32_10(
-            U32x4{static_cast<uint32_t>(col0 >> 2) + q, node, static_cast<uint32_t>(req),
-                  0x80000000u | (static_cast<uint32_t>(req >> 32) & 0x7fffffffu)},
-            k0, k1);
-        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float u = (static_cast<float>(w[e] >> 8) + 0.5f) * (1.0f / 16777216.0f);
-          const float key = v[q * 4 + e] - __logf(-__logf(u));
-          if (key > best) {
-            best = key;
-            bidx = col0 + q * 4 + e;
+        for (int e = 0; e < 32; ++e) {
+          m = fmaxf(m, __fmul_rn(v[e], p.inv_temp));
+          const float b = bf16_round(v[e]);
+          if (b > gbest) {
+            gbest = b;
+            gcol = n0 + c * 32 + e;
           }
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) m = fmaxf(m, __fmul_rn(v[e], p.inv_temp));
+      }
+    }
+    // pass 2: per-chunk masses with the tile max (sequential fp32 sums)
+    float cs[kChunks];
+    float S = 0.f;
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      cs[c] = 0.f;
+      if (c < nch) {
+        float v[32];
+        sm100::tmem_ld32(taddr + c * 32, v);
+        float a = 0.f;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) a = __fadd_rn(a, lm_tile_weight(v[e], p.inv_temp, m));
+        cs[c] = a;
+        S = __fadd_rn(S, a);
+      }
+    }
+    float key = gbest;
+    int col = gcol;
+    if (!p.greedy) {
+      const uint32_t node = rv ? static_cast<uint32_t>(p.row_local[row]) : 0u;
+      const uint64_t req = rv ? static_cast<uint64_t>(p.row_request[row]) : 0ull;
+      const U32x4 r = philox4x32_10(U32x4{static_cast<uint32_t>(n0 / BN), node, static_cast<uint32_t>(req),
+                                          0x80000000u | (static_cast<uint32_t>(req >> 32) & 0x7fffffffu)},
+                                    static_cast<uint32_t>(p.seed), static_cast<uint32_t>(p.seed >> 32));
+      const float E = exp_variate((static_cast<uint64_t>(r.y) << 32) | r.x);
+      key = __fsub_rn(__fadd_rn(m, logf(S)), logf(E));
+      const float thr = __fmul_rn((static_cast<float>(r.z >> 8) + 0.5f) * (1.0f / 16777216.0f), S);
+      // chunk holding the crossing: the first c with base_c + cs[c] > thr
+      float base = 0.f;
+      int kc = -1;
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        if (kc < 0 && c < nch) {
+          const float nb = __fadd_rn(base, cs[c]);
+          if (thr < nb)
+            kc = c;
+          else
+            base = nb;
+        }
+      }
+      col = -1;
+      if (kc < 0) {  // rounding left thr at the total: the last column (the reference's V - 1 rule)
+        kc = nch;
+        col = n0 + nch * 32 - 1;
+      }
+      // pass 3: the crossing inside chunk kc.  Each chunk's running sum
+      // repeats pass 2's operations in the same order, so at the chunk's end
+      // base + a equals nb > thr: the crossing always lies inside it.  TMEM
+      // loads are warp-wide, so the warp walks the range of its lanes' chunks.
+      const int c_lo = __reduce_min_sync(0xffffffffu, kc);
+      const int c_hi = min(__reduce_max_sync(0xffffffffu, kc), nch - 1);
+#pragma unroll 1
+      for (int c = c_lo; c <= c_hi; ++c) {
+        float v[32];
+        sm100::tmem_ld32(taddr + c * 32, v);
+        if (c == kc) {
+          float a = 0.f;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            a = __fadd_rn(a, lm_tile_weight(v[e], p.inv_temp, m));
+            if (col < 0 && thr < __fadd_rn(base, a)) col = n0 + c * 32 + e;
+          }
+          if (col < 0) col = n0 + c * 32 + 31;
         }
       }
     }
-    if (rv) p.partials[static_cast<int64_t>(row) * p.n_tiles + n0 / BN] =
-        make_float4(m, sum, best, __int_as_float(bidx));
+    if (rv) p.partials[static_cast<int64_t>(row) * p.n_tiles + n0 / BN] = make_float4(m, S, key, __int_as_float(col));
   }
 };
 
@@ -631,13 +719,17 @@ struct EpiLmHead {
 template <class Epi>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Shape& shape_in, const typename Epi::Params& ep,
            cudaStream_t stream, const SplitWorkspace* split = nullptr) {
-  static int configured_device_mask = 0;
+  // Devices on which this instantiation's shared-memory limit is raised.
+  // Setting it twice (two host threads racing on the first call) is harmless.
+  static std::atomic<uint64_t> configured_devices{0};
   int dev = 0;
   SG_CUDA_CHECK(cudaGetDevice(&dev));
-  if (!(configured_device_mask & (1 << dev))) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(SG_ERR_UNSUPPORTED, "gemm: device index >= 64");
+  const uint64_t bit = 1ull << dev;
+  if (!(configured_devices.load(std::memory_order_acquire) & bit)) {
     SG_CUDA_CHECK(cudaFuncSetAttribute(gemm_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(SMEM_BYTES)));
-    configured_device_mask |= (1 << dev);
+    configured_devices.fetch_or(bit, std::memory_order_acq_rel);
   }
   const int sms = device_sm_count();
   Shape shape = shape_in;

@@ -397,10 +397,18 @@ __global__ void __launch_bounds__(256) qkv_post_row_kernel(const QkvPost p) {
 // lse and Gumbel-max token of every row from the per-vocab-tile partials
 // (max, sum exp(l - max), best perturbed logit, its column).
 __global__ void lm_combine_kernel(const float4* __restrict__ partials, int n_tiles, int rows,
-                                  float* __restrict__ lse, int64_t* __restrict__ posterior) {
+                                  float* __restrict__ lse, int64_t* __restrict__ posterior,
+                                  const int32_t* __restrict__ abort_status) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
+  if (abort_status != nullptr && *abort_status != 0) {
+    if (lane == 0) {
+      if (lse != nullptr) lse[row] = NAN;
+      if (posterior != nullptr) posterior[row] = -1;
+    }
+    return;
+  }
   const float4* pr = partials + static_cast<int64_t>(row) * n_tiles;
   float m = -INFINITY;
   for (int t = lane; t < n_tiles; t += 32) m = fmaxf(m, pr[t].x);
@@ -535,9 +543,9 @@ int launch_qkv_post(const QkvPost& p, cudaStream_t stream) {
 }
 
 int launch_lm_combine(const float4* partials, int n_tiles, int rows, float* lse, int64_t* posterior,
-                      cudaStream_t stream) {
+                      const int32_t* abort_status, cudaStream_t stream) {
   if (rows <= 0) return SG_OK;
-  lm_combine_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(partials, n_tiles, rows, lse, posterior);
+  lm_combine_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(partials, n_tiles, rows, lse, posterior, abort_status);
   return check_launch("lm_combine_kernel");
 }
 

@@ -74,8 +74,11 @@ struct QkvPost {
 };
 int launch_qkv_post(const QkvPost& p, cudaStream_t stream);
 
+// lse[row] and posterior[row] from the per-vocab-tile partials of the
+// LM-head epilogue.  With a non-null `abort_status` holding a non-zero code
+// (a GEMM that gave up a bounded wait), every row gets posterior -1, lse NaN.
 int launch_lm_combine(const float4* partials, int n_tiles, int rows, float* lse, int64_t* posterior,
-                      cudaStream_t stream);
+                      const int32_t* abort_status, cudaStream_t stream);
 
 int launch_child_logprob(const __nv_bfloat16* h, const __nv_bfloat16* lm_head, int hidden, int64_t vocab,
                          const int64_t* tokens,

@@ -25,6 +25,7 @@ import torch
 from . import _lib
 from ._lib import check, ptr, stream_ptr
 from .arena import PersistentKVArena
+from .sampling import _topology
 
 LAYER_WEIGHTS = 8
 
@@ -202,18 +203,11 @@ class Wave:
         parents, tokens = [], []
         max_rows, max_depth = 1, 0
         for par, tok in trees:
-            if len(par) != len(tok) or len(par) < 1 or par[0] != -1:
-                raise ValueError("each tree needs one token per row and a root with parent -1")
-            depth = [0] * len(par)
-            for j in range(1, len(par)):
-                if not 0 <= par[j] < j:
-                    raise ValueError("Tree parents must precede their children")
-                depth[j] = depth[par[j]] + 1
-            siblings = set(zip(par[1:], tok[1:]))
-            if len(siblings) != len(par) - 1:
-                raise ValueError("A tree parent cannot repeat a child token")
+            if len(par) != len(tok) or len(par) < 1:
+                raise ValueError("each tree needs one token per row (the root row's input token first)")
+            _, _, depth = _topology(par, list(tok)[1:])
             max_rows = max(max_rows, len(par))
-            max_depth = max(max_depth, max(depth))
+            max_depth = max(max_depth, depth)
             parents += list(par)
             tokens += list(tok)
             offsets.append(len(parents))

@@ -1,9 +1,8 @@
 """Tree-sampling acceptance through the C ABI, with the reference's verifier API.
 
 The per-request functions keep the names, arguments, return values and error
-behaviour of the reference verifiers in
-``gbv_experiments/fused_tree_sampling.py`` (``_topology`` :2089-2102,
-``tree_verify_ancestral_fused_scan`` :2172-2202,
+types of the reference verifiers in
+``gbv_experiments/fused_tree_sampling.py`` (``tree_verify_ancestral_fused_scan`` :2172-2202,
 ``tree_verify_ancestral_sparse_exit_fused_scan`` :2205-2259,
 ``..._batched`` :2262-2373, ``tree_verify_ancestral_same_draw_fused``
 :2376-2414), so the decoder's verifier dispatch
@@ -25,19 +24,31 @@ from ._lib import SG_RULE_SCAN, SG_RULE_SPARSE_EXIT, check, ptr, stream_ptr
 
 
 def _topology(parents, tokens):
-    """Reference ``_topology`` (fused_tree_sampling.py:2089-2102)."""
-    parents = list(parents)
-    tokens = list(tokens)
-    node_count = len(parents)
-    if (node_count < 1 or len(tokens) != node_count - 1
-            or parents[0] != -1
-            or any(parent < 0 or parent >= node for node, parent in enumerate(parents[1:], 1))
-            or len(set(zip(parents[1:], tokens))) != len(tokens)):
-        raise ValueError("Invalid probability-tree topology")
-    depths = [0] * node_count
-    for node in range(1, node_count):
-        depths[node] = depths[parents[node]] + 1
-    return parents, tokens, max(depths)
+    """Check one probability tree and return (parents, edge tokens, depth).
+
+    The rules a tree must satisfy (the reference validates the same ones,
+    fused_tree_sampling.py:2089-2102, sampling.py:922-926): node 0 is the root
+    (parent -1), every other node's parent is an earlier node, there is one
+    edge token per non-root node, and no node has two children with the same
+    token.  A violation raises ValueError."""
+    parents = [int(p) for p in parents]
+    tokens = [int(t) for t in tokens]
+    n = len(parents)
+    if n == 0 or parents[0] != -1 or len(tokens) != n - 1:
+        raise ValueError("Invalid probability-tree topology: need a root with parent -1 and one token per edge")
+    depth = [0] * n
+    edges = set()
+    for node in range(1, n):
+        parent = parents[node]
+        if not 0 <= parent < node:
+            raise ValueError(f"Invalid probability-tree topology: node {node} has parent {parent}, "
+                             "which does not precede it")
+        edge = (parent, tokens[node - 1])
+        if edge in edges:
+            raise ValueError(f"Invalid probability-tree topology: node {parent} repeats child token {edge[1]}")
+        edges.add(edge)
+        depth[node] = depth[parent] + 1
+    return parents, tokens, max(depth)
 
 
 def _check_rows(all_p, node_count, what):
@@ -47,16 +58,18 @@ def _check_rows(all_p, node_count, what):
 
 
 def _validate_probabilities(all_p, normalised: bool):
+    """Every row must be finite and non-negative with positive mass; the
+    sparse-exit rule also needs rows that already sum to one (it routes on
+    child masses without normalising).  Violations raise FloatingPointError."""
+    row_sums = all_p.sum(dim=-1, dtype=torch.float64)
+    bad = (~torch.isfinite(all_p)).any() | (all_p < 0).any()
     if normalised:
-        valid = (torch.isfinite(all_p).all() & (all_p >= 0).all()
-                 & torch.isclose(all_p.sum(-1), all_p.new_ones(all_p.shape[0]),
-                                 rtol=1e-10, atol=1e-12).all())
-        if not bool(valid):
-            raise FloatingPointError("Sparse-exit verifier requires normalized Target probabilities")
+        bad = bad | ((row_sums - 1.0).abs() > 1e-12 + 1e-10).any()
     else:
-        valid = (torch.isfinite(all_p).all() & (all_p >= 0).all() & (all_p.sum(-1) > 0).all())
-        if not bool(valid):
-            raise FloatingPointError("Invalid Target probabilities for DDTree")
+        bad = bad | (row_sums <= 0).any()
+    if bool(bad):
+        kind = "normalised, " if normalised else ""
+        raise FloatingPointError(f"Target probabilities must be finite, non-negative, {kind}with positive row mass")
 
 
 def _as_fp32_rows(all_p: torch.Tensor) -> torch.Tensor:
@@ -136,12 +149,14 @@ def accept_packed(probs: torch.Tensor, trees: PackedTrees, *, rule: int = SG_RUL
 
 
 def decode_output(packed_row, max_depth: int, vocab: int, tokens, what: str):
-    accepted_count = int(packed_row[max_depth])
-    bonus = int(packed_row[max_depth + 1])
-    if not 0 <= accepted_count <= max_depth or not 0 <= bonus < vocab:
-        raise RuntimeError(f"{what} returned invalid control values")
-    nodes = [int(node) for node in packed_row[:accepted_count]]
-    return nodes, [tokens[node - 1] for node in nodes], bonus
+    """(nodes, tokens, bonus) of one row of the kernels' [max_depth + 2]
+    layout: slots [0, count) hold the accepted nodes, slot max_depth the
+    count, slot max_depth + 1 the bonus token."""
+    count, bonus = int(packed_row[max_depth]), int(packed_row[max_depth + 1])
+    if count < 0 or count > max_depth or bonus < 0 or bonus >= vocab:
+        raise RuntimeError(f"{what}: kernel output out of range (count {count}, bonus {bonus})")
+    nodes = [int(v) for v in packed_row[:count]]
+    return nodes, [tokens[v - 1] for v in nodes], bonus
 
 
 def tree_verify_ancestral_fused_scan(parents, tokens, all_p, generator=None, validate: bool = True):

@@ -56,7 +56,7 @@ def test_static_scratch_sampler_matches_verify_pass(cuda_lib):
     engine.arena.storage.normal_(0.0, 1.0)
     lib = _lib.load()
     rng = np.random.default_rng(11)
-    for call, (count, seed, temperature) in enumerate([(6, 1234, 1.0), (3, 98765, 0.7)]):
+    for call, (count, seed, temperature) in enumerate([(6, 1234, 1.0), (3, 98765, 0.7), (5, 4321, 0.0)]):
         trees, lengths = _wave(rng, shape.vocab, count, 4, 40)
         request_ids = [100 * call + i for i in range(count)]
         wave = Wave(trees, list(range(count)), lengths, request_ids=request_ids)
@@ -69,14 +69,40 @@ def test_static_scratch_sampler_matches_verify_pass(cuda_lib):
         nodes, reqs = _row_keys(trees, request_ids)
         lse = torch.full((Q,), float("nan"), device="cuda")
         post = torch.full((Q,), -1, dtype=torch.long, device="cuda")
+        torch.cuda.synchronize()
+        if call > 0:   # everything this call needs is allocated by now
+            free_before, reserved_before = torch.cuda.mem_get_info()[0], torch.cuda.memory_reserved()
         st = lib.sg_lm_head_sample_static(ptr(hidden), ptr(weights.final_norm), ptr(weights.lm_head), Q, shape.hidden,
                                           shape.vocab, ctypes.c_float(shape.rms_eps), ptr(nodes), ptr(reqs), seed,
                                           ctypes.c_float(temperature), ptr(lse), ptr(post), stream_ptr())
         assert st == 0, lib.sg_last_error()
         torch.cuda.synchronize()
+        if call > 0:
+            # the call itself allocated nothing: device free memory and the
+            # caching allocator's reservation are unchanged across it
+            assert torch.cuda.mem_get_info()[0] == free_before
+            assert torch.cuda.memory_reserved() == reserved_before
         assert int(engine.status) == 0
         assert torch.equal(post, post_ref), call
         torch.testing.assert_close(lse, lse_ref, rtol=0.0, atol=TOL)
+
+
+def test_static_scratch_rejects_misaligned_rows(cuda_lib):
+    """A residual-row pointer that is not 16-byte aligned (a row slice at an
+    odd float offset) is refused before any launch instead of faulting."""
+    lib = _lib.load()
+    x = torch.zeros((4, 512), device="cuda")
+    small = torch.zeros(16384, device="cuda")   # covers a 32 x 512 bf16 LM head
+    nodes = torch.zeros(4, dtype=torch.int32, device="cuda")
+    reqs = torch.zeros(4, dtype=torch.long, device="cuda")
+    lse = torch.empty(4, device="cuda")
+    post = torch.empty(4, dtype=torch.long, device="cuda")
+    st = lib.sg_lm_head_sample_static(x.data_ptr() + 4, ptr(small), ptr(small), 3, 512, 32, ctypes.c_float(1e-6),
+                                      ptr(nodes), ptr(reqs), 0, ctypes.c_float(1.0), ptr(lse), ptr(post),
+                                      stream_ptr())
+    assert st == _lib.SG_ERR_INVALID_ARGUMENT
+    assert b"misaligned" in lib.sg_last_error()
+    torch.cuda.synchronize()
 
 
 def test_static_scratch_rejects_oversized_requests(cuda_lib):
