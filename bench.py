@@ -6,7 +6,8 @@
 One JSON line is printed by rank 0.  Under torchrun (N > 1) every rank runs
 its own shard of requests with a full model replica (data parallel, no
 data-path collective; weak scaling); the step time is the max over ranks of
-the CUDA-event time and `value` aggregates the accepted tokens of all ranks.
+the CUDA-event time and `value` is the accepted tokens of ALL ranks per
+second (`per_gpu` divides it by N).
 
 Workload `verify` (default): Qwen3-8B shape
 (36 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128, intermediate 12288,
@@ -14,11 +15,18 @@ vocab 151936), random-init bf16 weights, 64 requests per GPU with cache
 prefixes uniform in [1024, 4096] (synthetic KV), one canonical best-first
 tree per request cut to its tier (tier mix 40x16 + 12x32 + 8x64 + 4x128 rows
 = 2048 rows).  One step = one packed verify pass: target forward over the
-2048 rows, LM head fused with online softmax and Gumbel-max sampling, tree
-walk, and commit of the accepted rows' KV.  Weights (16.4 GB) and KV
-(~24 GB read per step) are far larger than L2, so no flush is needed.
+2048 rows, LM head fused with softmax and sampling, tree walk, and commit of
+the accepted rows' KV.  Weights (16.4 GB) and KV (~24 GB read per step) are
+far larger than L2, so no flush is needed.  At N = 1 the same line nests the
+configuration-2 acceptance sweep and the configuration-3 (Qwen3-4B shape)
+pass, measured in the same run.
 `verify4b` is configuration 3 (Qwen3-4B shape, 16 requests, 512 rows);
 `accept` is the kernel-isolated acceptance sweep (configuration 2).
+
+`--impl reference` times the reference's CPU path (restated in oracle/: torch
+fp32 target pass with the packed tree mask, fp32 softmax, the reference's
+fp64 inverse-CDF walk, KV commit) on the host cores, on a bounded sample of
+the same wave; it never loads the CUDA library.
 """
 from __future__ import annotations
 
@@ -39,16 +47,14 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 KV_BYTES_PER_TOKEN = 36 * 8 * 128 * 2 * 2  # layers x kv heads x head_dim x bf16 x {K,V}
+METRIC = "accepted tokens/s (total over GPUs)"
+UNIT = "accepted tokens/s"
 
-# DRAM bytes (read + write) of one layer's tree-attention launch on the
-# configuration-4 wave, from an ncu capture of that launch
-# (dram__bytes_read.sum 736.3 MB + dram__bytes_write.sum 15.5 MB).
+# DRAM bytes (read + write) per launch from ncu captures of the same kernels
+# (profiles/): the layer-0 tree attention and gate/up + SwiGLU GEMM on the
+# configuration-4 wave, and the acceptance launch of the configuration-2 sweep.
 NCU_ATTENTION_TRAFFIC_CFG4 = 736.310016e6 + 15.491584e6
-# Same for one gate/up + SwiGLU GEMM launch on the configuration-4 rows
-# (dram__bytes_read.sum 218.2 MB + dram__bytes_write.sum 41.1 MB).
 NCU_SWIGLU_TRAFFIC_CFG4 = 218.232576e6 + 41.149184e6
-# Same for one acceptance launch of the configuration-2 sweep
-# (dram__bytes_read.sum 53.6 MB + dram__bytes_write.sum 0.81 MB).
 NCU_ACCEPT_TRAFFIC_CFG2 = 53.622528e6 + 0.811264e6
 
 
@@ -58,6 +64,25 @@ def peaks():
         d = json.loads(path.read_text())
         return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
     return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def product_library_loaded() -> bool:
+    """Whether this process has mapped libspecgrove_b200.so."""
+    try:
+        return "libspecgrove_b200.so" in Path("/proc/self/maps").read_text()
+    except OSError:
+        return False
 
 
 class ClockSampler:
@@ -155,7 +180,7 @@ def dist_setup(args):
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    else:
+    elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return world, rank, local
 
@@ -184,11 +209,19 @@ def sum_over_ranks(value: float, world: int) -> float:
     return float(t.item())
 
 
+def make_events(n):
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+    for e in evs:           # materialise the cudaEvent_t handles
+        e.record()
+    torch.cuda.synchronize()
+    return evs
+
+
 # ---------------------------------------------------------------------------
-# Acceptance sweep workload
+# Acceptance sweep (configuration 2)
 # ---------------------------------------------------------------------------
 class AcceptWorkload:
-    name = "acceptance_sweep: 64 trees / 4096 nodes / V=151936 fp32 probs + KV commit 36x8x128 bf16"
+    name = "config2: acceptance sweep, 64 trees / 4096 nodes / V=151936 fp32 probs + KV commit 36x8x128 bf16"
 
     def __init__(self, rank: int):
         from specgrove_b200 import workloads
@@ -235,16 +268,92 @@ class AcceptWorkload:
         return int((outs[..., self.D] + 1).sum())
 
 
+def measure_accept(args, world, rank, wl=None):
+    """Acceptance + commit steps of configuration 2, L2 flushed between steps."""
+    from specgrove_b200 import _lib
+    hbm, _, _, peak_kind = peaks()
+    wl = wl or AcceptWorkload(rank)
+    K, W = args.steps, args.warmup
+    outs = torch.empty((K, wl.T, wl.D + 2), dtype=torch.long, device="cuda")
+    warm = torch.empty((wl.T, wl.D + 2), dtype=torch.long, device="cuda")
+    for i in range(W):
+        wl.step(10_000 + i, warm)
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # The rows a step visits (~55 MB, the 64 roots every step) fit in L2, so
+    # L2 is flushed between timed steps by writing a buffer four times its
+    # size; each step is timed by its own events, which exclude the flush.
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+    launches0 = _lib.launch_count()
+    barrier(world)
+    torch.cuda.synchronize()
+    # A step is two short kernels (~tens of us), less than the host needs to
+    # enqueue it; a device sleep ahead of the start event lets the host queue
+    # all K steps first, so the events time the kernels back to back instead
+    # of the host's enqueue gaps.
+    torch.cuda._sleep(int(4_000_000 * K))
+    start.record()
+    for i in range(K):
+        flush.fill_(i & 0xFF)
+        wl.step(i, outs[i], ev[i])
+    stop.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    launches = _lib.launch_count() - launches0
+    ms_local = statistics.mean(e[0].elapsed_time(e[2]) for e in ev)
+    ms = max_over_ranks(ms_local, world)
+    total_units = sum_over_ranks(wl.units(outs), world)
+    if int(wl.status) != 0:
+        raise RuntimeError(f"device status {int(wl.status)}")
+    accept_ms = [e[0].elapsed_time(e[1]) for e in ev]
+    commit_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    visited = (outs[..., wl.D] + 1).double()        # scan rule: accepted + exit row
+    accept_bytes = float(visited.sum()) / K * wl.vocab * 4
+    # kept tokens x 147,456 B, read and written (the reference's append copies
+    # every kept row); the root row and rows already at their final position
+    # never move, so the bytes actually moved are fewer
+    commit_bytes = float(visited.sum()) / K * KV_BYTES_PER_TOKEN * 2
+    moved = outs[..., :wl.D] >= 0
+    depth_idx = torch.arange(1, wl.D + 1, device=outs.device).expand_as(moved)
+    moved_rows = float((moved & (outs[..., :wl.D] != depth_idx)).sum()) / K
+    accept_gbs = accept_bytes / (statistics.mean(accept_ms) / 1000) / 1e9
+    commit_gbs = commit_bytes / (statistics.mean(commit_ms) / 1000) / 1e9
+    return {
+        "workload": wl.name, "value": total_units / (ms * K / 1000.0), "unit": UNIT, "ms_per_step": ms,
+        "launches": launches, "rule": "scan (Philox per node)",
+        "l2": "flushed between timed steps (512 MB write); ms_per_step = mean per-step event span "
+              "(acceptance + commit), flush excluded",
+        "ms_per_step_with_flush": start.elapsed_time(stop) / K,
+        "acceptance": {"bound": "hbm", "kernel": "accept_probs_kernel", "achieved": accept_gbs, "peak": hbm,
+                       "peak_kind": peak_kind, "unit": "GB/s", "frac": accept_gbs / hbm,
+                       "traffic": NCU_ACCEPT_TRAFFIC_CFG2, "algorithmic_bytes_per_launch": accept_bytes,
+                       "launch_ms": statistics.mean(accept_ms)},
+        "commit": {"bound": "hbm", "kernel": "kv_commit_accepted_kernel", "achieved": commit_gbs, "peak": hbm,
+                   "unit": "GB/s", "frac": commit_gbs / hbm, "algorithmic_bytes_per_launch": commit_bytes,
+                   "moved_bytes_per_launch": moved_rows * KV_BYTES_PER_TOKEN * 2,
+                   "launch_ms": statistics.mean(commit_ms)},
+    }
+
+
+# ---------------------------------------------------------------------------
+# Verify pass (configurations 3 and 4)
+# ---------------------------------------------------------------------------
+def wave_spec(config: str):
+    from specgrove_b200 import workloads
+    from specgrove_b200.engine import QWEN3_4B, QWEN3_8B
+    if config == "verify4b":
+        return (QWEN3_4B, workloads.TIER_MIX_CONFIG3, (512, 2048),
+                "config3: Qwen3-4B shape, 16 requests, prefixes U[512,2048], tiers {16,32,64}, 512 rows")
+    return (QWEN3_8B, workloads.TIER_MIX_CONFIG4, (1024, 4096),
+            "config4: Qwen3-8B shape, 64 requests, prefixes U[1024,4096], tiers {16,32,64,128}, 2048 rows")
+
+
 class VerifyWorkload:
     def __init__(self, rank: int, config: str, layers: int | None = None):
         from specgrove_b200 import workloads
-        from specgrove_b200.engine import QWEN3_4B, QWEN3_8B, B200Engine, Wave, Weights
-        if config == "verify4b":
-            self.shape, mix, prefix = QWEN3_4B, workloads.TIER_MIX_CONFIG3, (512, 2048)
-            self.name = "config3: Qwen3-4B shape, 16 requests, prefixes U[512,2048], tiers {16,32,64}, 512 rows"
-        else:
-            self.shape, mix, prefix = QWEN3_8B, workloads.TIER_MIX_CONFIG4, (1024, 4096)
-            self.name = "config4: Qwen3-8B shape, 64 requests, prefixes U[1024,4096], tiers {16,32,64,128}, 2048 rows"
+        from specgrove_b200.engine import B200Engine, Wave, Weights
+        self.shape, mix, prefix, self.name = wave_spec(config)
         if layers is not None and layers != self.shape.num_layers:
             import dataclasses
             # profiling captures only: fewer layers keep an ncu capture small
@@ -276,6 +385,10 @@ class VerifyWorkload:
             self.exchange = ScoreExchange(R, len(self.wl.tier_options), "cuda")
             self.exchange.pack(self.scores)
 
+    def close(self):
+        self.engine.close()
+        del self.engine, self.weights, self.dw
+
     def step(self, seed: int, out: torch.Tensor, trace=None):
         if self.exchange is not None:
             self.exchange.exchange()
@@ -301,26 +414,17 @@ class VerifyWorkload:
         return float(f)
 
 
-def make_events(n):
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
-    for e in evs:           # materialise the cudaEvent_t handles
-        e.record()
-    torch.cuda.synchronize()
-    return evs
-
-
-def run_verify(args, world, rank):
+def measure_verify(args, world, rank, wl):
+    """K untraced steps timed as one event span (max over ranks), then a few
+    traced steps for the per-stage split."""
     from specgrove_b200 import _lib
     from specgrove_b200.engine import TRACE_EVENTS, TRACE_STAGES
-    hbm, tc, tc_sus, peak_kind = peaks()
-    wl = VerifyWorkload(rank, args.workload, args.layers)
     K, W = args.steps, args.warmup
     outs = torch.empty((K, wl.R, wl.D + 2), dtype=torch.long, device="cuda")
     warm = torch.empty((wl.R, wl.D + 2), dtype=torch.long, device="cuda")
     for i in range(W):
         wl.step(10_000 + i, warm)
     torch.cuda.synchronize()
-    traces = [make_events(TRACE_EVENTS) for _ in range(K)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = _lib.launch_count()
     with ClockSampler(torch.cuda.current_device()) as clocks:
@@ -328,7 +432,7 @@ def run_verify(args, world, rank):
         torch.cuda.synchronize()
         start.record()
         for i in range(K):
-            wl.step(i, outs[i], traces[i])
+            wl.step(i, outs[i])
         stop.record()
         torch.cuda.synchronize()
         barrier(world)
@@ -337,9 +441,20 @@ def run_verify(args, world, rank):
         raise RuntimeError(f"device status {int(wl.engine.status)}")
     ms = max_over_ranks(start.elapsed_time(stop) / K, world)
     total_units = sum_over_ranks(wl.units(outs), world)
-    value = total_units / (ms * K / 1000.0)
+    # stage split from separate traced steps (events between the kernels)
+    traces = [make_events(TRACE_EVENTS) for _ in range(3)]
+    for i, t in enumerate(traces):
+        wl.step(20_000 + i, warm, t)
+    torch.cuda.synchronize()
     stages = {name: statistics.mean(t[i].elapsed_time(t[i + 1]) for t in traces)
               for i, name in enumerate(TRACE_STAGES)}
+    return dict(ms=ms, units=total_units, value=total_units / (ms * K / 1000.0), launches=launches,
+                stages=stages, clocks=clocks.summary(), outs=outs)
+
+
+def verify_rooflines(wl, m):
+    hbm, tc, tc_sus, peak_kind = peaks()
+    stages, ms = m["stages"], m["ms"]
     attn_ms = stages["L0 attention"]
     attn_bytes = wl.attention_bytes()                  # one layer's K/V reads
     attn_gbs = attn_bytes / (attn_ms / 1000) / 1e9
@@ -349,39 +464,78 @@ def run_verify(args, world, rank):
     gu_flops = 2.0 * wl.rows * (2 * wl.shape.intermediate) * wl.shape.hidden
     gu_tflops = gu_flops / (gu_ms / 1000) / 1e12
     cfg4 = wl.name.startswith("config4")
+    # dominant kernel by time: the gate/up GEMM with the SwiGLU epilogue
+    # (timed inside the step, so against the sustained bf16 peak)
+    return {"bound": "tensor", "kernel": "gemm_kernel<EpiSwiGlu> (layer 0 gate/up)",
+            "achieved": gu_tflops, "peak": tc_sus, "peak_kind": peak_kind + " sustained",
+            "unit": "TFLOP/s", "frac": gu_tflops / tc_sus,
+            "traffic": NCU_SWIGLU_TRAFFIC_CFG4 if cfg4 else None,
+            "traffic_source": "ncu capture, profiles/gemm_swiglu_cfg4_small.md" if cfg4 else None,
+            "algorithmic_flops_per_launch": gu_flops, "launch_ms": gu_ms,
+            "attention": {"bound": "hbm", "kernel": "tree_attention_tm_kernel (layer 0)",
+                          "achieved": attn_gbs, "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
+                          "frac": attn_gbs / hbm,
+                          "traffic": NCU_ATTENTION_TRAFFIC_CFG4 if cfg4 else None,
+                          "algorithmic_bytes_per_launch": attn_bytes, "launch_ms": attn_ms},
+            "pass": {"bound": "tensor", "achieved": pass_tflops, "peak": tc_sus, "unit": "TFLOP/s",
+                     "frac": pass_tflops / tc_sus, "algorithmic_flops_per_step": flops,
+                     "peak_kind": peak_kind + " sustained",
+                     "vs_burst_peak": {"peak": tc, "frac": pass_tflops / tc}}}
+
+
+def run_verify(args, world, rank):
+    wl = VerifyWorkload(rank, args.workload, args.layers)
+    m = measure_verify(args, world, rank, wl)
     e2e = e2e_verify(wl, args, world)
-    cpu = cpu_baseline_verify(wl) if (rank == 0 and world == 1 and not args.no_cpu) else None
-    clk = clocks.summary()
+    ms, value = m["ms"], m["value"]
     line = {
-        "metric": "accepted tokens/s/GPU", "value": value, "unit": "accepted tokens/s",
-        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+        "metric": METRIC, "value": value, "unit": UNIT,
+        "per_gpu": {"metric": "accepted tokens/s/GPU", "value": value / world},
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, "
         "synthetic KV prefixes, seeded best-first trees)",
         "config": {"workload": wl.name, "model": "Qwen3-8B shape" if wl.shape.hidden == 4096 else "Qwen3-4B shape",
                    "collective": "per-step NCCL all_gather_into_tensor of allocator scores" if world > 1 else None,
                    "requests_per_gpu": wl.R, "rows_per_gpu": wl.rows, "global_batch_rows": wl.rows * world,
                    "verify_pass_us_per_row": ms * 1000 / wl.rows, "temperature": 1.0,
-                   "parallelism": f"dp{world}", "l2": "inputs larger than L2 (16.4 GB weights, ~24 GB KV/step)"},
-        # dominant kernel by time: the gate/up GEMM with the SwiGLU epilogue
-        # (timed inside the step, so against the sustained bf16 peak)
-        "roofline": {"bound": "tensor", "kernel": "gemm_kernel<EpiSwiGlu> (layer 0 gate/up)",
-                     "achieved": gu_tflops, "peak": tc_sus, "peak_kind": peak_kind + " sustained",
-                     "unit": "TFLOP/s", "frac": gu_tflops / tc_sus,
-                     "traffic": NCU_SWIGLU_TRAFFIC_CFG4 if cfg4 else None,
-                     "algorithmic_flops_per_launch": gu_flops, "launch_ms": gu_ms,
-                     "attention": {"bound": "hbm", "kernel": "tree_attention_tm_kernel (layer 0)",
-                                   "achieved": attn_gbs, "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
-                                   "frac": attn_gbs / hbm,
-                                   "traffic": NCU_ATTENTION_TRAFFIC_CFG4 if cfg4 else None,
-                                   "algorithmic_bytes_per_launch": attn_bytes, "launch_ms": attn_ms},
-                     "pass": {"bound": "tensor", "achieved": pass_tflops, "peak": tc_sus, "unit": "TFLOP/s",
-                              "frac": pass_tflops / tc_sus, "algorithmic_flops_per_step": flops,
-                              "peak_kind": peak_kind + " sustained"}},
-        "stages_ms": {k: round(v, 4) for k, v in stages.items()},
+                   "parallelism": f"dp{world}", "l2": "inputs larger than L2 (16.4 GB weights, ~24 GB KV/step)",
+                   "timing": "K untraced steps between two events; stages_ms from 3 separate traced steps"},
+        "roofline": verify_rooflines(wl, m),
+        "stages_ms": {k: round(v, 4) for k, v in m["stages"].items()},
         "profiling_only": args.layers is not None and args.layers != 36,
-        "cpu_baseline": cpu, "clocks": clk, "e2e": e2e, "gpu_launches": launches,
+        "clocks": m["clocks"], "e2e": e2e, "gpu_launches": m["launches"],
     }
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline_verify(wl)
+    line["cpu_baseline"] = cpu
+    if world == 1 and not args.no_nested and args.layers is None and args.workload == "verify":
+        wl.close()
+        del wl
+        torch.cuda.empty_cache()
+        line["nested"] = nested_configs(args, world, rank)
     return line
+
+
+def nested_configs(args, world, rank):
+    """Configurations 2 and 3 measured in the same run as the headline."""
+    out = {}
+    acc = AcceptWorkload(rank)
+    out["config2"] = measure_accept(args, world, rank, acc)
+    del acc
+    torch.cuda.empty_cache()
+    wl3 = VerifyWorkload(rank, "verify4b")
+    m3 = measure_verify(args, world, rank, wl3)
+    r3 = verify_rooflines(wl3, m3)
+    out["config3"] = {"workload": wl3.name, "value": m3["value"], "unit": UNIT, "ms_per_step": m3["ms"],
+                      "verify_pass_us_per_row": m3["ms"] * 1000 / wl3.rows, "rows": wl3.rows,
+                      "pass": r3["pass"], "gate_up_gemm": {k: r3[k] for k in ("achieved", "frac", "launch_ms")},
+                      "attention": {k: r3["attention"][k] for k in ("achieved", "frac", "launch_ms")},
+                      "stages_ms": {k: round(v, 4) for k, v in m3["stages"].items()}}
+    wl3.close()
+    del wl3
+    torch.cuda.empty_cache()
+    return out
 
 
 def e2e_verify(wl, args, world):
@@ -412,122 +566,169 @@ def e2e_verify(wl, args, world):
     torch.cuda.synchronize()
     ms = max_over_ranks(start.elapsed_time(stop) / steps, world)
     total = sum_over_ranks(units, world)
-    return {"value": total / (ms * steps / 1000.0), "unit": "accepted tokens/s",
+    return {"value": total / (ms * steps / 1000.0), "unit": UNIT,
             "h2d_bytes_per_step": host.numel() * 8, "d2h_bytes_per_step": out_host.numel() * 8,
             "steps": steps, "ms_per_step": ms}
 
 
-def cpu_baseline_verify(wl, requests: int = 4, budget_s: float = 20.0):
-    """The reference's step restated on the host (oracle/forward.py: torch fp32
-    target pass with the packed tree mask, fp32 softmax, fp64 walk) on a
-    bounded slice: the first `requests` requests of the wave, all layers."""
-    from oracle.forward import CpuWeights, verify_step
+# ---------------------------------------------------------------------------
+# CPU path: the reference's step restated in oracle/ (torch fp32 + C walk)
+# ---------------------------------------------------------------------------
+class HostWeights:
+    """Random-init fp32 weights of a Qwen3 shape on the host, in the engine's
+    packed layout (oracle.forward.CpuWeights reads them).  One random layer
+    is generated and used by every layer: each layer's arithmetic is that of a
+    distinct random layer, without generating 8 B distinct host values."""
+
+    def __init__(self, shape, seed: int):
+        g = torch.Generator().manual_seed(seed)
+        H, D, I = shape.hidden, shape.head_dim, shape.intermediate
+        nq, nkv = shape.num_q_heads, shape.num_kv_heads
+        normal = lambda *size: torch.empty(size).normal_(0.0, 0.02, generator=g)
+        ones = lambda n: torch.ones(n)
+        self.shape = shape
+        self.embed = normal(shape.vocab, H)
+        self.lm_head = normal(shape.vocab, H)
+        self.final_norm = ones(H)
+        D2 = torch.arange(0, D, 2, dtype=torch.int64).float() / D
+        self.inv_freq = 1.0 / (shape.rope_theta ** D2)
+        layer = [ones(H), normal((nq + 2 * nkv) * D, H), ones(D), ones(D), normal(H, nq * D), ones(H),
+                 normal(2 * I, H), normal(H, I)]
+        self.layers = [layer] * shape.num_layers
+
+    def nbytes(self):
+        return 0
+
+
+def cpu_sample_requests(tiers, want=(16, 16, 32, 64)):
+    """Indices of a representative request sample: the first requests with
+    the given tiers (16, 16, 32, 64 rows: 32 rows per request, the wave's
+    own mean for configurations 3 and 4)."""
+    picked, used = [], set()
+    for t in want:
+        for i, ti in enumerate(tiers):
+            if ti == t and i not in used:
+                picked.append(i)
+                used.add(i)
+                break
+    return picked
+
+
+class CpuStep:
+    """One CPU verify step over a request sample: target pass (oracle.forward),
+    fp32 softmax, the reference's fp64 inverse-CDF walk (oracle C library,
+    Philox uniforms per node), and commit of the kept rows' K/V into each
+    request's tail (append_packed_sequence, decode.py:215-261)."""
+
+    def __init__(self, cw, trees, lengths, seed: int):
+        s = cw.shape
+        g = torch.Generator().manual_seed(seed)
+        self.cw, self.trees, self.lengths = cw, trees, lengths
+        self.prefixes = [[(torch.randn((s.num_kv_heads, L, s.head_dim), generator=g),
+                           torch.randn((s.num_kv_heads, L, s.head_dim), generator=g))
+                          for _ in range(s.num_layers)] for L in lengths]
+        self.tails = [[torch.zeros((2, s.num_kv_heads, len(par), s.head_dim)) for _ in range(s.num_layers)]
+                      for par, _ in trees]
+        self.parents = np.asarray([p for par, _ in trees for p in par], np.int64)
+        self.tokens = np.asarray([t if j else -1 for par, tok in trees for j, t in enumerate(tok)], np.int64)
+        self.depth = 0
+        for par, _ in trees:
+            d = [0] * len(par)
+            for j in range(1, len(par)):
+                d[j] = d[par[j]] + 1
+            self.depth = max(self.depth, max(d))
+        self.rows = len(self.parents)
+
+    def __call__(self, seed: int) -> int:
+        from oracle import cpu as oracle
+        from oracle.forward import verify_logits
+        logits, offsets, kv = verify_logits(self.cw, self.prefixes, self.trees, self.lengths, return_kv=True)
+        probs = torch.softmax(logits, dim=-1).numpy()
+        out, _ = oracle.accept_probs(probs, offsets, self.parents, self.tokens, self.depth, seed=seed,
+                                     request_ids=np.arange(len(self.trees)), arith=oracle.ARITH_FP64)
+        units = 0
+        for i, (r0, tail) in enumerate(zip(offsets, self.tails)):
+            count = int(out[i, self.depth])
+            keep = torch.tensor([0] + out[i, :count].tolist()) + r0
+            for l, (k, v) in enumerate(kv):
+                tail[l][0, :, :len(keep)] = k[keep].transpose(0, 1)
+                tail[l][1, :, :len(keep)] = v[keep].transpose(0, 1)
+            units += count + 1
+        return units
+
+
+def cpu_verify_arm(config: str, rank: int = 0):
+    """Host-only construction of the CPU step for a verify workload (no CUDA
+    library, no GPU memory): same shape, tier mix, prefix lengths and seeds."""
+    from oracle.forward import CpuWeights
+    from specgrove_b200 import workloads
+    shape, mix, prefix, name = wave_spec(config)
+    wl = workloads.verify_workload(shape.vocab, mix, prefix, seed=rank, device="cpu")
+    idx = cpu_sample_requests(wl.tiers)
+    cw = CpuWeights(HostWeights(shape, seed=1234), lazy=False)
+    step = CpuStep(cw, [wl.trees[i] for i in idx], [wl.cache_lengths[i] for i in idx], seed=rank)
+    return name, step, idx, wl
+
+
+def cpu_baseline_verify(wl, budget_s: float = 20.0):
+    """The CPU leg of the headline line (rank 0, N = 1): the CPU step over a
+    representative sample of the same wave, all host threads."""
     torch.set_num_threads(os.cpu_count())
-    cw = CpuWeights(wl.weights)
-    trees = wl.wl.trees[:requests]
-    lengths = wl.wl.cache_lengths[:requests]
-    store = wl.engine.arena
-    prefixes = []
-    for i, L in enumerate(lengths):
-        base = i * store.capacity
-        prefixes.append([(store.key_storage[l][:, base:base + L].float().cpu(),
-                          store.value_storage[l][:, base:base + L].float().cpu())
-                         for l in range(wl.shape.num_layers)])
-    rows = sum(len(t[0]) for t in trees)
+    name, step, idx, _ = cpu_verify_arm("verify4b" if wl.name.startswith("config3") else "verify")
     units, seconds, reps = 0, 0.0, 0
     while reps < 1 or (seconds < budget_s and reps < 5):
         t0 = time.perf_counter()
-        res, _ = verify_step(cw, prefixes, trees, lengths, seed=reps)
+        units += step(reps)
         seconds += time.perf_counter() - t0
-        units += sum(len(nodes) + 1 for nodes, _ in res)
         reps += 1
-    return {"value": units / seconds, "unit": "accepted tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "us_per_row": seconds / reps / rows * 1e6,
-            "sample": f"{reps} step(s) of {requests} requests ({rows} rows), all {wl.shape.num_layers} layers, "
-                      f"torch fp32 on {torch.get_num_threads()} threads"}
+    return {"value": units / seconds, "unit": UNIT, "cores": torch.get_num_threads(), "cpu_model": cpu_model(),
+            "kind": "port", "us_per_row": seconds / reps / step.rows * 1e6,
+            "sample": f"{reps} step(s) of {len(idx)} requests (tiers 16/16/32/64, {step.rows} rows) of the same "
+                      f"wave, all {step.cw.shape.num_layers} layers, torch fp32 + fp64 walk + KV commit on "
+                      f"{torch.get_num_threads()} threads"}
 
 
-def run_b200(args, world, rank):
-    from specgrove_b200 import _lib
-    hbm, tc, tc_sus, peak_kind = peaks()
+def cpu_baseline_accept(wl, arith=None):
+    """The reference's rule (sequential fp64 running sums, the CPU helper of
+    fused_tree_sampling.py:2607-2612) over the same trees, all host cores."""
+    from oracle import cpu as oracle
+    probs = wl.probs.cpu().numpy()
+    parents, tokens = wl.batch.flat()
+    arith = oracle.ARITH_FP64 if arith is None else arith
+    rng = np.random.default_rng(0)
+    units, seconds, reps = 0, 0.0, 0
+    while seconds < 10.0 and reps < 50:
+        uniforms = rng.random((wl.T, wl.D + 1))
+        t0 = time.perf_counter()
+        out, _ = oracle.accept_probs(probs, wl.batch.row_offsets, parents, tokens, wl.D, uniforms=uniforms,
+                                     arith=arith)
+        seconds += time.perf_counter() - t0
+        units += int((out[:, wl.D] + 1).sum())
+        reps += 1
+    return {"value": units / seconds, "unit": UNIT, "cores": 1, "cpu_model": cpu_model(),
+            "kind": "port", "sample": f"{reps} full acceptance steps (64 trees, explicit uniforms, "
+                                      "fp64 running-sum rule, one thread); KV commit not included"}
+
+
+def run_accept(args, world, rank):
     wl = AcceptWorkload(rank)
-    K, W = args.steps, args.warmup
-    outs = torch.empty((K, wl.T, wl.D + 2), dtype=torch.long, device="cuda")
-    warm = torch.empty((wl.T, wl.D + 2), dtype=torch.long, device="cuda")
-    for i in range(W):
-        wl.step(10_000 + i, warm)
-    torch.cuda.synchronize()
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # The rows a step visits (~55 MB, the 64 roots every step) fit in L2, so
-    # L2 is flushed between timed steps by writing a buffer four times its
-    # size; each step is timed by its own events, which exclude the flush.
-    flush = torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
-    launches0 = _lib.launch_count()
     with ClockSampler(torch.cuda.current_device()) as clocks:
-        barrier(world)
-        torch.cuda.synchronize()
-        # A step is two short kernels (~tens of us), less than the host needs
-        # to enqueue it; a device sleep ahead of the start event lets the host
-        # queue all K steps first, so the events time the kernels back to
-        # back instead of the host's enqueue gaps.
-        torch.cuda._sleep(int(4_000_000 * K))
-        start.record()
-        for i in range(K):
-            flush.fill_(i & 0xFF)
-            wl.step(i, outs[i], ev[i])
-        stop.record()
-        torch.cuda.synchronize()
-        barrier(world)
-    launches = _lib.launch_count() - launches0
-    ms_with_flush = start.elapsed_time(stop) / K
-    ms_local = statistics.mean(e[0].elapsed_time(e[2]) for e in ev)
-    ms = max_over_ranks(ms_local, world)
-    units_local = wl.units(outs)
-    total_units = sum_over_ranks(units_local, world)
-    value = total_units / (ms * K / 1000.0)
-    if int(wl.status) != 0:
-        raise RuntimeError(f"device status {int(wl.status)}")
-    # roofline of the dominant kernel (acceptance): visited rows x V x 4 bytes per launch
-    accept_ms = [e[0].elapsed_time(e[1]) for e in ev]
-    commit_ms = [e[1].elapsed_time(e[2]) for e in ev]
-    visited = (outs[..., wl.D] + 1).double()        # scan rule: accepted + exit row
-    accept_bytes = float(visited.sum()) / K * wl.vocab * 4
-    # kept tokens x 147,456 B, read and written (the reference's append copies
-    # every kept row); here the root row and rows already at their final
-    # position never move, so the bytes actually moved are fewer
-    commit_bytes = float(visited.sum()) / K * KV_BYTES_PER_TOKEN * 2
-    moved = outs[..., :wl.D] >= 0
-    depth_idx = torch.arange(1, wl.D + 1, device=outs.device).expand_as(moved)
-    moved_rows = float((moved & (outs[..., :wl.D] != depth_idx)).sum()) / K
-    moved_bytes = moved_rows * KV_BYTES_PER_TOKEN * 2
-    accept_gbs = accept_bytes / (statistics.mean(accept_ms) / 1000) / 1e9
-    commit_gbs = commit_bytes / (statistics.mean(commit_ms) / 1000) / 1e9
-    # e2e through the public API with host buffers: probabilities and tree
-    # metadata copied from pinned host memory, decisions read back, per step.
+        m = measure_accept(args, world, rank, wl)
     e2e = e2e_accept(wl, args, world)
     cpu = cpu_baseline_accept(wl) if (rank == 0 and world == 1 and not args.no_cpu) else None
-    clk = clocks.summary()
-    line = {
-        "metric": "accepted tokens/s/GPU", "value": value, "unit": "accepted tokens/s",
-        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+    roof = dict(m["acceptance"])
+    roof["commit"] = m["commit"]
+    return {
+        "metric": METRIC, "value": m["value"], "unit": UNIT,
+        "per_gpu": {"metric": "accepted tokens/s/GPU", "value": m["value"] / world},
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": m["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
         "config": {"workload": wl.name, "trees_per_gpu": wl.T, "nodes_per_gpu": wl.trees.total_rows,
-                   "vocab": wl.vocab, "rule": "scan (Philox per node)", "parallelism": f"dp{world}",
-                   "l2": "flushed between timed steps (512 MB write); ms_per_step = mean per-step event span "
-                         "(acceptance + commit), flush excluded",
-                   "ms_per_step_with_flush": ms_with_flush},
-        "roofline": {"bound": "hbm", "kernel": "accept_probs_kernel", "achieved": accept_gbs, "peak": hbm,
-                     "peak_kind": peak_kind, "unit": "GB/s", "frac": accept_gbs / hbm,
-                     "traffic": NCU_ACCEPT_TRAFFIC_CFG2,
-                     "algorithmic_bytes_per_launch": accept_bytes,
-                     "launch_ms": statistics.mean(accept_ms),
-                     "commit": {"achieved": commit_gbs, "frac": commit_gbs / hbm,
-                                "bytes_per_launch": commit_bytes, "moved_bytes_per_launch": moved_bytes,
-                                "launch_ms": statistics.mean(commit_ms)}},
-        "cpu_baseline": cpu, "clocks": clk, "e2e": e2e, "gpu_launches": launches,
+                   "vocab": wl.vocab, "rule": m["rule"], "parallelism": f"dp{world}", "l2": m["l2"],
+                   "ms_per_step_with_flush": m["ms_per_step_with_flush"]},
+        "roofline": roof, "cpu_baseline": cpu, "clocks": clocks.summary(), "e2e": e2e,
+        "gpu_launches": m["launches"],
     }
-    return line
 
 
 def e2e_accept(wl, args, world):
@@ -569,53 +770,60 @@ def e2e_accept(wl, args, world):
     torch.cuda.synchronize()
     ms = max_over_ranks(start.elapsed_time(stop) / steps, world)
     total = sum_over_ranks(units, world)
-    return {"value": total / (ms * steps / 1000.0), "unit": "accepted tokens/s",
+    return {"value": total / (ms * steps / 1000.0), "unit": UNIT,
             "h2d_bytes_per_step": probs_host.numel() * 4 + meta_host.numel() * 8,
             "d2h_bytes_per_step": out_host.numel() * 8, "steps": steps, "ms_per_step": ms}
 
 
-def cpu_baseline_accept(wl, arith=None):
-    """The reference's rule (sequential fp64 running sums, the CPU helper of
-    fused_tree_sampling.py:2607-2612) over the same trees, all host cores."""
-    from oracle import cpu as oracle
-    probs = wl.probs.cpu().numpy()
-    parents, tokens = wl.batch.flat()
-    arith = oracle.ARITH_FP64 if arith is None else arith
-    rng = np.random.default_rng(0)
-    units, seconds, reps = 0, 0.0, 0
-    while seconds < 10.0 and reps < 50:
-        uniforms = rng.random((wl.T, wl.D + 1))
-        t0 = time.perf_counter()
-        out, _ = oracle.accept_probs(probs, wl.batch.row_offsets, parents, tokens, wl.D, uniforms=uniforms,
-                                     arith=arith)
-        seconds += time.perf_counter() - t0
-        units += int((out[:, wl.D] + 1).sum())
-        reps += 1
-    return {"value": units / seconds, "unit": "accepted tokens/s", "cores": os.cpu_count(),
-            "kind": "port", "sample": f"{reps} full acceptance steps (64 trees, explicit uniforms, "
-                                      "fp64 running-sum rule); KV commit not included"}
-
-
 def run_reference(args, world, rank):
-    """The reference's CPU path for the same workload and metric: the oracle
-    port (the reference's step restated in torch fp32 / C), all host cores."""
+    """The reference's CPU path for the same workload, metric and config, on
+    the host cores; never loads the CUDA library.  Under torchrun only rank 0
+    runs it."""
     if rank != 0:
         return None
+    torch.set_num_threads(os.cpu_count())
+    K, W = args.steps, args.warmup
     if args.workload == "accept":
-        wl = AcceptWorkload(rank)
-        cpu = cpu_baseline_accept(wl)
-        dtype = "fp64"
+        from oracle import cpu as oracle
+        from specgrove_b200 import workloads
+        batch, probs = workloads.acceptance_sweep(seed=rank, device="cpu")
+        probs = probs.numpy()
+        parents, tokens = batch.flat()
+        D = batch.max_depth
+        rng = np.random.default_rng(0)
+
+        def step(i):
+            u = rng.random((len(batch.parents), D + 1))
+            out, _ = oracle.accept_probs(probs, batch.row_offsets, parents, tokens, D, uniforms=u,
+                                         arith=oracle.ARITH_FP64)
+            return int((out[:, D] + 1).sum())
+        name, sample, dtype = AcceptWorkload.name, "every step: the full 64-tree sweep, fp64 rule", "fp64"
+        rows = batch.total_rows
     else:
-        wl = VerifyWorkload(rank, args.workload, args.layers)
-        cpu = cpu_baseline_verify(wl, requests=2, budget_s=10.0)
+        name, cstep, idx, wl = cpu_verify_arm(args.workload, rank)
+        step = cstep
+        rows = cstep.rows
+        sample = (f"every step: {len(idx)} of the wave's {len(wl.trees)} requests (tiers 16/16/32/64, "
+                  f"{rows} rows, 32 rows per request like the full wave), all layers; torch fp32 target pass, "
+                  f"fp32 softmax, fp64 inverse-CDF walk, KV commit")
         dtype = "fp32"
-    line = {"impl": "reference", "metric": "accepted tokens/s/GPU", "value": cpu["value"],
-            "unit": "accepted tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+    for i in range(W):
+        step(10_000 + i)
+    units, t0 = 0, time.perf_counter()
+    for i in range(K):
+        units += step(i)
+    seconds = time.perf_counter() - t0
+    value = units / seconds
+    cpu = {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "cpu_model": cpu_model(),
+           "kind": "port", "sample": sample, "us_per_row": seconds / K / rows * 1e6}
+    return {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": seconds / K * 1000,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
-            "data": "synthetic", "config": {"workload": wl.name, "parallelism": "cpu"},
-            "cpu_baseline": cpu, "e2e": {"value": cpu["value"], "unit": "accepted tokens/s",
-                                         "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    return line
+            "data": "synthetic", "config": {"workload": name, "parallelism": "cpu", "same_config": True,
+                                            "rows_per_step": rows},
+            "cpu_baseline": cpu, "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                                         "d2h_bytes_per_step": 0},
+            "product_library_loaded": product_library_loaded()}
 
 
 def main():
@@ -626,17 +834,25 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="verify", choices=["verify", "verify4b", "accept"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-nested", action="store_true", help="skip the nested configuration-2/3 blocks")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: build the model with this many layers (not a benchmark number)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.impl == "reference":
+        # host-only: no process group, no CUDA context; rank 0 alone measures
+        world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+        line = run_reference(args, world, rank)
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+        return
     world, rank, local = dist_setup(args)
     try:
         if args.impl == "reference":
             line = run_reference(args, world, rank)
         elif args.workload == "accept":
-            line = run_b200(args, world, rank)
+            line = run_accept(args, world, rank)
         else:
             line = run_verify(args, world, rank)
         if rank == 0 and line is not None:

@@ -285,6 +285,22 @@ typedef struct {
   int32_t* status;               /* optional device status word */
   void* const* trace_events;     /* optional host array of SG_TRACE_EVENTS
                                     cudaEvent_t recorded at stage boundaries */
+  /* Drafter feature hand-off (continuous_tree_block_decode.py:2144-2158: the
+   * decoder concatenates output.hidden_states[l + 1] of every
+   * engine.draft.target_layer_ids layer l and keeps the rows [0] + accepted
+   * nodes of each request).  hidden_states[l + 1] is the residual stream after
+   * layer l, and for the last layer the final-normed stream, as in HF Qwen3. */
+  int32_t num_feature_layers;    /* 0: no features */
+  const int32_t* feature_layers; /* HOST array [num_feature_layers], each in [0, num_layers) */
+  void* features_out;            /* bf16 [Q, num_feature_layers * hidden], 16-byte aligned:
+                                    layer feature_layers[f] in columns
+                                    [f * hidden, (f + 1) * hidden); written by the
+                                    layers' residual GEMM epilogues */
+  void* features_kept;           /* optional bf16 [<= Q, num_feature_layers * hidden]:
+                                    the rows [0] + accepted nodes of every
+                                    request, requests in order */
+  int64_t* features_kept_offsets;/* [R + 1] row offsets of each request's kept
+                                    rows in features_kept (with features_kept) */
 } sg_wave_desc;
 
 /* Stage boundaries recorded into sg_wave_desc.trace_events (the stage

@@ -250,6 +250,19 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
     return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: temperature must be finite and >= 0 (0 = greedy)");
   const bool greedy = w.temperature == 0.f;
   const float inv_temp = greedy ? 1.0f : 1.0f / w.temperature;
+  // feature slot of every layer (-1: not a drafter feature layer)
+  std::vector<int> feature_slot(static_cast<size_t>(m.num_layers), -1);
+  const int nfeat = w.num_feature_layers;
+  if (nfeat < 0 || (nfeat > 0 && (w.feature_layers == nullptr || w.features_out == nullptr ||
+                                  (reinterpret_cast<uintptr_t>(w.features_out) & 15u) != 0)))
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: feature layers need a 16-byte aligned features_out");
+  for (int f = 0; f < nfeat; ++f) {
+    const int l = w.feature_layers[f];
+    if (l < 0 || l >= m.num_layers) return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: feature layer out of range");
+    feature_slot[l] = f;
+  }
+  if (w.features_kept != nullptr && (nfeat == 0 || w.features_kept_offsets == nullptr))
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: features_kept needs feature layers and offsets");
   int dev = 0;
   SG_CUDA_CHECK(cudaGetDevice(&dev));
   if (dev != e->device) return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: engine belongs to another device");
@@ -365,7 +378,12 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
     gemm::EpiSwiGlu::Params pg{e->h, I, w.status};
     if ((st = gemm::launch<gemm::EpiSwiGlu>(e->xn_map, lm.gate_up, s_gu, pg, stream, small_wave(s_gu))) != SG_OK) return st;
     if (l == 0) trace(w, 8, stream);
-    gemm::EpiResidual::Params pd{e->x, H, nullptr, 0, w.status};
+    // the residual stream after this layer is hidden_states[l + 1]; the last
+    // layer's entry is the final-normed stream, copied after the final norm
+    __nv_bfloat16* feat = nullptr;
+    if (feature_slot[l] >= 0 && l + 1 < m.num_layers)
+      feat = static_cast<__nv_bfloat16*>(w.features_out) + static_cast<int64_t>(feature_slot[l]) * H;
+    gemm::EpiResidual::Params pd{e->x, H, feat, static_cast<int64_t>(nfeat) * H, w.status};
     if ((st = gemm::launch<gemm::EpiResidual>(e->h_map, lm.down, s_down, pd, stream, small_wave(s_down))) != SG_OK) return st;
     if (l == 0) trace(w, 9, stream);
   }
@@ -376,6 +394,13 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
   if ((st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(m.final_norm), H, Q, m.rms_eps, e->xn,
                                    stream)) != SG_OK)
     return st;
+  if (feature_slot[m.num_layers - 1] >= 0) {
+    const size_t pitch = static_cast<size_t>(nfeat) * H * 2;
+    SG_CUDA_CHECK(cudaMemcpy2DAsync(static_cast<uint8_t*>(w.features_out) +
+                                        static_cast<size_t>(feature_slot[m.num_layers - 1]) * H * 2,
+                                    pitch, e->xn, static_cast<size_t>(H) * 2, static_cast<size_t>(H) * 2, Q,
+                                    cudaMemcpyDeviceToDevice, stream));
+  }
   trace(w, 11, stream);
   gemm::EpiLmHead::Params pl;
   pl.partials = e->partials;
@@ -402,6 +427,11 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
   trace(w, 13, stream);
   if ((st = sg_tree_follow(posterior, w.row_offsets, w.parents, w.tokens, R, w.max_rows_per_request, w.max_depth,
                            w.accept_out, w.status, stream)) != SG_OK)
+    return st;
+  if (w.features_kept != nullptr &&
+      (st = layers::launch_gather_kept_rows(w.features_out, static_cast<int64_t>(nfeat) * H * 2, w.row_offsets,
+                                            w.accept_out, R, w.max_depth, w.features_kept, w.features_kept_offsets,
+                                            w.status, stream)) != SG_OK)
     return st;
   trace(w, 14, stream);
   if (w.commit) {

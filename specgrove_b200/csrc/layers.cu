@@ -476,7 +476,62 @@ __global__ void child_logprob_kernel(const __nv_bfloat16* __restrict__ h, const 
   if (lane == 0) logprob[row] = acc * inv_temp - lse[prow];
 }
 
+// One CTA per request: its kept rows go to dst rows base .. base + count,
+// base = kept rows of the earlier requests (summed by the CTA itself).
+// Counts or nodes outside the tree are reported and their rows skipped.
+__global__ void __launch_bounds__(256) gather_kept_rows_kernel(const uint4* __restrict__ src, int64_t row_vecs,
+                                                               const int64_t* __restrict__ row_offsets,
+                                                               const int64_t* __restrict__ accept_out,
+                                                               int num_trees, int max_depth, uint4* __restrict__ dst,
+                                                               int64_t* __restrict__ dst_offsets, int32_t* status) {
+  __shared__ int64_t s_part[8];
+  const int t = blockIdx.x;
+  const int stride = max_depth + 2;
+  auto kept = [&](int tree) -> int64_t {
+    const int64_t c = accept_out[static_cast<int64_t>(tree) * stride + max_depth];
+    return (c >= 0 && c <= max_depth) ? c + 1 : 0;
+  };
+  int64_t part = 0;
+  for (int u = threadIdx.x; u < t; u += blockDim.x) part += kept(u);
+#pragma unroll
+  for (int d = 16; d >= 1; d >>= 1) part += __shfl_xor_sync(0xffffffffu, part, d);
+  if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = part;
+  __syncthreads();
+  int64_t base = 0;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) base += s_part[w];
+  const int64_t count = kept(t);
+  if (threadIdx.x == 0) {
+    if (count == 0) report(status, SG_ERR_TREE);
+    if (t == 0) dst_offsets[0] = 0;
+    dst_offsets[t + 1] = base + count;
+  }
+  const int64_t r0 = row_offsets[t], n = row_offsets[t + 1] - r0;
+  for (int64_t j = 0; j < count; ++j) {
+    const int64_t node = j == 0 ? 0 : accept_out[static_cast<int64_t>(t) * stride + j - 1];
+    if (node < 0 || node >= n) {
+      if (threadIdx.x == 0) report(status, SG_ERR_TREE);
+      continue;
+    }
+    const uint4* s = src + (r0 + node) * row_vecs;
+    uint4* o = dst + (base + j) * row_vecs;
+    for (int64_t v = threadIdx.x; v < row_vecs; v += blockDim.x) o[v] = s[v];
+  }
+}
+
 }  // namespace
+
+int launch_gather_kept_rows(const void* src, int64_t row_bytes, const int64_t* row_offsets, const int64_t* accept_out,
+                            int num_trees, int max_depth, void* dst, int64_t* dst_offsets, int32_t* status,
+                            cudaStream_t stream) {
+  if (num_trees <= 0) return SG_OK;
+  if (row_bytes <= 0 || row_bytes % 16 != 0 || (reinterpret_cast<uintptr_t>(src) & 15u) != 0 ||
+      (reinterpret_cast<uintptr_t>(dst) & 15u) != 0)
+    return fail(SG_ERR_INVALID_ARGUMENT, "gather of kept rows: rows and buffers must be 16-byte aligned");
+  gather_kept_rows_kernel<<<num_trees, 256, 0, stream>>>(static_cast<const uint4*>(src), row_bytes / 16, row_offsets,
+                                                         accept_out, num_trees, max_depth, static_cast<uint4*>(dst),
+                                                         dst_offsets, status);
+  return check_launch("gather_kept_rows_kernel");
+}
 
 int launch_attention_work(const int64_t* row_offsets, const int64_t* cache_len, int num_trees, int group,
                           int num_kv_heads, AttentionWork work, int num_layers, cudaStream_t stream) {

@@ -80,6 +80,14 @@ int launch_qkv_post(const QkvPost& p, cudaStream_t stream);
 int launch_lm_combine(const float4* partials, int n_tiles, int rows, float* lse, int64_t* posterior,
                       const int32_t* abort_status, cudaStream_t stream);
 
+// Gather each request's kept rows ([0] + accepted nodes, read from the
+// acceptance output accept_out[t, max_depth + 2]) of `src` (row_bytes per
+// row, rows packed by row_offsets) into `dst`, requests in order, and write
+// dst_offsets[t] .. dst_offsets[t + 1] for each.  row_bytes % 16 == 0.
+int launch_gather_kept_rows(const void* src, int64_t row_bytes, const int64_t* row_offsets, const int64_t* accept_out,
+                            int num_trees, int max_depth, void* dst, int64_t* dst_offsets, int32_t* status,
+                            cudaStream_t stream);
+
 int launch_child_logprob(const __nv_bfloat16* h, const __nv_bfloat16* lm_head, int hidden, int64_t vocab,
                          const int64_t* tokens,
                          const int64_t* parents, const int64_t* row_offsets, const int32_t* tree,

@@ -84,7 +84,10 @@ class _WaveDesc(ctypes.Structure):
                 ("commit", ctypes.c_int32), ("accept_out", ctypes.c_void_p), ("lengths_out", ctypes.c_void_p),
                 ("posterior", ctypes.c_void_p), ("lse", ctypes.c_void_p), ("child_logprob", ctypes.c_void_p),
                 ("hidden_out", ctypes.c_void_p), ("status", ctypes.c_void_p),
-                ("trace_events", ctypes.POINTER(ctypes.c_void_p))]
+                ("trace_events", ctypes.POINTER(ctypes.c_void_p)),
+                ("num_feature_layers", ctypes.c_int32), ("feature_layers", ctypes.POINTER(ctypes.c_int32)),
+                ("features_out", ctypes.c_void_p), ("features_kept", ctypes.c_void_p),
+                ("features_kept_offsets", ctypes.c_void_p)]
 
 TRACE_EVENTS = 16
 TRACE_STAGES = ["meta+embed", "L0 in-norm", "L0 qkv gemm", "L0 qk-norm+rope+kv", "L0 attention", "L0 o gemm",
