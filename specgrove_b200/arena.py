@@ -13,12 +13,12 @@ launch over every plane instead of four launches per layer.
 """
 from __future__ import annotations
 
+from contextlib import nullcontext
 from typing import Sequence
 
 import torch
 
-from . import _lib
-from ._lib import check, ptr, stream_ptr
+from . import ops
 
 
 class ArenaLayer:
@@ -117,12 +117,10 @@ class PersistentKVArena:
         meta = meta.pin_memory().to(self.storage.device, non_blocking=True)
         n = len(src_rows)
         self._status.zero_()
-        st = _lib.load().sg_kv_commit(
-            ptr(self.storage), self.plane_rows, ptr(src_base), src_plane_rows, self.num_planes,
-            self.row_bytes, ptr(meta[:n]), ptr(meta[n:2 * n]), ptr(meta[2 * n:]),
-            len(group_sizes), max(group_sizes) if group_sizes else 0, ptr(self._status),
-            stream_ptr(stream))
-        check(st, "sg_kv_commit")
+        src = src_base.view(-1, src_plane_rows, self.head_dim)
+        with torch.cuda.stream(stream) if stream is not None else nullcontext():
+            ops.load().kv_commit(self.storage, src, meta[:n], meta[n:2 * n], meta[2 * n:],
+                                 max(group_sizes) if group_sizes else 0, self._status)
 
     def commit_tail(self, slots: Sequence[int], keep_rows: Sequence[Sequence[int]], stream=None):
         """In-place commit: the wave wrote its tree rows at ``old_length + j``
@@ -171,17 +169,14 @@ class PersistentKVArena:
             meta = meta.pin_memory()
         meta = meta.to(self.storage.device, non_blocking=True)
         n = len(src_rows)
-        lib = _lib.load()
+        commit = ops.load().kv_commit
         for l, layer in enumerate(packed.layers):
             for kv, src in ((0, layer.keys), (1, layer.values)):
                 src = src.contiguous()
                 if src.dtype != self.storage.dtype or src.shape[-1] != self.head_dim:
                     raise ValueError("Packed cache dtype/head_dim differ from the arena")
                 dst = self.storage[l, kv]
-                st = lib.sg_kv_commit(ptr(dst), self.plane_rows, ptr(src), src.shape[-2],
-                                      self.num_kv_heads, self.row_bytes, ptr(meta[:n]),
-                                      ptr(meta[n:2 * n]), ptr(meta[2 * n:]), len(groups),
-                                      max(groups), ptr(self._status), stream_ptr(None))
-                check(st, "sg_kv_commit")
+                commit(dst, src.view(-1, src.shape[-2], self.head_dim), meta[:n], meta[n:2 * n], meta[2 * n:],
+                       max(groups), self._status)
         for slot, inc in increments:
             self.lengths[slot] += inc

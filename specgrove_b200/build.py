@@ -72,12 +72,45 @@ def build(verbose: bool = False, jobs: int | None = None) -> Path:
         tmp = LIBRARY.with_suffix(".so.tmp")
         # cudart is linked statically; driver entry points are resolved at run
         # time (cudaGetDriverEntryPoint), so the library loads without a GPU.
-        cmd = [nvcc(), *ARCH_FLAGS, "-shared", "-o", str(tmp), *map(str, objs)]
+        # The soname lets the torch-op extension's dependency resolve to the
+        # copy ctypes already loaded (one set of library state per process).
+        cmd = [nvcc(), *ARCH_FLAGS, "-shared", "-Xlinker", f"-soname={LIBRARY.name}", "-o", str(tmp),
+               *map(str, objs)]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
         os.replace(tmp, LIBRARY)
+    build_torch_ops(verbose)
     return LIBRARY
+
+
+TORCH_OPS_SOURCE = CSRC / "torch_ops.cpp"
+TORCH_OPS = PACKAGE_DIR / "_torch_ops.so"
+
+
+def build_torch_ops(verbose: bool = False) -> Path:
+    """The torch custom-op extension (torch.ops.specgrove_b200.*): host C++
+    compiled by g++ against torch's headers, linked to the C-ABI library."""
+    if not _stale(TORCH_OPS, [TORCH_OPS_SOURCE, LIBRARY, *sorted(INCLUDE.glob("*.h"))]):
+        return TORCH_OPS
+    import torch
+    from torch.utils import cpp_extension as ce
+    torch_dir = Path(torch.__file__).resolve().parent
+    includes = [torch_dir / "include", torch_dir / "include" / "torch" / "csrc" / "api" / "include",
+                Path(os.environ.get("CUDA_HOME", "/usr/local/cuda")) / "include", INCLUDE]
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    tmp = TORCH_OPS.with_suffix(".so.tmp")
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           "-DTORCH_EXTENSION_NAME=_torch_ops", *[f"-I{p}" for p in includes], str(TORCH_OPS_SOURCE),
+           "-o", str(tmp), f"-L{torch_dir / 'lib'}", f"-L{PACKAGE_DIR}", f"-l:{LIBRARY.name}",
+           "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda",
+           "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_dir / 'lib'}"]
+    del ce
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, TORCH_OPS)
+    return TORCH_OPS
 
 
 if __name__ == "__main__":

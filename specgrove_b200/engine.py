@@ -16,13 +16,14 @@ Weights are either random-initialised with the Qwen3 architecture shapes
 from __future__ import annotations
 
 import ctypes
+from contextlib import nullcontext
 from dataclasses import dataclass
 from typing import Sequence
 
 import numpy as np
 import torch
 
-from . import _lib
+from . import _lib, ops
 from ._lib import check, ptr, stream_ptr
 from .arena import PersistentKVArena
 from .sampling import _topology
@@ -292,8 +293,15 @@ class B200Engine:
                       accept_out: torch.Tensor | None = None, lengths_out: torch.Tensor | None = None,
                       posterior: torch.Tensor | None = None, lse: torch.Tensor | None = None,
                       child_logprob: torch.Tensor | None = None, hidden_out: torch.Tensor | None = None,
+                      feature_layers: Sequence[int] = (), features_out: torch.Tensor | None = None,
+                      features_kept: torch.Tensor | None = None, features_kept_offsets: torch.Tensor | None = None,
                       max_depth: int | None = None, stream=None, trace=None) -> torch.Tensor:
-        """Enqueue one verify pass (no host synchronisation)."""
+        """Enqueue one verify pass (no host synchronisation).
+
+        ``feature_layers`` / ``features_out`` (bf16 [rows, len(layers) * hidden])
+        export HF's ``hidden_states[l + 1]`` of those layers for every packed
+        row; ``features_kept`` / ``features_kept_offsets`` also gather each
+        request's rows [0] + accepted nodes (the drafter's next input)."""
         w = dw.wave
         for s, L, (r0, r1) in zip(w.slots, w.cache_lengths, zip(w.row_offsets, w.row_offsets[1:])):
             if not 0 <= s < self.arena.num_slots:
@@ -307,15 +315,40 @@ class B200Engine:
             accept_out = torch.empty((w.num_requests, D + 2), dtype=torch.long, device=self.device)
         if commit and lengths_out is None:
             lengths_out = torch.empty(w.num_requests, dtype=torch.long, device=self.device)
-        desc = _WaveDesc(w.num_requests, w.num_rows, w.max_rows_per_request, D, ptr(dw.row_offsets), ptr(dw.parents),
-                         ptr(dw.tokens), ptr(dw.slots), ptr(dw.cache_lengths), ptr(dw.position_base),
-                         ptr(dw.request_ids), seed & ((1 << 64) - 1), float(temperature), int(bool(commit)),
-                         ptr(accept_out), ptr(lengths_out), ptr(posterior), ptr(lse), ptr(child_logprob),
-                         ptr(hidden_out), ptr(self.status), None)
-        if trace is not None:
+        if feature_layers:
+            H = self.shape.hidden
+            if (features_out is None or features_out.dtype != torch.bfloat16 or not features_out.is_contiguous()
+                    or features_out.shape[0] < w.num_rows or features_out.shape[-1] != len(feature_layers) * H):
+                raise ValueError("features_out must be contiguous bf16 [rows, len(feature_layers) * hidden]")
+            if features_kept is not None and (features_kept_offsets is None
+                                              or features_kept_offsets.numel() < w.num_requests + 1):
+                raise ValueError("features_kept needs features_kept_offsets [requests + 1]")
+        if trace is None:
+            with torch.cuda.stream(stream) if stream is not None else nullcontext():
+                ops.load().verify_pass(self.handle.value, dw.buf, w.num_requests, w.num_rows,
+                                       w.max_rows_per_request, D, ops.seed_arg(seed), float(temperature),
+                                       bool(commit), accept_out, lengths_out, posterior, lse, child_logprob,
+                                       hidden_out, self.status, [int(l) for l in feature_layers],
+                                       features_out if feature_layers else None,
+                                       features_kept if feature_layers else None,
+                                       features_kept_offsets if feature_layers else None)
+        else:
+            # profiling: the C descriptor also takes the stage-boundary events
+            desc = _WaveDesc(w.num_requests, w.num_rows, w.max_rows_per_request, D, ptr(dw.row_offsets),
+                             ptr(dw.parents), ptr(dw.tokens), ptr(dw.slots), ptr(dw.cache_lengths),
+                             ptr(dw.position_base), ptr(dw.request_ids), seed & ((1 << 64) - 1), float(temperature),
+                             int(bool(commit)), ptr(accept_out), ptr(lengths_out), ptr(posterior), ptr(lse),
+                             ptr(child_logprob), ptr(hidden_out), ptr(self.status), None)
+            layers = (ctypes.c_int32 * max(1, len(feature_layers)))(*[int(l) for l in feature_layers])
+            if feature_layers:
+                desc.num_feature_layers = len(feature_layers)
+                desc.feature_layers = ctypes.cast(layers, ctypes.POINTER(ctypes.c_int32))
+                desc.features_out = ptr(features_out)
+                desc.features_kept = ptr(features_kept)
+                desc.features_kept_offsets = ptr(features_kept_offsets)
             arr = (ctypes.c_void_p * TRACE_EVENTS)(*[e.cuda_event for e in trace])
             desc.trace_events = ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p))
-        check(self.lib.sg_verify_pass(self.handle, ctypes.byref(desc), stream_ptr(stream)), "sg_verify_pass")
+            check(self.lib.sg_verify_pass(self.handle, ctypes.byref(desc), stream_ptr(stream)), "sg_verify_pass")
         self._last_lengths_out = lengths_out
         return accept_out
 

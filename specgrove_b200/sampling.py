@@ -17,10 +17,12 @@ from Philox4x32-10 keyed by (seed, request, node).
 """
 from __future__ import annotations
 
+from contextlib import nullcontext as _nullcontext
+
 import torch
 
-from . import _lib
-from ._lib import SG_RULE_SCAN, SG_RULE_SPARSE_EXIT, check, ptr, stream_ptr
+from . import ops
+from ._lib import SG_RULE_SCAN, SG_RULE_SPARSE_EXIT
 
 
 def _topology(parents, tokens):
@@ -139,12 +141,9 @@ def accept_packed(probs: torch.Tensor, trees: PackedTrees, *, rule: int = SG_RUL
         stride = uniforms.shape[1]
     if out is None:
         out = torch.empty((trees.count, depth + 2), dtype=torch.long, device=probs.device)
-    lib = _lib.load()
-    st = lib.sg_tree_accept_probs(
-        ptr(probs), probs.shape[1], ptr(trees.row_offsets), ptr(trees.parents), ptr(trees.tokens),
-        trees.count, trees.max_nodes, depth, rule, ptr(uniforms), stride, seed & ((1 << 64) - 1),
-        ptr(request_ids), ptr(out), ptr(status), stream_ptr(stream))
-    check(st, "sg_tree_accept_probs")
+    with torch.cuda.stream(stream) if stream is not None else _nullcontext():
+        ops.load().tree_accept_out(probs, trees.row_offsets, trees.parents, trees.tokens, trees.max_nodes, depth,
+                                   rule, uniforms, ops.seed_arg(seed), request_ids, status, out)
     return out
 
 
@@ -260,10 +259,9 @@ def follow_packed(posterior: torch.Tensor, trees: PackedTrees, *, max_depth: int
     posterior = posterior.to(torch.long).contiguous()
     if out is None:
         out = torch.empty((trees.count, depth + 2), dtype=torch.long, device=posterior.device)
-    st = _lib.load().sg_tree_follow(ptr(posterior), ptr(trees.row_offsets), ptr(trees.parents),
-                                    ptr(trees.tokens), trees.count, trees.max_nodes, depth, ptr(out),
-                                    ptr(status), stream_ptr(stream))
-    check(st, "sg_tree_follow")
+    with torch.cuda.stream(stream) if stream is not None else _nullcontext():
+        ops.load().tree_follow_out(posterior, trees.row_offsets, trees.parents, trees.tokens, trees.max_nodes,
+                                   depth, status, out)
     return out
 
 

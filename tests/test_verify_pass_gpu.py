@@ -69,6 +69,27 @@ def make_trees(rng, count, vocab, lo, hi):
     return trees
 
 
+def hf_wave_hidden_states(model, prompts, trees):
+    """HF ``hidden_states`` of the packed wave (the tensors the decoder's
+    feature gather reads, continuous_tree_block_decode.py:2144-2158)."""
+    from transformers import DynamicCache
+    with torch.no_grad():
+        caches = []
+        for p in prompts:
+            c = DynamicCache()
+            model(input_ids=torch.tensor([p], device="cuda"), past_key_values=c, use_cache=True)
+            caches.append(c)
+        packed = DynamicCache()
+        for l in range(model.config.num_hidden_layers):
+            packed.update(torch.cat([c.layers[l].keys for c in caches], dim=-2),
+                          torch.cat([c.layers[l].values for c in caches], dim=-2), l)
+        lengths = [len(p) for p in prompts]
+        ids, pos, mask, _ = packed_block_inputs(trees, lengths, lengths, dtype=torch.bfloat16, device="cuda")
+        out = model.model(input_ids=ids, past_key_values=packed, position_ids=pos, attention_mask=mask,
+                          use_cache=True, output_hidden_states=True)
+    return [h[0] for h in out.hidden_states]
+
+
 def hf_wave_logprobs(model, prompts, trees):
     """The reference's target pass: per-request prefill caches, packed
     DynamicCache, dense tree mask, HF Qwen3Model, lm_head, fp32 log_softmax."""
@@ -215,3 +236,44 @@ def test_gumbel_sampling_law(cuda_lib):
         # TV of an N-sample empirical law around the truth: ~ sqrt(k / N) for k effective categories
         k_eff = 1.0 / (p ** 2).sum().item()
         assert tv < 0.1 + 0.8 * math.sqrt(min(k_eff, 512) / N), (row, tv, k_eff)
+
+
+def test_feature_handoff_matches_hf_hidden_states(cuda_lib):
+    """sg_verify_pass exports hidden_states[l + 1] of the drafter's target
+    layers for every packed row (the last layer's entry final-normed, as in
+    HF), and gathers each request's rows [0] + accepted nodes in request
+    order: the decoder's feature gather (continuous_tree_block_decode.py:
+    2144-2158) without a pass over all hidden states."""
+    model = hf_model(layers=3, hidden=256, nq=4, nkv=2, head_dim=64, inter=512, vocab=1024, logit_scale=1.0)
+    rng = np.random.default_rng(9)
+    prompts = [rng.integers(0, 1024, size=int(rng.integers(20, 90))).tolist() for _ in range(4)]
+    trees = make_trees(rng, 4, 1024, 3, 30)
+    hf_hidden = hf_wave_hidden_states(model, prompts, trees)
+    engine = B200Engine(Weights.from_hf(model), num_slots=4, capacity=256, max_rows=256)
+    engine.prefill(prompts, [0, 1, 2, 3])
+    layers = [0, 2]
+    wave = Wave(trees, [0, 1, 2, 3], [len(p) for p in prompts])
+    Q, H = wave.num_rows, 256
+    feats = torch.zeros((Q, len(layers) * H), dtype=torch.bfloat16, device="cuda")
+    kept = torch.zeros_like(feats)
+    kept_off = torch.full((5,), -1, dtype=torch.long, device="cuda")
+    out = engine.verify_device(wave.to("cuda"), seed=4, commit=False, feature_layers=layers, features_out=feats,
+                               features_kept=kept, features_kept_offsets=kept_off)
+    torch.cuda.synchronize()
+    assert int(engine.status) == 0
+    for f, l in enumerate(layers):
+        ours = feats[:, f * H:(f + 1) * H].float()
+        ref = hf_hidden[l + 1].float()
+        scale = ref.abs().max().item()
+        err = (ours - ref).abs()
+        assert err.max().item() < 3e-2 * scale, (l, err.max().item(), scale)
+        assert err.mean().item() < 3e-3 * scale, (l, err.mean().item(), scale)
+    D = wave.max_depth
+    host = out.cpu().tolist()
+    rows, offs = [], [0]
+    for i in range(4):
+        count = host[i][D]
+        rows += [wave.row_offsets[i] + n for n in [0] + host[i][:count]]
+        offs.append(len(rows))
+    assert kept_off.cpu().tolist() == offs
+    assert torch.equal(kept[:len(rows)], feats[torch.tensor(rows, device="cuda")])
