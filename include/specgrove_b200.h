@@ -356,6 +356,18 @@ SG_API int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stream);
  * NaN.  Misaligned pointers return SG_ERR_INVALID_ARGUMENT before any launch.
  */
 SG_API size_t sg_lm_head_sample_workspace_bytes(int32_t rows, int32_t hidden, int32_t vocab);
+
+/*
+ * sg_lm_head_sample over rows that are already final-normed, in bf16
+ * ([rows, hidden], 16-byte aligned): HF's last_hidden_state, which the
+ * reference's lazy-projection verifiers receive together with the LM head
+ * (fused_tree_sampling.py:2758-2840, continuous_tree_block_decode.py:1933-1964).
+ * Same keys, outputs and workspace size as sg_lm_head_sample.
+ */
+SG_API int sg_lm_head_sample_bf16(const void* xn, const void* lm_head, int32_t rows, int32_t hidden, int32_t vocab,
+                                  const int32_t* row_node, const int64_t* row_request, uint64_t seed,
+                                  float temperature, float* lse, int64_t* posterior, void* workspace,
+                                  size_t workspace_bytes, void* stream);
 SG_API int sg_lm_head_sample(const float* x, const void* final_norm, const void* lm_head, int32_t rows,
                              int32_t hidden, int32_t vocab, float rms_eps, const int32_t* row_node,
                              const int64_t* row_request, uint64_t seed, float temperature, float* lse,

@@ -56,6 +56,9 @@ _SIGNATURES = {
     "sg_lm_head_sample": (ctypes.c_int, [
         c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, ctypes.c_float, c_void_p, c_void_p, c_uint64,
         ctypes.c_float, c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_void_p]),
+    "sg_lm_head_sample_bf16": (ctypes.c_int, [
+        c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_uint64, ctypes.c_float, c_void_p,
+        c_void_p, c_void_p, ctypes.c_size_t, c_void_p]),
     "sg_lm_head_sample_static": (ctypes.c_int, [
         c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, ctypes.c_float, c_void_p, c_void_p, c_uint64,
         ctypes.c_float, c_void_p, c_void_p, c_void_p]),

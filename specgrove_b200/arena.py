@@ -150,6 +150,13 @@ class PersistentKVArena:
         """
         if not (len(caches) == len(query_offsets) == len(keep_query_rows) and caches):
             raise ValueError("Persistent cache append metadata disagree")
+        if getattr(packed, "pool", None) is self:
+            # a wave packed without copying (decoder_seams.pack_cache_sequence):
+            # the pass wrote its tree rows at each slot's tail, keep them in place
+            if any(cache.pool is not self for cache in caches):
+                raise ValueError("Persistent cache belongs to another pool")
+            self.commit_tail([cache.slot for cache in caches], keep_query_rows)
+            return
         src_rows, dst_rows, groups, increments = [], [], [], []
         for cache, q_off, rows in zip(caches, query_offsets, keep_query_rows):
             if cache.pool is not self:

@@ -52,9 +52,11 @@ int lm_head_check(const char* who, const float* x, const void* final_norm, const
 
 int lm_head_run(const float* x, const void* final_norm, const void* lm_head, int32_t rows, int32_t hidden,
                 int32_t vocab, float rms_eps, const int32_t* row_node, const int64_t* row_request, uint64_t seed,
-                float temperature, float* lse, int64_t* posterior, void* scratch, cudaStream_t s) {
+                float temperature, float* lse, int64_t* posterior, void* scratch, cudaStream_t s,
+                const void* normed) {
   int32_t* status = static_cast<int32_t*>(scratch);
-  __nv_bfloat16* xn = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(scratch) + 256);
+  __nv_bfloat16* xn = normed != nullptr ? static_cast<__nv_bfloat16*>(const_cast<void*>(normed))
+                                        : reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(scratch) + 256);
   float4* partials = reinterpret_cast<float4*>(static_cast<uint8_t*>(scratch) + 256 +
                                                align256(static_cast<size_t>(rows) * hidden * 2));
   const int tiles = (vocab + gemm::BN - 1) / gemm::BN;
@@ -70,8 +72,9 @@ int lm_head_run(const float* x, const void* final_norm, const void* lm_head, int
   // written earlier in this call (all rows x hidden normalised values, all
   // rows x tiles partials).
   SG_CUDA_CHECK(cudaMemsetAsync(status, 0, sizeof(int32_t), s));
-  if ((st = layers::launch_rmsnorm(x, static_cast<const __nv_bfloat16*>(final_norm), hidden, rows, rms_eps, xn, s)) !=
-      SG_OK)
+  if (normed == nullptr &&
+      (st = layers::launch_rmsnorm(x, static_cast<const __nv_bfloat16*>(final_norm), hidden, rows, rms_eps, xn, s)) !=
+          SG_OK)
     return st;
   gemm::EpiLmHead::Params pl;
   pl.partials = partials;
@@ -114,4 +117,26 @@ extern "C" int sg_lm_head_sample(const float* x, const void* final_norm, const v
   }
   return lm_head_run(x, final_norm, lm_head, rows, hidden, vocab, rms_eps, row_node, row_request, seed, temperature,
                      lse, posterior, workspace, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sg_lm_head_sample_bf16(const void* xn, const void* lm_head, int32_t rows, int32_t hidden,
+                                      int32_t vocab, const int32_t* row_node, const int64_t* row_request,
+                                      uint64_t seed, float temperature, float* lse, int64_t* posterior,
+                                      void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace sg;
+  if (rows == 0) return SG_OK;
+  // the checks of the fp32 entry, with the normed rows standing in for x and
+  // the final norm (16-byte aligned rows: TMA reads them directly)
+  int st = lm_head_check("sg_lm_head_sample_bf16", static_cast<const float*>(xn), lm_head, lm_head, rows, hidden,
+                         vocab, row_node, row_request, temperature, lse, posterior);
+  if (st != SG_OK) return st;
+  if (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_lm_head_sample_bf16: workspace must be a 256-byte aligned buffer");
+  const size_t need = lm_head_scratch_need(rows, hidden, vocab);
+  if (workspace_bytes < need) {
+    set_error("sg_lm_head_sample_bf16: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+    return SG_ERR_WORKSPACE;
+  }
+  return lm_head_run(nullptr, nullptr, lm_head, rows, hidden, vocab, 0.f, row_node, row_request, seed, temperature,
+                     lse, posterior, workspace, static_cast<cudaStream_t>(stream), xn);
 }

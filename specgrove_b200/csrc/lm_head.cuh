@@ -21,8 +21,11 @@ int lm_head_check(const char* who, const float* x, const void* final_norm, const
 
 // Enqueue norm -> LM head + sampling -> combine with `scratch` (256-byte
 // aligned, lm_head_scratch_need bytes).  temperature 0 selects greedy rows.
+// With `normed` (bf16 [rows, hidden] already-normalised rows) the norm is
+// skipped and x / final_norm are ignored.
 int lm_head_run(const float* x, const void* final_norm, const void* lm_head, int32_t rows, int32_t hidden,
                 int32_t vocab, float rms_eps, const int32_t* row_node, const int64_t* row_request, uint64_t seed,
-                float temperature, float* lse, int64_t* posterior, void* scratch, cudaStream_t stream);
+                float temperature, float* lse, int64_t* posterior, void* scratch, cudaStream_t stream,
+                const void* normed = nullptr);
 
 }  // namespace sg

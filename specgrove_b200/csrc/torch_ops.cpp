@@ -189,6 +189,35 @@ std::tuple<at::Tensor, at::Tensor> lm_head_sample(const at::Tensor& x, const at:
   return {lse, posterior};
 }
 
+std::tuple<at::Tensor, at::Tensor> lm_head_sample_normed(const at::Tensor& xn, const at::Tensor& lm_head,
+                                                         const at::Tensor& row_node, const at::Tensor& row_request,
+                                                         int64_t seed, double temperature) {
+  expect(xn, at::kBFloat16, "xn");
+  expect(lm_head, at::kBFloat16, "lm_head");
+  expect(row_node, at::kInt, "row_node");
+  expect(row_request, at::kLong, "row_request");
+  TORCH_CHECK(xn.dim() == 2 && lm_head.dim() == 2 && lm_head.size(1) == xn.size(1), "xn [rows, hidden] and "
+              "lm_head [vocab, hidden] disagree");
+  const int64_t rows = xn.size(0), hidden = xn.size(1), vocab = lm_head.size(0);
+  TORCH_CHECK(row_node.numel() == rows && row_request.numel() == rows, "one node and request key per row");
+  c10::cuda::CUDAGuard guard(xn.device());
+  at::Tensor lse = at::empty({rows}, xn.options().dtype(at::kFloat));
+  at::Tensor posterior = at::empty({rows}, xn.options().dtype(at::kLong));
+  const size_t bytes = sg_lm_head_sample_workspace_bytes(static_cast<int32_t>(rows), static_cast<int32_t>(hidden),
+                                                         static_cast<int32_t>(vocab));
+  at::Tensor ws = at::empty({static_cast<int64_t>(bytes) + 256}, xn.options().dtype(at::kByte));
+  uint8_t* base = ws.data_ptr<uint8_t>();
+  uint8_t* aligned = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(base) + 255) & ~uintptr_t(255));
+  check_status(sg_lm_head_sample_bf16(xn.data_ptr(), lm_head.data_ptr(), static_cast<int32_t>(rows),
+                                      static_cast<int32_t>(hidden), static_cast<int32_t>(vocab),
+                                      row_node.data_ptr<int32_t>(), row_request.data_ptr<int64_t>(),
+                                      static_cast<uint64_t>(seed), static_cast<float>(temperature),
+                                      lse.data_ptr<float>(), posterior.data_ptr<int64_t>(), aligned, bytes,
+                                      stream_of(xn)),
+               "specgrove_b200::lm_head_sample_normed");
+  return {lse, posterior};
+}
+
 // --------------------------------------------------------- the verify pass
 
 // `wave` is the int64 wave buffer of specgrove_b200.engine.Wave: row offsets
@@ -269,6 +298,12 @@ std::tuple<at::Tensor, at::Tensor> lm_head_sample_meta(const at::Tensor& x, cons
   return {at::empty({x.size(0)}, x.options()), at::empty({x.size(0)}, x.options().dtype(at::kLong))};
 }
 
+std::tuple<at::Tensor, at::Tensor> lm_head_sample_normed_meta(const at::Tensor& xn, const at::Tensor&,
+                                                              const at::Tensor&, const at::Tensor&, int64_t, double) {
+  return {at::empty({xn.size(0)}, xn.options().dtype(at::kFloat)),
+          at::empty({xn.size(0)}, xn.options().dtype(at::kLong))};
+}
+
 void tree_accept_out_meta(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t,
                           int64_t, int64_t, const std::optional<at::Tensor>&, int64_t,
                           const std::optional<at::Tensor>&, const std::optional<at::Tensor>&, at::Tensor&) {}
@@ -307,6 +342,8 @@ TORCH_LIBRARY(specgrove_b200, m) {
         "Tensor(b!) lengths_out, Tensor accept_out, int max_depth, Tensor(c!)? status) -> ()");
   m.def("lm_head_sample(Tensor x, Tensor final_norm, Tensor lm_head, Tensor row_node, Tensor row_request, "
         "int seed, float temperature, float rms_eps) -> (Tensor, Tensor)");
+  m.def("lm_head_sample_normed(Tensor xn, Tensor lm_head, Tensor row_node, Tensor row_request, int seed, "
+        "float temperature) -> (Tensor, Tensor)");
   m.def("verify_pass(int engine, Tensor wave, int num_requests, int num_rows, int max_rows_per_request, "
         "int max_depth, int seed, float temperature, bool commit, Tensor(a!) accept_out, "
         "Tensor(b!)? lengths_out, Tensor(c!)? posterior, Tensor(d!)? lse, Tensor(e!)? child_logprob, "
@@ -322,6 +359,7 @@ TORCH_LIBRARY_IMPL(specgrove_b200, CUDA, m) {
   m.impl("kv_commit", &kv_commit);
   m.impl("kv_commit_accepted", &kv_commit_accepted);
   m.impl("lm_head_sample", &lm_head_sample);
+  m.impl("lm_head_sample_normed", &lm_head_sample_normed);
   m.impl("verify_pass", &verify_pass);
 }
 
@@ -333,5 +371,6 @@ TORCH_LIBRARY_IMPL(specgrove_b200, Meta, m) {
   m.impl("kv_commit", &kv_commit_meta);
   m.impl("kv_commit_accepted", &kv_commit_accepted_meta);
   m.impl("lm_head_sample", &lm_head_sample_meta);
+  m.impl("lm_head_sample_normed", &lm_head_sample_normed_meta);
   m.impl("verify_pass", &verify_pass_meta);
 }
