@@ -509,12 +509,82 @@ def run_verify(args, world, rank):
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline_verify(wl)
     line["cpu_baseline"] = cpu
-    if world == 1 and not args.no_nested and args.layers is None and args.workload == "verify":
+    if not args.no_nested and args.layers is None and args.workload == "verify":
+        weights = wl.weights
         wl.close()
         del wl
         torch.cuda.empty_cache()
-        line["nested"] = nested_configs(args, world, rank)
+        nested = nested_configs(args, world, rank) if world == 1 else {}
+        nested["config5"] = measure_serving(args, world, rank, weights)
+        line["nested"] = nested
     return line
+
+
+# Synthetic monotone wave-cost curve (rows -> ms) for the allocator, shaped
+# like the measured configuration-4 pass (a fixed part, then ~17 us per row).
+SERVE_COST_CURVE = [(16, 2.0), (256, 5.5), (512, 9.0), (1024, 17.5), (2048, 34.7)]
+
+
+def measure_serving(args, world, rank, weights=None):
+    """Configuration 5: open-loop serving of the Qwen3-8B shape, requests
+    partitioned over the ranks, one verify pass per wave with the per-wave
+    NCCL allgather of allocator scores.  The makespan is the CUDA-event span
+    of the whole serving loop on each rank (max over ranks)."""
+    from specgrove_b200 import _lib
+    from specgrove_b200.allocator import ScoreExchange
+    from specgrove_b200.engine import QWEN3_8B, B200Engine, Wave, Weights
+    from specgrove_b200.serving import OpenLoopServer, make_requests
+    shape = QWEN3_8B
+    weights = weights or Weights.random(shape, seed=1234)
+    tiers = [16, 32, 64, 128]
+    n_req, rate, max_new = args.serve_requests, 8.0 * world, 256
+    requests = make_requests(n_req, rate, (256, 8192), tiers, shape.vocab, seed=5)
+    slots = 64
+    capacity = 8192 + max_new + max(tiers) + 16
+    engine = B200Engine(weights, num_slots=slots, capacity=capacity, max_rows=2048, max_requests=slots)
+    gen = torch.Generator(device="cuda").manual_seed(77 + rank)
+    engine.arena.storage.normal_(0.0, 1.0, generator=gen)            # synthetic prompt KV
+
+    def step(trees, slot_ids, lengths, rids, seed):
+        wave = Wave(trees, slot_ids, lengths, request_ids=rids)
+        out = engine.verify_device(wave.to("cuda"), seed=seed, commit=True)
+        return out[:, wave.max_depth].cpu().tolist()
+
+    exchange = ScoreExchange(slots, len(tiers), "cuda")
+    server = OpenLoopServer(requests, step, rank=rank, world=world, exchange=exchange, num_slots=slots,
+                            capacity=capacity, tier_rows=tiers, row_budget=2048, max_new_tokens=max_new,
+                            row_cost_curve=SERVE_COST_CURVE)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = _lib.launch_count()
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record()
+        stats = server.run(seed=1_000_000 * rank)
+        stop.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    if int(engine.status) != 0:
+        raise RuntimeError(f"device status {int(engine.status)}")
+    span_ms = start.elapsed_time(stop)
+    makespan = max_over_ranks(span_ms, world)
+    tokens = sum_over_ranks(stats.tokens, world)
+    waves = max_over_ranks(stats.waves, world)
+    lat = sorted(stats.finish_times)
+    engine.close()
+    del engine
+    torch.cuda.empty_cache()
+    return {"workload": f"config5: Qwen3-8B shape, {n_req} requests, Poisson {8.0:g} req/s per GPU, prompts "
+                        f"log-uniform [256, 8192] (synthetic KV), {max_new} tokens each, tiers {{16,32,64,128}}, "
+                        "service weights U{1,2,4}, 2048-row budget per GPU, least-loaded admission",
+            "metric": METRIC, "value": tokens / (makespan / 1000.0), "unit": UNIT, "n_gpus": world,
+            "makespan_ms": makespan, "tokens": tokens, "waves_max_rank": waves,
+            "rows_per_wave_rank0": stats.rows / max(1, stats.waves), "host_ms_rank0": stats.host_ms,
+            "requests_rank0": stats.requests, "exchanges": stats.exchanges,
+            "latency_s_rank0": {"p50": lat[len(lat) // 2] if lat else None, "max": lat[-1] if lat else None},
+            "collective": "per-wave NCCL all_gather_into_tensor of allocator scores + clock/load/done header"
+                          if world > 1 else "none (one rank)",
+            "gpu_launches": _lib.launch_count() - launches0, "clocks": clocks.summary()}
 
 
 def nested_configs(args, world, rank):
@@ -834,7 +904,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="verify", choices=["verify", "verify4b", "accept"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--no-nested", action="store_true", help="skip the nested configuration-2/3 blocks")
+    ap.add_argument("--no-nested", action="store_true", help="skip the nested configuration-2/3/5 blocks")
+    ap.add_argument("--serve-requests", type=int, default=256, help="configuration-5 request count")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: build the model with this many layers (not a benchmark number)")
     args = ap.parse_args()

@@ -97,8 +97,9 @@ class RequestScores:
 class ScoreExchange:
     """Fixed-size per-wave allgather of allocator scores.
 
-    Layout per rank: row 0 = [request count, 0...]; rows 1..max_requests =
-    [valid, progress, age, service weight, utility_0 .. utility_{T-1}] (fp64).
+    Layout per rank: row 0 = [request count, header values (e.g. the rank's
+    clock, load and done flag) ...]; rows 1..max_requests = [valid, progress,
+    age, service weight, utility_0 .. utility_{T-1}] (fp64).
     """
 
     def __init__(self, max_requests: int, num_tiers: int, device, group=None):
@@ -112,12 +113,16 @@ class ScoreExchange:
         self.local = torch.zeros((max_requests + 1, self.width), dtype=torch.float64, device=device)
         self.gathered = torch.zeros((self.world, max_requests + 1, self.width), dtype=torch.float64, device=device)
 
-    def pack(self, scores: RequestScores) -> None:
+    def pack(self, scores: RequestScores, header: Sequence[float] = ()) -> None:
         n = len(scores.progress)
         if n > self.max_requests:
             raise ValueError("more requests than the exchange was sized for")
+        if len(header) > self.width - 1:
+            raise ValueError("header wider than a score row")
         host = torch.zeros((self.max_requests + 1, self.width), dtype=torch.float64)
         host[0, 0] = n
+        if len(header):
+            host[0, 1:1 + len(header)] = torch.tensor([float(v) for v in header], dtype=torch.float64)
         for i in range(n):
             host[1 + i, :4] = torch.tensor([1.0, scores.progress[i], scores.ages[i], scores.service_weights[i]],
                                            dtype=torch.float64)
@@ -137,6 +142,8 @@ class ScoreExchange:
         """(leading progress, maximum age) over every rank's valid requests."""
         g = gathered.cpu()
         valid = g[:, 1:, 0] > 0
+        if not bool(valid.any()):
+            return 0, 0
         progress = g[:, 1:, 1][valid]
         ages = g[:, 1:, 2][valid]
         return int(progress.max().item()), int(ages.max().item())
