@@ -95,6 +95,30 @@ SG_API int sg_tree_accept_probs(const float* probs, int64_t vocab,
                          uint64_t seed, const int64_t* request_ids,
                          int64_t* out, int32_t* status, void* stream);
 
+/* Element types of logit rows (sg_tree_accept_logits `dtype`). */
+enum sg_dtype { SG_DTYPE_F32 = 0, SG_DTYPE_BF16 = 1 };
+
+/*
+ * Tree-sampling acceptance straight from logit rows: only the visited rows
+ * are normalised (reference direct-logits verifiers,
+ *   fused_tree_sampling.py:2417-2465  tree_verify_ancestral_logits_fused_scan
+ *   fused_tree_sampling.py:2468-2533  tree_verify_ancestral_logits_fused_scan_batched
+ * and their kernels :942-1115, :1117-1236).  At a visited node the weights
+ * are w_j = exp(double(logit_j) / T - max), the token is the first whose
+ * exact inclusive prefix of w exceeds u[depth] * sum(w) (fallback V - 1).
+ * logits       [total_rows, vocab] fp32 or bf16 (dtype), row-major
+ * temperature  > 0
+ * uniforms     [num_trees, uniform_stride] fp64, u[depth] read, or NULL for
+ *              Philox4x32-10(seed, (node, request, purpose 0)) like
+ *              sg_tree_accept_probs' scan rule
+ * Other arguments and the output layout as sg_tree_accept_probs.
+ */
+SG_API int sg_tree_accept_logits(const void* logits, int32_t dtype, int64_t vocab, const int64_t* row_offsets,
+                                 const int64_t* parents, const int64_t* tokens, int32_t num_trees,
+                                 int32_t max_nodes, int32_t max_depth, double temperature, const double* uniforms,
+                                 int32_t uniform_stride, uint64_t seed, const int64_t* request_ids, int64_t* out,
+                                 int32_t* status, void* stream);
+
 /*
  * Walk the trees with one pre-drawn posterior token per node
  * (reference fused_tree_sampling.py:120-151 fused_tree_follow_kernel, used by

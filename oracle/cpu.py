@@ -32,6 +32,10 @@ def lib() -> ctypes.CDLL:
         L.sgo_tree_accept_probs.argtypes = [
             c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p,
             c_int32, c_uint64, c_void_p, c_int32, c_void_p]
+        L.sgo_tree_accept_logits.restype = ctypes.c_int
+        L.sgo_tree_accept_logits.argtypes = [
+            c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_double, c_void_p, c_int32,
+            c_uint64, c_void_p, c_int32, c_void_p]
         L.sgo_tree_follow.restype = ctypes.c_int
         L.sgo_tree_follow.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
                                       c_void_p]
@@ -73,6 +77,29 @@ def accept_probs(probs: np.ndarray, row_offsets, parents, tokens, max_depth: int
     st = lib().sgo_tree_accept_probs(_p(probs), probs.shape[1], _p(row_offsets), _p(parents),
                                      _p(tokens), trees, max_depth, rule, _p(uniforms), stride,
                                      seed, _p(request_ids), arith, _p(out))
+    return out, st
+
+
+def accept_logits(logits: np.ndarray, row_offsets, parents, tokens, max_depth: int, temperature: float = 1.0,
+                  uniforms: np.ndarray | None = None, seed: int = 0, request_ids=None,
+                  arith: int = ARITH_EXACT) -> tuple[np.ndarray, int]:
+    """Direct-logits walk (fp32 logits; bf16 widened exactly by the caller);
+    returns (out [trees, max_depth+2] int64, status)."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    row_offsets = np.ascontiguousarray(row_offsets, dtype=np.int64)
+    parents = np.ascontiguousarray(parents, dtype=np.int64)
+    tokens = np.ascontiguousarray(tokens, dtype=np.int64)
+    trees = len(row_offsets) - 1
+    stride = 0
+    if uniforms is not None:
+        uniforms = np.ascontiguousarray(uniforms, dtype=np.float64).reshape(trees, -1)
+        stride = uniforms.shape[1]
+    if request_ids is not None:
+        request_ids = np.ascontiguousarray(request_ids, dtype=np.int64)
+    out = np.full((trees, max_depth + 2), -1, dtype=np.int64)
+    st = lib().sgo_tree_accept_logits(_p(logits), logits.shape[1], _p(row_offsets), _p(parents), _p(tokens), trees,
+                                      max_depth, float(temperature), _p(uniforms), stride, seed, _p(request_ids),
+                                      arith, _p(out))
     return out, st
 
 

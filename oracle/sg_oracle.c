@@ -297,6 +297,91 @@ int sgo_tree_accept_probs(const float* probs, int64_t vocab, const int64_t* row_
   return worst;
 }
 
+/*
+ * Direct-logits scan rule (fused_tree_sampling.py:942-1115, the kernel of
+ * tree_verify_ancestral_logits_fused_scan(_batched), :2417-2533): at the
+ * visited node x_j = double(logit_j) / T, w_j = exp(x_j - max x); the token
+ * is the first index whose inclusive prefix of w exceeds u[depth] * sum(w)
+ * (fallback V - 1).  ARITH_EXACT sums floor(w * 2^64) exactly (the CUDA
+ * kernel's arithmetic), ARITH_FP64 is the reference kernel's fp64 running sum.
+ * Logits are fp32 here (bf16 rows are widened exactly by the caller).
+ */
+static u128 weight_mass(double w) {
+  return w >= 1.0 ? ((u128)1) << 64 : (u128)(uint64_t)(w * 18446744073709551616.0);
+}
+
+static int64_t draw_logit_row(const float* row, int64_t V, double inv, double u, int arith, int* bad) {
+  float m = -INFINITY;
+  for (int64_t t = 0; t < V; ++t) {
+    if (row[t] != row[t]) *bad = 1;
+    if (row[t] > m) m = row[t];
+  }
+  const double xmax = (double)m * inv;
+  if (arith == ARITH_EXACT) {
+    u128 total = 0;
+    for (int64_t t = 0; t < V; ++t) total += weight_mass(exp((double)row[t] * inv - xmax));
+    if (total == 0) return -1;
+    u128 thr = mass_scale(u, total), run = 0;
+    for (int64_t t = 0; t < V; ++t) {
+      run += weight_mass(exp((double)row[t] * inv - xmax));
+      if (run > thr) return t;
+    }
+    return -1;
+  }
+  double total = 0.0;
+  for (int64_t t = 0; t < V; ++t) total += exp((double)row[t] * inv - xmax);
+  double thr = u * total, run = 0.0;
+  for (int64_t t = 0; t < V; ++t) {
+    run += exp((double)row[t] * inv - xmax);
+    if (thr < run) return t;
+  }
+  return -1;
+}
+
+int sgo_tree_accept_logits(const float* logits, int64_t vocab, const int64_t* row_offsets, const int64_t* parents,
+                           const int64_t* tokens, int32_t num_trees, int32_t max_depth, double temperature,
+                           const double* uniforms, int32_t uniform_stride, uint64_t seed,
+                           const int64_t* request_ids, int32_t arith, int64_t* out) {
+  int worst = 0;
+  const double inv = 1.0 / temperature;
+#pragma omp parallel for schedule(dynamic, 1) reduction(max : worst)
+  for (int t = 0; t < num_trees; ++t) {
+    const int64_t r0 = row_offsets[t];
+    const int n = (int)(row_offsets[t + 1] - r0);
+    const int64_t* par = parents + r0;
+    const int64_t* tok = tokens + r0;
+    int64_t* o = out + (int64_t)t * (max_depth + 2);
+    for (int i = 0; i < max_depth + 2; ++i) o[i] = -1;
+    int st = 0, bad = 0;
+    if (n < 1 || par[0] != -1) st = 3;
+    for (int j = 1; j < n && !st; ++j)
+      if (par[j] < 0 || par[j] >= j || tok[j] < 0 || tok[j] >= vocab) st = 3;
+    const uint64_t req = request_ids ? (uint64_t)request_ids[t] : (uint64_t)t;
+    int cur = 0, accepted = 0;
+    for (int depth = 0; depth <= max_depth && !st; ++depth) {
+      double u, unused;
+      if (uniforms)
+        u = uniforms[(int64_t)t * uniform_stride + depth];
+      else
+        sgo_node_uniforms(seed, req, (uint32_t)cur, &u, &unused);
+      int64_t token = draw_logit_row(logits + (r0 + cur) * vocab, vocab, inv, u, arith, &bad);
+      if (token < 0) token = vocab - 1;
+      const int child = find_child(par, tok, n, cur, token);
+      if (child >= 0 && depth < max_depth) {
+        o[accepted++] = child;
+        cur = child;
+        continue;
+      }
+      o[max_depth] = accepted;
+      o[max_depth + 1] = token;
+      break;
+    }
+    if (bad && st == 0) st = 4;
+    if (st > worst) worst = st;
+  }
+  return worst;
+}
+
 /* Walk pre-drawn posterior tokens (fused_tree_sampling.py:120-151). */
 int sgo_tree_follow(const int64_t* posterior, const int64_t* row_offsets, const int64_t* parents,
                     const int64_t* tokens, int32_t num_trees, int32_t max_depth, int64_t* out) {

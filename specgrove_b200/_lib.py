@@ -32,6 +32,9 @@ _SIGNATURES = {
     "sg_tree_accept_probs": (ctypes.c_int, [
         c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
         c_void_p, c_int32, c_uint64, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "sg_tree_accept_logits": (ctypes.c_int, [
+        c_void_p, c_int32, c_int64, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_double,
+        c_void_p, c_int32, c_uint64, c_void_p, c_void_p, c_void_p, c_void_p]),
     "sg_tree_follow": (ctypes.c_int, [
         c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p,
         c_void_p]),

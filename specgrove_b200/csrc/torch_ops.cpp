@@ -83,6 +83,41 @@ at::Tensor tree_accept(const at::Tensor& probs, const at::Tensor& row_offsets, c
   return out;
 }
 
+void tree_accept_logits_out(const at::Tensor& logits, const at::Tensor& row_offsets, const at::Tensor& parents,
+                            const at::Tensor& tokens, int64_t max_nodes, int64_t max_depth, double temperature,
+                            const std::optional<at::Tensor>& uniforms, int64_t seed,
+                            const std::optional<at::Tensor>& request_ids, const std::optional<at::Tensor>& status,
+                            at::Tensor& out) {
+  TORCH_CHECK(logits.is_cuda() && logits.is_contiguous() && logits.dim() == 2 &&
+                  (logits.scalar_type() == at::kFloat || logits.scalar_type() == at::kBFloat16),
+              "logits must be a contiguous CUDA float32 or bfloat16 [rows, vocab] tensor");
+  expect(row_offsets, at::kLong, "row_offsets");
+  expect(parents, at::kLong, "parents");
+  expect(tokens, at::kLong, "tokens");
+  expect(out, at::kLong, "out");
+  const int64_t trees = row_offsets.numel() - 1;
+  TORCH_CHECK(trees >= 1 && max_depth >= 0 && max_nodes >= 1, "tree_accept_logits: bad tree counts");
+  TORCH_CHECK(out.numel() == trees * (max_depth + 2), "out must be [trees, max_depth + 2]");
+  int32_t stride = 0;
+  if (uniforms.has_value()) {
+    expect(*uniforms, at::kDouble, "uniforms");
+    TORCH_CHECK(uniforms->numel() % trees == 0, "uniforms must be [trees, stride]");
+    stride = static_cast<int32_t>(uniforms->numel() / trees);
+  }
+  if (request_ids.has_value()) expect(*request_ids, at::kLong, "request_ids");
+  if (status.has_value()) expect(*status, at::kInt, "status");
+  c10::cuda::CUDAGuard guard(logits.device());
+  check_status(sg_tree_accept_logits(logits.data_ptr(), logits.scalar_type() == at::kBFloat16 ? SG_DTYPE_BF16
+                                                                                               : SG_DTYPE_F32,
+                                     logits.size(1), row_offsets.data_ptr<int64_t>(), parents.data_ptr<int64_t>(),
+                                     tokens.data_ptr<int64_t>(), static_cast<int32_t>(trees),
+                                     static_cast<int32_t>(max_nodes), static_cast<int32_t>(max_depth), temperature,
+                                     data_or_null<double>(uniforms), stride, static_cast<uint64_t>(seed),
+                                     data_or_null<int64_t>(request_ids), out.data_ptr<int64_t>(),
+                                     data_or_null<int32_t>(status), stream_of(logits)),
+               "specgrove_b200::tree_accept_logits");
+}
+
 void tree_follow_out(const at::Tensor& posterior, const at::Tensor& row_offsets, const at::Tensor& parents,
                      const at::Tensor& tokens, int64_t max_nodes, int64_t max_depth,
                      const std::optional<at::Tensor>& status, at::Tensor& out) {
@@ -311,6 +346,10 @@ void tree_accept_out_meta(const at::Tensor&, const at::Tensor&, const at::Tensor
 void tree_follow_out_meta(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t,
                           int64_t, const std::optional<at::Tensor>&, at::Tensor&) {}
 
+void tree_accept_logits_out_meta(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t,
+                                 int64_t, double, const std::optional<at::Tensor>&, int64_t,
+                                 const std::optional<at::Tensor>&, const std::optional<at::Tensor>&, at::Tensor&) {}
+
 void kv_commit_meta(at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t,
                     const std::optional<at::Tensor>&) {}
 
@@ -331,6 +370,9 @@ TORCH_LIBRARY(specgrove_b200, m) {
         "int max_depth, int rule, Tensor? uniforms, int seed, Tensor? request_ids, Tensor(a!)? status) -> Tensor");
   m.def("tree_accept_out(Tensor probs, Tensor row_offsets, Tensor parents, Tensor tokens, int max_nodes, "
         "int max_depth, int rule, Tensor? uniforms, int seed, Tensor? request_ids, Tensor(a!)? status, "
+        "Tensor(b!) out) -> ()");
+  m.def("tree_accept_logits_out(Tensor logits, Tensor row_offsets, Tensor parents, Tensor tokens, int max_nodes, "
+        "int max_depth, float temperature, Tensor? uniforms, int seed, Tensor? request_ids, Tensor(a!)? status, "
         "Tensor(b!) out) -> ()");
   m.def("tree_follow(Tensor posterior, Tensor row_offsets, Tensor parents, Tensor tokens, int max_nodes, "
         "int max_depth, Tensor(a!)? status) -> Tensor");
@@ -354,6 +396,7 @@ TORCH_LIBRARY(specgrove_b200, m) {
 TORCH_LIBRARY_IMPL(specgrove_b200, CUDA, m) {
   m.impl("tree_accept", &tree_accept);
   m.impl("tree_accept_out", &tree_accept_out);
+  m.impl("tree_accept_logits_out", &tree_accept_logits_out);
   m.impl("tree_follow", &tree_follow);
   m.impl("tree_follow_out", &tree_follow_out);
   m.impl("kv_commit", &kv_commit);
@@ -366,6 +409,7 @@ TORCH_LIBRARY_IMPL(specgrove_b200, CUDA, m) {
 TORCH_LIBRARY_IMPL(specgrove_b200, Meta, m) {
   m.impl("tree_accept", &tree_accept_meta);
   m.impl("tree_accept_out", &tree_accept_out_meta);
+  m.impl("tree_accept_logits_out", &tree_accept_logits_out_meta);
   m.impl("tree_follow", &tree_follow_meta);
   m.impl("tree_follow_out", &tree_follow_out_meta);
   m.impl("kv_commit", &kv_commit_meta);

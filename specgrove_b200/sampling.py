@@ -265,6 +265,103 @@ def follow_packed(posterior: torch.Tensor, trees: PackedTrees, *, max_depth: int
     return out
 
 
+def accept_logits_packed(logits: torch.Tensor, trees: PackedTrees, *, temperature: float = 1.0,
+                         uniforms: torch.Tensor | None = None, seed: int = 0,
+                         request_ids: torch.Tensor | None = None, max_depth: int | None = None,
+                         out: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                         stream=None) -> torch.Tensor:
+    """One launch of the direct-logits walk (``sg_tree_accept_logits``) over
+    packed fp32 or bf16 logit rows; returns the device [trees, max_depth + 2]
+    output (reference layout)."""
+    if not logits.is_cuda or logits.ndim != 2 or logits.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("accept_logits_packed expects a CUDA float32 or bfloat16 [rows, vocab] tensor")
+    logits = logits.contiguous()
+    if logits.shape[0] < trees.total_rows:
+        raise ValueError("fewer logit rows than packed tree nodes")
+    depth = trees.max_depth if max_depth is None else int(max_depth)
+    if uniforms is not None:
+        uniforms = uniforms.reshape(trees.count, -1).contiguous()
+    if out is None:
+        out = torch.empty((trees.count, depth + 2), dtype=torch.long, device=logits.device)
+    with torch.cuda.stream(stream) if stream is not None else _nullcontext():
+        ops.load().tree_accept_logits_out(logits, trees.row_offsets, trees.parents, trees.tokens, trees.max_nodes,
+                                          depth, float(temperature), uniforms, ops.seed_arg(seed), request_ids,
+                                          status, out)
+    return out
+
+
+def _check_logit_temperature(temperature, probability_dtype):
+    if (not isinstance(temperature, (float, int)) or not temperature > 0
+            or temperature == float("inf")):
+        raise ValueError("Direct-logits temperature must be finite and positive")
+    if probability_dtype != torch.float64:
+        raise ValueError("Direct-logits verifier requires FP64 probability arithmetic")
+
+
+def _logit_stats(count, node_count):
+    return {"visited_probability_rows": count + 1, "total_tree_rows": node_count, "lm_head_rows": node_count}
+
+
+def tree_verify_ancestral_logits_fused_scan(parents, tokens, all_logits, temperature: float,
+                                            probability_dtype=torch.float64, generator=None,
+                                            validate: bool = True):
+    """Reference fused_tree_sampling.py:2417-2465 on the B200 kernel:
+    (nodes, tokens, bonus, stats); uniforms drawn from ``generator`` as the
+    reference draws them (``torch.rand(max_depth + 1)`` float64)."""
+    parents, tokens, max_depth = _topology(parents, tokens)
+    node_count = len(parents)
+    if (not all_logits.is_cuda or all_logits.ndim != 2 or all_logits.shape[0] != node_count
+            or all_logits.shape[1] < 1 or not all_logits.is_floating_point()):
+        raise ValueError("Direct-logits Target tensor mismatch")
+    _check_logit_temperature(temperature, probability_dtype)
+    if any(t < 0 or t >= all_logits.shape[1] for t in tokens):
+        raise ValueError("Tree token is outside the Target vocabulary")
+    if validate and not bool(torch.isfinite(all_logits).all()):
+        raise FloatingPointError("Target logits must be finite")
+    uniforms = torch.rand(max_depth + 1, dtype=torch.float64, device=all_logits.device, generator=generator)
+    rows = all_logits if all_logits.dtype in (torch.float32, torch.bfloat16) else all_logits.float()
+    trees = PackedTrees([parents], [tokens], all_logits.device)
+    out = accept_logits_packed(rows, trees, temperature=temperature, uniforms=uniforms, max_depth=max_depth)
+    nodes, toks, bonus = decode_output(out[0].tolist(), max_depth, all_logits.shape[1], tokens,
+                                       "Direct-logits sampler")
+    return nodes, toks, bonus, _logit_stats(len(nodes), node_count)
+
+
+def tree_verify_ancestral_logits_fused_scan_batched(parents_batch, tokens_batch, all_logits, temperature: float,
+                                                    probability_dtype=torch.float64, generators=None,
+                                                    validate: bool = True):
+    """Reference fused_tree_sampling.py:2468-2533: equally shaped trees
+    ([B, n, V] logits), one launch, one uniform draw per request generator.
+    Ragged batches (a list of [n_i, V]) run as one launch too."""
+    count = len(parents_batch)
+    if (count < 1 or len(tokens_batch) != count or generators is None or len(generators) != count):
+        raise ValueError("Batched direct-logits inputs are inconsistent")
+    _check_logit_temperature(temperature, probability_dtype)
+    rows = list(all_logits.unbind(0)) if isinstance(all_logits, torch.Tensor) else list(all_logits)
+    topo = [_topology(p, t) for p, t in zip(parents_batch, tokens_batch)]
+    if len(rows) != count or any(r.ndim != 2 or r.shape[0] != len(p) or not r.is_cuda
+                                 for r, (p, _, _) in zip(rows, topo)):
+        raise ValueError("Batched direct-logits tensor shape mismatch")
+    vocab = rows[0].shape[1]
+    if any(t < 0 or t >= vocab for _, toks, _ in topo for t in toks):
+        raise ValueError("Tree token is outside the Target vocabulary")
+    if validate and not all(bool(torch.isfinite(r).all()) for r in rows):
+        raise FloatingPointError("Target logits must be finite")
+    depth = max(d for _, _, d in topo)
+    device = rows[0].device
+    uniforms = torch.zeros((count, depth + 1), dtype=torch.float64, device=device)
+    for i, ((_, _, d), gen) in enumerate(zip(topo, generators)):
+        uniforms[i, :d + 1] = torch.rand(d + 1, dtype=torch.float64, device=device, generator=gen)
+    flat = torch.cat([r if r.dtype in (torch.float32, torch.bfloat16) else r.float() for r in rows], 0)
+    trees = PackedTrees([p for p, _, _ in topo], [t for _, t, _ in topo], device)
+    host = accept_logits_packed(flat, trees, temperature=temperature, uniforms=uniforms, max_depth=depth).tolist()
+    results = []
+    for (par, toks, _), row in zip(topo, host):
+        nodes, out_toks, bonus = decode_output(row, depth, vocab, toks, "Batched direct-logits sampler")
+        results.append((nodes, out_toks, bonus, _logit_stats(len(nodes), len(par))))
+    return results
+
+
 def philox_node_uniforms(seed: int, request: int, node: int) -> tuple[float, float]:
     """Host restatement of the kernel's per-node uniforms (for reproducibility
     checks): Philox4x32-10, key = seed, counter = (node, request lo, request hi, 0)."""
@@ -282,7 +379,8 @@ def philox_node_uniforms(seed: int, request: int, node: int) -> tuple[float, flo
 
 
 __all__ = [
-    "PackedTrees", "accept_packed", "follow_packed", "decode_output",
+    "PackedTrees", "accept_packed", "accept_logits_packed", "follow_packed", "decode_output",
+    "tree_verify_ancestral_logits_fused_scan", "tree_verify_ancestral_logits_fused_scan_batched",
     "tree_verify_ancestral_fused_scan", "tree_verify_ancestral_sparse_exit_fused_scan",
     "tree_verify_ancestral_sparse_exit_fused_scan_batched", "tree_verify_ancestral_same_draw_fused",
     "philox_node_uniforms", "SG_RULE_SCAN", "SG_RULE_SPARSE_EXIT",

@@ -155,6 +155,39 @@ def save_accept(name: str, cases):
     np.savez_compressed(OUT / name, **arrays)
 
 
+def build_accept_logits(ref, gen):
+    """Direct-logits walk (the rule of fused_tree_sampling.py:942-1115): the
+    reference's own _sample_row_inverse_cdf on the fp64 weights
+    exp(double(logit) / T - max), ancestrally with child_for_edge.  Logits
+    are bf16-representable so the same rows serve fp32 and bf16 inputs."""
+    fts, tbs = ref.fused, ref.tbs
+    cases = []
+    for n, vocab, temperature in [(1, 64, 1.0), (5, 300, 1.0), (9, 1000, 0.7), (17, 256, 1.6), (8, 4096, 1.0),
+                                  (33, 512, 0.35), (12, 2049, 1.0)]:
+        parents, tokens, _ = random_tree(gen, n, vocab)
+        logits = torch.randn((n, vocab), generator=gen, dtype=torch.float32) * 2.0
+        for j in range(1, n):
+            logits[parents[j], tokens[j]] += float(torch.empty(1).uniform_(2.0, 6.0, generator=gen))
+        logits = logits.to(torch.bfloat16).to(torch.float32)
+        _, _, max_depth = fts._topology(parents, tokens[1:])
+        uniforms = torch.rand(max_depth + 1, dtype=torch.float64, generator=gen)
+        node, nodes, bonus = 0, [], None
+        for depth in range(max_depth + 1):
+            x = logits[node].to(torch.float64) * (1.0 / temperature)
+            weights = torch.exp(x - x.max())
+            token = fts._sample_row_inverse_cdf(weights, float(uniforms[depth]))
+            child = tbs.child_for_edge(parents, tokens[1:], node, token)
+            if child is not None and depth < max_depth:
+                nodes.append(child)
+                node = child
+                continue
+            bonus = token
+            break
+        cases.append(dict(parents=parents, tokens=tokens, probs=logits.numpy(), uniforms=uniforms.numpy(),
+                          max_depth=max_depth, nodes=nodes, bonus=bonus, vocab=vocab, temperature=temperature))
+    return cases
+
+
 def build_follow(ref, gen):
     sampling = ref.sampling
     cases = []
@@ -308,6 +341,14 @@ def main():
     build_kv_commit(ref, gen)
     build_packed_inputs(ref, gen)
     build_allocator(ref, gen)
+    # later fixtures use their own generator, so the ones above stay byte-identical
+    logits_cases = build_accept_logits(ref, torch.Generator().manual_seed(20261202))
+    save_accept("accept_logits.npz", logits_cases)
+    with np.load(OUT / "accept_logits.npz") as z:
+        arrays = dict(z)
+    for i, c in enumerate(logits_cases):
+        arrays[f"temperature_{i}"] = np.float64(c["temperature"])
+    np.savez_compressed(OUT / "accept_logits.npz", **arrays)
     for p in sorted(OUT.glob("*.*")):
         print(p.name, p.stat().st_size)
 

@@ -24,6 +24,24 @@ def _cases(path):
 
 
 @pytest.mark.parametrize("arith", [oracle.ARITH_EXACT, oracle.ARITH_FP64])
+def test_oracle_logits_rule_matches_reference(golden_dir, arith):
+    """Direct-logits walk (fused_tree_sampling.py:942-1115) against the
+    reference's _sample_row_inverse_cdf over exp(double(logit) / T - max)."""
+    z = np.load(golden_dir / "accept_logits.npz")
+    offsets = z["row_offsets"]
+    for i in range(int(z["count"])):
+        r0, r1 = int(offsets[i]), int(offsets[i + 1])
+        D = int(z[f"max_depth_{i}"])
+        out, st = oracle.accept_logits(z[f"probs_{i}"], [0, r1 - r0], z["parents"][r0:r1], z["tokens"][r0:r1], D,
+                                       temperature=float(z[f"temperature_{i}"]), uniforms=z[f"uniforms_{i}"][None],
+                                       arith=arith)
+        assert st == 0
+        count = int(out[0, D])
+        assert out[0, :count].tolist() == z[f"nodes_{i}"].tolist(), i
+        assert int(out[0, D + 1]) == int(z[f"bonus_{i}"]), i
+
+
+@pytest.mark.parametrize("arith", [oracle.ARITH_EXACT, oracle.ARITH_FP64])
 @pytest.mark.parametrize("name,rule", [("accept_scan.npz", oracle.RULE_SCAN),
                                        ("accept_sparse.npz", oracle.RULE_SPARSE_EXIT)])
 def test_oracle_matches_reference_walk(golden_dir, name, rule, arith):
