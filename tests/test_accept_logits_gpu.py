@@ -17,7 +17,7 @@ from specgrove_b200.workloads import random_topology
 pytestmark = pytest.mark.gpu
 
 
-def _trees(rng, sizes, vocab, logits, topology=None):
+def _trees(rng, sizes, vocab, logits, topology=None, boost=(14.0, 20.0)):
     parents_b, tokens_b = [], []
     off = 0
     for n in sizes:
@@ -30,7 +30,7 @@ def _trees(rng, sizes, vocab, logits, topology=None):
                 t = int(rng.integers(0, vocab))
             used.add(t)
             toks.append(t)
-            logits[off + parents[j], t] += float(rng.uniform(4.0, 9.0))   # children likely: walks go deep
+            logits[off + parents[j], t] += float(rng.uniform(*boost))   # children likely: walks go deep
         parents_b.append(parents)
         tokens_b.append(toks)
         off += n
@@ -92,7 +92,7 @@ def test_logits_kernel_matches_oracle_with_philox(cuda_lib):
     V = 151936
     g = torch.Generator(device="cuda").manual_seed(7)
     host = (torch.randn((sum(sizes), V), generator=g, device="cuda") * 3.0).cpu()
-    parents_b, tokens_b = _trees(rng, sizes, V, host)
+    parents_b, tokens_b = _trees(rng, sizes, V, host, boost=(17.0, 24.0))
     logits = host.to(torch.bfloat16)
     trees = PackedTrees(parents_b, tokens_b, "cuda")
     rids = torch.arange(20, dtype=torch.long, device="cuda") * 977 + 5
@@ -106,6 +106,7 @@ def test_logits_kernel_matches_oracle_with_philox(cuda_lib):
                                         request_ids=rids.cpu().numpy())
     assert st == 0 and int(status) == 0
     assert (out == expected).all()
+    assert (out[:, trees.max_depth] > 1).any()      # deep walks are covered
 
 
 def test_reference_named_verifiers_draw_like_the_reference(cuda_lib, ref):
@@ -116,7 +117,7 @@ def test_reference_named_verifiers_draw_like_the_reference(cuda_lib, ref):
     rng = np.random.default_rng(3)
     g = torch.Generator(device="cuda").manual_seed(3)
     host = (torch.randn((T * n, V), generator=g, device="cuda") * 2.0).cpu()
-    parents_b, tokens_b = _trees(rng, [n] * T, V, host, random_topology(rng, n, 16, 4)[0])
+    parents_b, tokens_b = _trees(rng, [n] * T, V, host, random_topology(rng, n, 16, 4)[0], boost=(4.0, 9.0))
     logits = host.cuda().view(T, n, V)
     single = sampling.tree_verify_ancestral_logits_fused_scan(parents_b[0], tokens_b[0], logits[0], 1.0,
                                                              generator=torch.Generator(device="cuda").manual_seed(9))
