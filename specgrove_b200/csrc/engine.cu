@@ -15,6 +15,7 @@
 //   append_packed_sequence (:2121)   -> in-place arena commit
 #include <cuda_bf16.h>
 
+#include <cstdlib>
 #include <memory>
 #include <vector>
 
@@ -47,6 +48,8 @@ struct Engine {
   size_t workspace_bytes = 0;
   float* x;
   __nv_bfloat16 *xn, *qkv, *q, *attn, *h;
+  float* ssq;      // [max_rows][ss_parts] row sums of squares of the residual (folded RMSNorms)
+  int ss_parts;    // column tiles of the residual GEMMs
   float4* partials;
   float* lse_ws;
   int64_t* posterior_ws;
@@ -64,6 +67,30 @@ T* carve(uint8_t*& cursor, size_t count) {
   uintptr_t p = (reinterpret_cast<uintptr_t>(cursor) + 255) & ~uintptr_t(255);
   cursor = reinterpret_cast<uint8_t*>(p + count * sizeof(T));
   return reinterpret_cast<T*>(p);
+}
+
+// SG_QKV_FUSED=0 runs the q/k norm + RoPE + KV write as its own kernel after
+// a plain q/k/v GEMM (the two forms compute the same values; the switch is
+// for A/B timing).
+bool qkv_fused() {
+  static const bool fused = [] {
+    const char* v = std::getenv("SG_QKV_FUSED");
+    return v == nullptr || v[0] != '0';
+  }();
+  return fused;
+}
+
+// SG_NORM_FUSED=0 runs the input and post-attention RMSNorms as kernels
+// instead of folding them into the neighbouring GEMM epilogues (the residual
+// epilogue writes bf16(x * w) and per-tile sums of squares, the next GEMM
+// scales each row by rsqrt(mean(x^2) + eps)).  The folded form needs the
+// fused q/k/v epilogue.
+bool norm_fused() {
+  static const bool fused = [] {
+    const char* v = std::getenv("SG_NORM_FUSED");
+    return v == nullptr || v[0] != '0';
+  }();
+  return fused && qkv_fused();
 }
 
 inline void trace(const sg_wave_desc& w, int point, cudaStream_t stream) {
@@ -93,6 +120,7 @@ size_t workspace_size(const sg_model_desc& m, int rows, int sms) {
   s += rows * vt * 16 + 256;                  // partials
   s += rows * 4 + 256;                        // lse
   s += rows * 8 + 256;                        // posterior
+  s += rows * ((H + gemm::BN - 1) / gemm::BN) * 4 + 256;  // row sums of squares (folded norms)
   s += rows * layers::kAncWords * 4 + 256;    // anc
   s += rows * 4 * 3 + 3 * 256;                // position, tree, local
   s += rows * 8 + 256;                        // request id
@@ -186,6 +214,8 @@ extern "C" int sg_engine_create(const sg_model_desc* model, const sg_arena_desc*
   e->partials = carve<float4>(cur, static_cast<size_t>(max_rows) * e->vocab_tiles);
   e->lse_ws = carve<float>(cur, max_rows);
   e->posterior_ws = carve<int64_t>(cur, max_rows);
+  e->ss_parts = (H + gemm::BN - 1) / gemm::BN;
+  e->ssq = carve<float>(cur, static_cast<size_t>(max_rows) * e->ss_parts);
   e->meta.anc = carve<uint32_t>(cur, static_cast<size_t>(max_rows) * layers::kAncWords);
   e->meta.position = carve<int32_t>(cur, max_rows);
   e->meta.tree = carve<int32_t>(cur, max_rows);
@@ -286,6 +316,12 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
   if ((st = layers::launch_embed(w.tokens, static_cast<const __nv_bfloat16*>(m.embed), m.vocab, H, Q, e->x, w.status,
                                  stream)) != SG_OK)
     return st;
+  const bool nf = norm_fused();
+  const int P = e->ss_parts;
+  const float inv_h = 1.0f / static_cast<float>(H);
+  if (nf && (st = layers::launch_norm_fold(e->x, static_cast<const __nv_bfloat16*>(e->layer_ptrs[W_IN_NORM]), H, Q,
+                                           e->xn, e->ssq, stream)) != SG_OK)
+    return st;
 
   if ((st = layers::launch_attention_work(w.row_offsets, w.cache_lengths, R, nq / nkv, nkv, e->work, m.num_layers,
                                          stream)) != SG_OK)
@@ -307,10 +343,34 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
     __nv_bfloat16* k_plane0 = arena + static_cast<int64_t>(l) * 2 * nkv * plane_stride;
     __nv_bfloat16* v_plane0 = k_plane0 + static_cast<int64_t>(nkv) * plane_stride;
 
-    if ((st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(lw[W_IN_NORM]), H, Q, m.rms_eps, e->xn,
-                                     stream)) != SG_OK)
+    if (!nf && (st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(lw[W_IN_NORM]), H, Q, m.rms_eps,
+                                            e->xn, stream)) != SG_OK)
       return st;
     if (l == 0) trace(w, 2, stream);
+    // input RMSNorm's row scale: sums from the fold kernel (layer 0, one part)
+    // or from the previous down projection's tiles
+    const gemm::RowNorm rn_in = nf ? gemm::RowNorm{e->ssq, l == 0 ? 1 : P, inv_h, m.rms_eps} : gemm::RowNorm{};
+    if (qkv_fused()) {
+      // q/k/v projection with q/k RMSNorm, RoPE and the KV-tail write in its epilogue
+      if (D == 128) {
+        gemm::EpiQkvPost<128>::Params pf{e->q, qw, k_plane0, v_plane0, plane_stride, e->meta.arena_row,
+                                         e->meta.rope, static_cast<const __nv_bfloat16*>(lw[W_Q_NORM]),
+                                         static_cast<const __nv_bfloat16*>(lw[W_K_NORM]), nq, nkv, m.rms_eps,
+                                         w.status, rn_in};
+        st = gemm::launch<gemm::EpiQkvPost<128>>(e->xn_map, lm.qkv, s_qkv, pf, stream, small_wave(s_qkv));
+      } else {
+        gemm::EpiQkvPost<64>::Params pf{e->q, qw, k_plane0, v_plane0, plane_stride, e->meta.arena_row,
+                                        e->meta.rope, static_cast<const __nv_bfloat16*>(lw[W_Q_NORM]),
+                                        static_cast<const __nv_bfloat16*>(lw[W_K_NORM]), nq, nkv, m.rms_eps,
+                                        w.status, rn_in};
+        st = gemm::launch<gemm::EpiQkvPost<64>>(e->xn_map, lm.qkv, s_qkv, pf, stream, small_wave(s_qkv));
+      }
+      if (st != SG_OK) return st;
+      if (l == 0) {
+        trace(w, 3, stream);
+        trace(w, 4, stream);
+      }
+    } else {
     gemm::EpiStoreBf16::Params pq{e->qkv, qkv_n, w.status};
     if ((st = gemm::launch<gemm::EpiStoreBf16>(e->xn_map, lm.qkv, s_qkv, pq, stream, small_wave(s_qkv))) != SG_OK) return st;
     if (l == 0) trace(w, 3, stream);
@@ -341,6 +401,7 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
     qp.status = w.status;
     if ((st = layers::launch_qkv_post(qp, stream)) != SG_OK) return st;
     if (l == 0) trace(w, 4, stream);
+    }
 
     attn::Params ap;
     ap.q = e->q;
@@ -369,13 +430,20 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
     if (l == 0) trace(w, 5, stream);
 
     gemm::EpiResidual::Params po{e->x, H, nullptr, 0, w.status};
+    if (nf) {  // fold the post-attention RMSNorm into this epilogue and the gate/up GEMM
+      po.xw = e->xn;
+      po.ldw = H;
+      po.norm_w = static_cast<const __nv_bfloat16*>(lw[W_POST_NORM]);
+      po.ssq = e->ssq;
+      po.ss_parts = P;
+    }
     if ((st = gemm::launch<gemm::EpiResidual>(e->attn_map, lm.o, s_o, po, stream, small_wave(s_o))) != SG_OK) return st;
     if (l == 0) trace(w, 6, stream);
-    if ((st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(lw[W_POST_NORM]), H, Q, m.rms_eps,
-                                     e->xn, stream)) != SG_OK)
+    if (!nf && (st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(lw[W_POST_NORM]), H, Q,
+                                            m.rms_eps, e->xn, stream)) != SG_OK)
       return st;
     if (l == 0) trace(w, 7, stream);
-    gemm::EpiSwiGlu::Params pg{e->h, I, w.status};
+    gemm::EpiSwiGlu::Params pg{e->h, I, w.status, nf ? gemm::RowNorm{e->ssq, P, inv_h, m.rms_eps} : gemm::RowNorm{}};
     if ((st = gemm::launch<gemm::EpiSwiGlu>(e->xn_map, lm.gate_up, s_gu, pg, stream, small_wave(s_gu))) != SG_OK) return st;
     if (l == 0) trace(w, 8, stream);
     // the residual stream after this layer is hidden_states[l + 1]; the last
@@ -384,6 +452,13 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
     if (feature_slot[l] >= 0 && l + 1 < m.num_layers)
       feat = static_cast<__nv_bfloat16*>(w.features_out) + static_cast<int64_t>(feature_slot[l]) * H;
     gemm::EpiResidual::Params pd{e->x, H, feat, static_cast<int64_t>(nfeat) * H, w.status};
+    if (nf && l + 1 < m.num_layers) {  // fold the next layer's input RMSNorm
+      pd.xw = e->xn;
+      pd.ldw = H;
+      pd.norm_w = static_cast<const __nv_bfloat16*>(e->layer_ptrs[static_cast<size_t>(l + 1) * W_COUNT + W_IN_NORM]);
+      pd.ssq = e->ssq;
+      pd.ss_parts = P;
+    }
     if ((st = gemm::launch<gemm::EpiResidual>(e->h_map, lm.down, s_down, pd, stream, small_wave(s_down))) != SG_OK) return st;
     if (l == 0) trace(w, 9, stream);
   }
@@ -391,10 +466,23 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
   if (w.hidden_out != nullptr)
     SG_CUDA_CHECK(cudaMemcpyAsync(w.hidden_out, e->x, static_cast<size_t>(Q) * H * 4, cudaMemcpyDeviceToDevice,
                                   stream));
-  if ((st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(m.final_norm), H, Q, m.rms_eps, e->xn,
-                                   stream)) != SG_OK)
+  // final RMSNorm: folded into the LM head (one fold kernel per pass, the
+  // same computation as sg_lm_head_sample), or as a kernel
+  if (nf) {
+    if ((st = layers::launch_norm_fold(e->x, static_cast<const __nv_bfloat16*>(m.final_norm), H, Q, e->xn, e->ssq,
+                                       stream)) != SG_OK)
+      return st;
+  } else if ((st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(m.final_norm), H, Q, m.rms_eps,
+                                          e->xn, stream)) != SG_OK) {
     return st;
-  if (feature_slot[m.num_layers - 1] >= 0) {
+  }
+  if (nf && feature_slot[m.num_layers - 1] >= 0) {  // the final-normed stream, for the drafter
+    if ((st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(m.final_norm), H, Q, m.rms_eps,
+                                     static_cast<__nv_bfloat16*>(w.features_out) +
+                                         static_cast<int64_t>(feature_slot[m.num_layers - 1]) * H,
+                                     stream, static_cast<int64_t>(nfeat) * H)) != SG_OK)
+      return st;
+  } else if (feature_slot[m.num_layers - 1] >= 0) {
     const size_t pitch = static_cast<size_t>(nfeat) * H * 2;
     SG_CUDA_CHECK(cudaMemcpy2DAsync(static_cast<uint8_t*>(w.features_out) +
                                         static_cast<size_t>(feature_slot[m.num_layers - 1]) * H * 2,
@@ -411,6 +499,7 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
   pl.inv_temp = inv_temp;
   pl.greedy = greedy ? 1 : 0;
   pl.status = w.status;
+  pl.rn = nf ? gemm::RowNorm{e->ssq, 1, inv_h, m.rms_eps} : gemm::RowNorm{};
   if ((st = gemm::launch<gemm::EpiLmHead>(e->xn_map, e->lm_map, gemm::make_shape(Q, m.vocab, H), pl, stream)) !=
       SG_OK)
     return st;
@@ -422,7 +511,7 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
   if (w.child_logprob != nullptr &&
       (st = layers::launch_child_logprob(e->xn, static_cast<const __nv_bfloat16*>(m.lm_head), H, m.vocab, w.tokens, w.parents,
                                          w.row_offsets, e->meta.tree, e->meta.local, lse, inv_temp, Q,
-                                         w.child_logprob, stream)) != SG_OK)
+                                         w.child_logprob, stream, nf ? e->ssq : nullptr, 1, m.rms_eps)) != SG_OK)
     return st;
   trace(w, 13, stream);
   if ((st = sg_tree_follow(posterior, w.row_offsets, w.parents, w.tokens, R, w.max_rows_per_request, w.max_depth,

@@ -472,7 +472,30 @@ struct EpiStoreF32 {
   }
 };
 
-// Residual stream update: x (fp32) += acc, and x_bf16 = bf16(x) for the next GEMM.
+// Row scale of the RMSNorm folded into a GEMM: the producer of the GEMM's A
+// operand wrote bf16(x * w) and, per row, partial sums of squares of x over
+// `parts` column tiles; rstd = rsqrt(mean(x^2) + eps) multiplies the
+// accumulator of the row (A = x * rstd * w up to one bf16 rounding).
+struct RowNorm {
+  const float* ssq;  // [rows][parts], or null: no scaling
+  int parts;
+  float inv_h;       // 1 / hidden
+  float eps;
+  __device__ __forceinline__ float rstd(int row, bool valid) const {
+    if (ssq == nullptr) return 1.0f;
+    if (!valid) return 0.0f;
+    const float* s = ssq + static_cast<int64_t>(row) * parts;
+    float t = 0.f;
+    for (int i = 0; i < parts; ++i) t += s[i];
+    return rsqrtf(__fmaf_rn(t, inv_h, eps));
+  }
+};
+
+// Residual stream update: x (fp32) += acc.  Optional outputs, all from the
+// updated x: x_bf16 = bf16(x) (the drafter's hidden state), xw = bf16(x *
+// norm_w) (the next GEMM's A operand with the next RMSNorm's weight folded
+// in), ssq[row][n0 / BN] = sum of x^2 over this tile's columns (the next
+// GEMM's row scale, RowNorm).
 struct EpiResidual {
   struct Params {
     float* x;
@@ -480,11 +503,17 @@ struct EpiResidual {
     __nv_bfloat16* x_bf16;  // may be null
     int64_t ldb;
     int32_t* status;
+    __nv_bfloat16* xw;            // may be null
+    int64_t ldw;
+    const __nv_bfloat16* norm_w;  // [N] weight of the next RMSNorm (with xw)
+    float* ssq;                   // may be null; [rows][ss_parts]
+    int ss_parts;
   };
   static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int m0, int n0,
                                                int quarter, int lane, uint4* st) {
     const int row0 = m0 + quarter * 32;
     const int q = lane & 7;
+    float ssr[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // rows i * 4 + lane / 8, this lane's columns
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       const int col = n0 + c * 32;
@@ -518,9 +547,29 @@ struct EpiResidual {
           if (p.x_bf16 != nullptr)
             *reinterpret_cast<uint2*>(p.x_bf16 + static_cast<int64_t>(row) * p.ldb + col + q * 4) =
                 make_uint2(sm100::pack_bf16x2(x.x, x.y), sm100::pack_bf16x2(x.z, x.w));
+          if (p.xw != nullptr) {
+            const uint2 wr = *reinterpret_cast<const uint2*>(p.norm_w + col + q * 4);
+            const float2 w01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wr.x));
+            const float2 w23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wr.y));
+            *reinterpret_cast<uint2*>(p.xw + static_cast<int64_t>(row) * p.ldw + col + q * 4) =
+                make_uint2(sm100::pack_bf16x2(x.x * w01.x, x.y * w01.y), sm100::pack_bf16x2(x.z * w23.x, x.w * w23.y));
+          }
+          ssr[i] += (x.x * x.x + x.y * x.y) + (x.z * x.z + x.w * x.w);
         }
       }
       __syncwarp();
+    }
+    if (p.ssq != nullptr) {
+      // the 8 lanes of a row (same lane / 8) hold its 8 column groups
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float v = ssr[i];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        const int row = row0 + i * 4 + (lane >> 3);
+        if (q == 0 && row < s.M) p.ssq[static_cast<int64_t>(row) * p.ss_parts + n0 / BN] = v;
+      }
     }
   }
 };
@@ -533,10 +582,13 @@ struct EpiSwiGlu {
     __nv_bfloat16* out;
     int64_t ldo;
     int32_t* status;
+    RowNorm rn;  // the post-attention RMSNorm's row scale (ssq null: none)
   };
   static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int m0, int n0,
                                                int quarter, int lane, uint4* st) {
     if (n0 >= s.N) return;
+    const int row = m0 + quarter * 32 + lane;
+    const float rs = p.rn.rstd(row, row < s.M);
 #pragma unroll 1
     for (int c = 0; c < BN / 128; ++c) {  // 64 output columns per pass
       uint32_t w[32];
@@ -548,9 +600,9 @@ struct EpiSwiGlu {
         sm100::tmem_wait_ld();
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float g0 = g[2 * e], g1 = g[2 * e + 1];
-          w[h * 16 + e] = sm100::pack_bf16x2(g0 / (1.0f + __expf(-g0)) * u[2 * e],
-                                             g1 / (1.0f + __expf(-g1)) * u[2 * e + 1]);
+          const float g0 = g[2 * e] * rs, g1 = g[2 * e + 1] * rs;
+          w[h * 16 + e] = sm100::pack_bf16x2(g0 / (1.0f + __expf(-g0)) * (u[2 * e] * rs),
+                                             g1 / (1.0f + __expf(-g1)) * (u[2 * e + 1] * rs));
         }
       }
       store_bf16_rows(st, lane, w, p.out, p.ldo, m0 + quarter * 32, s.M, n0 / 2 + c * 64, 64);
@@ -558,6 +610,147 @@ struct EpiSwiGlu {
   }
 };
 
+
+// Stage 64 bf16 per row (8 x 16 B) and store row rr of the warp's 32 rows at
+// dst(rr) (a pointer to its 64 columns, or null to skip the row); the
+// transposed read-back lets 8 lanes cover one row's 128-byte line.
+template <class RowPtr>
+__device__ __forceinline__ void store_bf16_rows_to(uint4* st, int lane, const uint32_t (&w)[32], RowPtr dst) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) stage_put(st, lane, q, make_uint4(w[q * 4], w[q * 4 + 1], w[q * 4 + 2], w[q * 4 + 3]));
+  __syncwarp();
+  const int q = lane & 7;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int rr = i * 4 + (lane >> 3);
+    const uint4 v = stage_get(st, rr, q);
+    __nv_bfloat16* d = dst(rr);
+    if (d != nullptr) *reinterpret_cast<uint4*>(d + q * 8) = v;
+  }
+  __syncwarp();
+}
+
+// The q/k/v projection with the per-head work of the Qwen3 attention input
+// fused in (HF Qwen3Attention: q_norm / k_norm RMSNorm over each head, then
+// rotate-half RoPE at the row's position): a 256-column tile holds whole
+// heads (256 % D == 0), and each epilogue thread owns one row, so the head's
+// sum of squares and its rotary pairs (d, d + D/2) are in the thread's own
+// accumulator columns.  Query heads go to q_out [rows, nq * D]; key and value
+// heads straight to the request's KV-arena tail (arena_row[row], -1: skip).
+// Angles come from the pass's rotary table rope[row][d] = (cos, sin).
+template <int D>
+struct EpiQkvPost {
+  struct Params {
+    __nv_bfloat16* q_out;
+    int64_t ldq;
+    __nv_bfloat16* k_plane0;     // K plane of kv head 0 of this layer
+    __nv_bfloat16* v_plane0;     // V plane of kv head 0 of this layer
+    int64_t plane_stride;        // elements between consecutive kv heads' planes
+    const int64_t* arena_row;    // [rows]
+    const float2* rope;          // [rows][D/2]
+    const __nv_bfloat16* q_norm; // [D]
+    const __nv_bfloat16* k_norm; // [D]
+    int nq, nkv;
+    float eps;
+    int32_t* status;
+    RowNorm rn;  // the input RMSNorm's row scale (ssq null: none)
+  };
+  static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int m0, int n0,
+                                               int quarter, int lane, uint4* st) {
+    static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+    constexpr int HALF = D / 2;
+    const int row0 = m0 + quarter * 32;
+    const int row = row0 + lane;
+    const bool rv = row < s.M;
+    const float rs = p.rn.rstd(row, rv);
+    const int heads = min(BN, s.N - n0) / D;
+#pragma unroll 1
+    for (int hi = 0; hi < heads; ++hi) {
+      const int head = n0 / D + hi;
+      const uint32_t hbase = taddr + static_cast<uint32_t>(hi * D);
+      const bool is_q = head < p.nq;
+      const bool is_k = !is_q && head < p.nq + p.nkv;
+      // destination of row rr's columns [c0, c0 + 64) of this head
+      auto dst = [&](int c0) {
+        return [&, c0](int rr) -> __nv_bfloat16* {
+          const int r = row0 + rr;
+          if (r >= s.M) return nullptr;
+          if (is_q) return p.q_out + static_cast<int64_t>(r) * p.ldq + static_cast<int64_t>(head) * D + c0;
+          const int64_t ar = p.arena_row[r];
+          if (ar < 0) return nullptr;
+          const int kvh = is_k ? head - p.nq : head - p.nq - p.nkv;
+          return (is_k ? p.k_plane0 : p.v_plane0) + static_cast<int64_t>(kvh) * p.plane_stride + ar * D + c0;
+        };
+      };
+      if (!is_q && !is_k) {  // value head: plain copy
+#pragma unroll 1
+        for (int c = 0; c < D / 64; ++c) {
+          float a[32], b[32];
+          sm100::tmem_ld32(hbase + c * 64, a);
+          sm100::tmem_ld32(hbase + c * 64 + 32, b);
+          uint32_t w[32];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            w[e] = sm100::pack_bf16x2(a[2 * e] * rs, a[2 * e + 1] * rs);
+            w[16 + e] = sm100::pack_bf16x2(b[2 * e] * rs, b[2 * e + 1] * rs);
+          }
+          store_bf16_rows_to(st, lane, w, dst(c * 64));
+        }
+        continue;
+      }
+      float ss = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        float a[32];
+        sm100::tmem_ld32(hbase + c * 32, a);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float v = a[e] * rs;
+          ss += v * v;
+        }
+      }
+      // head RMSNorm of the input-normed projection: scale rs, then rstd
+      const float rstd = rsqrtf(ss / static_cast<float>(D) + p.eps) * rs;
+      const __nv_bfloat16* wn = is_q ? p.q_norm : p.k_norm;
+      const float2* rp = p.rope + static_cast<int64_t>(rv ? row : row0) * HALF;
+      uint32_t lo[HALF / 2], up[HALF / 2];  // packed bf16 pairs of dims [0, D/2) and [D/2, D)
+#pragma unroll
+      for (int c = 0; c < HALF / 32; ++c) {
+        float a[32], b[32];
+        sm100::tmem_ld32(hbase + c * 32, a);
+        sm100::tmem_ld32(hbase + HALF + c * 32, b);
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float ra[2], rb[2];
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int d = c * 32 + e + k;
+            const float2 cs = rv ? rp[d] : make_float2(1.f, 0.f);
+            const float xa = a[e + k] * rstd * __bfloat162float(wn[d]);
+            const float xb = b[e + k] * rstd * __bfloat162float(wn[d + HALF]);
+            // rotate_half: out_d = x_d cos - x_{d+H} sin,  out_{d+H} = x_{d+H} cos + x_d sin
+            ra[k] = xa * cs.x - xb * cs.y;
+            rb[k] = xb * cs.x + xa * cs.y;
+          }
+          lo[c * 16 + e / 2] = sm100::pack_bf16x2(ra[0], ra[1]);
+          up[c * 16 + e / 2] = sm100::pack_bf16x2(rb[0], rb[1]);
+        }
+      }
+      if constexpr (D == 128) {
+        store_bf16_rows_to(st, lane, lo, dst(0));
+        store_bf16_rows_to(st, lane, up, dst(64));
+      } else {
+        uint32_t w[32];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          w[e] = lo[e];
+          w[16 + e] = up[e];
+        }
+        store_bf16_rows_to(st, lane, w, dst(0));
+      }
+    }
+  }
+};
 
 // LM head fused with softmax and sampling: full-vocabulary logits never reach
 // HBM.  Per (row, 256-column vocab tile) the epilogue writes
@@ -616,6 +809,7 @@ struct EpiLmHead {
     float inv_temp;            // 1 / T (1 for greedy rows)
     int greedy;                // 1: argmax of bf16 logits
     int32_t* status;
+    RowNorm rn;                // the final RMSNorm's row scale (ssq null: none)
   };
   static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int m0, int n0,
                                                int quarter, int lane, uint4*) {
@@ -623,6 +817,9 @@ struct EpiLmHead {
     const int row = m0 + quarter * 32 + lane;
     const bool rv = row < s.M;
     const int nch = min(BN, s.N - n0) / 32;  // N % 32 == 0; uniform over the CTA
+    // logit = rstd * acc; x = logit / T = acc * xs (one rounded factor for every pass)
+    const float rs = p.rn.rstd(row, rv);
+    const float xs = __fmul_rn(rs, p.inv_temp);
     // pass 1: tile max of x = logit / T (greedy: first maximum of bf16(logit))
     float m = -INFINITY, gbest = -INFINITY;
     int gcol = n0;
@@ -633,8 +830,8 @@ struct EpiLmHead {
       if (p.greedy) {
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          m = fmaxf(m, __fmul_rn(v[e], p.inv_temp));
-          const float b = bf16_round(v[e]);
+          m = fmaxf(m, __fmul_rn(v[e], xs));
+          const float b = bf16_round(__fmul_rn(v[e], rs));
           if (b > gbest) {
             gbest = b;
             gcol = n0 + c * 32 + e;
@@ -642,7 +839,7 @@ struct EpiLmHead {
         }
       } else {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) m = fmaxf(m, __fmul_rn(v[e], p.inv_temp));
+        for (int e = 0; e < 32; ++e) m = fmaxf(m, __fmul_rn(v[e], xs));
       }
     }
     // pass 2: per-chunk masses with the tile max (sequential fp32 sums)
@@ -656,7 +853,7 @@ struct EpiLmHead {
         sm100::tmem_ld32(taddr + c * 32, v);
         float a = 0.f;
 #pragma unroll
-        for (int e = 0; e < 32; ++e) a = __fadd_rn(a, lm_tile_weight(v[e], p.inv_temp, m));
+        for (int e = 0; e < 32; ++e) a = __fadd_rn(a, lm_tile_weight(v[e], xs, m));
         cs[c] = a;
         S = __fadd_rn(S, a);
       }
@@ -704,7 +901,7 @@ struct EpiLmHead {
           float a = 0.f;
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            a = __fadd_rn(a, lm_tile_weight(v[e], p.inv_temp, m));
+            a = __fadd_rn(a, lm_tile_weight(v[e], xs, m));
             if (col < 0 && thr < __fadd_rn(base, a)) col = n0 + c * 32 + e;
           }
           if (col < 0) col = n0 + c * 32 + 31;

@@ -144,7 +144,8 @@ __global__ void embed_kernel(const int64_t* __restrict__ tokens, const __nv_bflo
 
 // y = bf16(x * rsqrt(mean(x^2) + eps) * w); one CTA of 256 threads per row.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ x, const __nv_bfloat16* __restrict__ w,
-                                                      int hidden, float eps, __nv_bfloat16* __restrict__ out) {
+                                                      int hidden, float eps, __nv_bfloat16* __restrict__ out,
+                                                      int64_t ld_out, float* __restrict__ ssq) {
   pdl_trigger();
   pdl_wait();
   const int row = blockIdx.x;
@@ -181,9 +182,11 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ 
     if (threadIdx.x == 0) red[0] = t;
   }
   __syncthreads();
-  const float rstd = rsqrtf(red[0] / static_cast<float>(hidden) + eps);
+  // folded form (ssq given): the consumer GEMM applies rstd per row
+  const float rstd = ssq != nullptr ? 1.0f : rsqrtf(red[0] / static_cast<float>(hidden) + eps);
+  if (ssq != nullptr && threadIdx.x == 0) ssq[row] = red[0];
   const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(w);
-  uint2* o = reinterpret_cast<uint2*>(out + static_cast<int64_t>(row) * hidden);
+  uint2* o = reinterpret_cast<uint2*>(out + static_cast<int64_t>(row) * ld_out);
   auto scale = [&](int i, float4 v) {
     const float2 wa = __bfloat1622float2(w2[2 * i]);
     const float2 wb = __bfloat1622float2(w2[2 * i + 1]);
@@ -448,7 +451,8 @@ __global__ void child_logprob_kernel(const __nv_bfloat16* __restrict__ h, const 
                                      const int64_t* __restrict__ parents, const int64_t* __restrict__ row_offsets,
                                      const int32_t* __restrict__ tree, const int32_t* __restrict__ local,
                                      const float* __restrict__ lse, float inv_temp, int rows,
-                                     float* __restrict__ logprob) {
+                                     float* __restrict__ logprob, const float* __restrict__ ssq, int ss_parts,
+                                     float inv_h, float eps) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -473,7 +477,15 @@ __global__ void child_logprob_kernel(const __nv_bfloat16* __restrict__ h, const 
   }
 #pragma unroll
   for (int d = 16; d >= 1; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
-  if (lane == 0) logprob[row] = acc * inv_temp - lse[prow];
+  // h holds bf16(x * w) when the final norm is folded (ssq given): the row
+  // scale rstd joins 1/T exactly as in the LM-head epilogue
+  float xs = inv_temp;
+  if (ssq != nullptr) {
+    float t = 0.f;
+    for (int i = 0; i < ss_parts; ++i) t += ssq[prow * ss_parts + i];
+    xs = __fmul_rn(rsqrtf(__fmaf_rn(t, inv_h, eps)), inv_temp);
+  }
+  if (lane == 0) logprob[row] = acc * xs - lse[prow];
 }
 
 // One CTA per request: its kept rows go to dst rows base .. base + count,
@@ -573,10 +585,21 @@ int launch_embed(const int64_t* tokens, const __nv_bfloat16* embed, int64_t voca
 }
 
 int launch_rmsnorm(const float* x, const __nv_bfloat16* weight, int hidden, int rows, float eps,
-                   __nv_bfloat16* out, cudaStream_t stream) {
+                   __nv_bfloat16* out, cudaStream_t stream, int64_t ld_out) {
   if (rows <= 0) return SG_OK;
   if (hidden % 4 != 0) return fail(SG_ERR_UNSUPPORTED, "rmsnorm: hidden % 4 != 0");
-  return launch_pdl("rmsnorm_kernel", rmsnorm_kernel, dim3(rows), dim3(256), 0, stream, x, weight, hidden, eps, out);
+  if (ld_out == 0) ld_out = hidden;
+  if (ld_out % 4 != 0) return fail(SG_ERR_UNSUPPORTED, "rmsnorm: output stride % 4 != 0");
+  return launch_pdl("rmsnorm_kernel", rmsnorm_kernel, dim3(rows), dim3(256), 0, stream, x, weight, hidden, eps, out,
+                    ld_out, static_cast<float*>(nullptr));
+}
+
+int launch_norm_fold(const float* x, const __nv_bfloat16* weight, int hidden, int rows, __nv_bfloat16* xw,
+                     float* ssq, cudaStream_t stream) {
+  if (rows <= 0) return SG_OK;
+  if (hidden % 4 != 0) return fail(SG_ERR_UNSUPPORTED, "rmsnorm: hidden % 4 != 0");
+  return launch_pdl("rmsnorm_kernel", rmsnorm_kernel, dim3(rows), dim3(256), 0, stream, x, weight, hidden, 0.f, xw,
+                    static_cast<int64_t>(hidden), ssq);
 }
 
 int launch_qkv_post(const QkvPost& p, cudaStream_t stream) {
@@ -608,10 +631,11 @@ int launch_child_logprob(const __nv_bfloat16* h, const __nv_bfloat16* lm_head, i
                          const int64_t* tokens,
                          const int64_t* parents, const int64_t* row_offsets, const int32_t* tree,
                          const int32_t* local, const float* lse, float inv_temp, int rows, float* logprob,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, const float* ssq, int ss_parts, float eps) {
   if (rows <= 0) return SG_OK;
   child_logprob_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(h, lm_head, hidden, vocab, tokens, parents, row_offsets, tree,
-                                                           local, lse, inv_temp, rows, logprob);
+                                                           local, lse, inv_temp, rows, logprob, ssq, ss_parts,
+                                                           1.0f / static_cast<float>(hidden), eps);
   return check_launch("child_logprob_kernel");
 }
 

@@ -48,7 +48,13 @@ int launch_embed(const int64_t* tokens, const __nv_bfloat16* embed, int64_t voca
                  float* x, int32_t* status, cudaStream_t stream);
 
 int launch_rmsnorm(const float* x, const __nv_bfloat16* weight, int hidden, int rows, float eps,
-                   __nv_bfloat16* out, cudaStream_t stream);
+                   __nv_bfloat16* out, cudaStream_t stream, int64_t ld_out = 0);
+
+// The RMSNorm folded into the next GEMM: xw = bf16(x * weight) and ssq[row]
+// = sum of x^2 (one part per row), the GEMM scaling each row by
+// rsqrt(ssq / hidden + eps) in its epilogue.
+int launch_norm_fold(const float* x, const __nv_bfloat16* weight, int hidden, int rows, __nv_bfloat16* xw,
+                     float* ssq, cudaStream_t stream);
 
 struct QkvPost {
   const __nv_bfloat16* qkv;     // [Q, (nq + 2 nkv) * D]
@@ -92,7 +98,7 @@ int launch_child_logprob(const __nv_bfloat16* h, const __nv_bfloat16* lm_head, i
                          const int64_t* tokens,
                          const int64_t* parents, const int64_t* row_offsets, const int32_t* tree,
                          const int32_t* local, const float* lse, float inv_temp, int rows, float* logprob,
-                         cudaStream_t stream);
+                         cudaStream_t stream, const float* ssq = nullptr, int ss_parts = 0, float eps = 0.f);
 
 }  // namespace layers
 }  // namespace sg

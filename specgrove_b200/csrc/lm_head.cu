@@ -20,7 +20,7 @@ bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 size_t lm_head_scratch_need(int rows, int hidden, int vocab) {
   const size_t tiles = static_cast<size_t>((vocab + gemm::BN - 1) / gemm::BN);
   return 256 /* status word */ + align256(static_cast<size_t>(rows) * hidden * 2) +
-         static_cast<size_t>(rows) * tiles * sizeof(float4);
+         align256(static_cast<size_t>(rows) * tiles * sizeof(float4)) + static_cast<size_t>(rows) * sizeof(float);
 }
 
 int lm_head_check(const char* who, const float* x, const void* final_norm, const void* lm_head, int32_t rows,
@@ -60,6 +60,11 @@ int lm_head_run(const float* x, const void* final_norm, const void* lm_head, int
   float4* partials = reinterpret_cast<float4*>(static_cast<uint8_t*>(scratch) + 256 +
                                                align256(static_cast<size_t>(rows) * hidden * 2));
   const int tiles = (vocab + gemm::BN - 1) / gemm::BN;
+  // the final RMSNorm folded into the LM head (as in sg_verify_pass): xn =
+  // bf16(x * final_norm), each row's logits scaled by rsqrt(mean(x^2) + eps)
+  float* ssq = normed != nullptr ? nullptr
+                                 : reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(partials) +
+                                                            align256(static_cast<size_t>(rows) * tiles * 16));
   CUtensorMap a_map, b_map;
   int st;
   if ((st = make_tmap_2d_bf16(&a_map, xn, hidden, rows, static_cast<uint64_t>(hidden) * 2, gemm::BK, gemm::BM)) !=
@@ -73,7 +78,7 @@ int lm_head_run(const float* x, const void* final_norm, const void* lm_head, int
   // rows x tiles partials).
   SG_CUDA_CHECK(cudaMemsetAsync(status, 0, sizeof(int32_t), s));
   if (normed == nullptr &&
-      (st = layers::launch_rmsnorm(x, static_cast<const __nv_bfloat16*>(final_norm), hidden, rows, rms_eps, xn, s)) !=
+      (st = layers::launch_norm_fold(x, static_cast<const __nv_bfloat16*>(final_norm), hidden, rows, xn, ssq, s)) !=
           SG_OK)
     return st;
   gemm::EpiLmHead::Params pl;
@@ -85,6 +90,7 @@ int lm_head_run(const float* x, const void* final_norm, const void* lm_head, int
   pl.greedy = temperature == 0.f ? 1 : 0;
   pl.inv_temp = pl.greedy ? 1.0f : 1.0f / temperature;
   pl.status = status;
+  pl.rn = gemm::RowNorm{ssq, 1, 1.0f / static_cast<float>(hidden), rms_eps};
   if ((st = gemm::launch<gemm::EpiLmHead>(a_map, b_map, gemm::make_shape(rows, vocab, hidden), pl, s)) != SG_OK)
     return st;
   // A GEMM that gave up on a bounded wait leaves partial results: the
