@@ -207,6 +207,85 @@ SG_API int sg_allocate_tiers(int32_t num_requests, const double* weights, int32_
                              double fixed_row_equivalent, const int32_t* curve_rows, const double* curve_cost,
                              int32_t curve_points, int32_t* allocation);
 
+/*
+ * sg_allocate_tiers on the device: the same knapsack, the same allocation
+ * bit for bit, as one CTA reading weights and utilities that device kernels
+ * produced (sg_build_draft_trees), so a wave is planned without a host round
+ * trip.  weights, utilities and allocation are DEVICE pointers (8-, 8-, 4-byte
+ * aligned); options and the cost curve are host arrays, checked on the host
+ * like sg_allocate_tiers.  At most 8 options, row_budget <= 8192, 64 curve
+ * points (SG_ERR_UNSUPPORTED otherwise).  workspace: device, 4-byte aligned,
+ * sg_allocate_tiers_device_workspace_bytes(num_requests, row_budget) bytes
+ * (per step and row total: the back pointer).  A weight or utility out of
+ * range (device-detected) sets SG_ERR_INVALID_ARGUMENT in *status, a wave
+ * that no allocation fits sets SG_ERR_CAPACITY; allocation is then -1.
+ */
+SG_API size_t sg_allocate_tiers_device_workspace_bytes(int32_t num_requests, int32_t row_budget);
+SG_API int sg_allocate_tiers_device(int32_t num_requests, const double* weights, int32_t num_options,
+                                    const int32_t* options, const double* utilities, int32_t row_budget,
+                                    double fixed_row_equivalent, const int32_t* curve_rows,
+                                    const double* curve_cost, int32_t curve_points, int32_t* allocation,
+                                    int32_t* status, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Draft-tree construction on the device (the proposal step before a wave).
+ *
+ * sg_proposal_topk: per row of drafter logits [rows, row_stride] (bf16 or
+ * fp32; a row = one (request, draft depth)), the k largest proposal masses
+ * of q = softmax(logits / T) in fp64 and their token ids, sorted by mass
+ * (ties to the lower token id): log_q[rows, k] fp64, ids[rows, k] int64.
+ * Replaces probabilities(logits, T, float64) + torch.topk(q, k) + log
+ * (sampling.py:29-36, tree.py:183-184).  1 <= k <= min(1024, vocab), T > 0.
+ * Non-finite logits set SG_ERR_PROBABILITY in *status.
+ */
+SG_API int sg_proposal_topk(const void* logits, int32_t dtype, int64_t row_stride, int32_t rows, int32_t vocab,
+                            int32_t k, double temperature, double* log_q, int64_t* ids, int32_t* status,
+                            void* stream);
+
+/*
+ * sg_build_draft_trees: the best-first prefix tree of every request
+ * (probability_tree, tree.py:148-212) from its ranked log masses
+ * log_q/ids [num_trees, length, width] (width = the top-k kept per depth,
+ * k = min(budget, vocab) in the reference), bit-equal to the reference's
+ * tree for the same log masses (same fp64 operation order, same tie order).
+ *   budgets      device [num_trees] per-request budgets (<= budget), or null
+ *   budget       node budget (and the row stride of the outputs), <= 4096
+ *   rewards      host [length] per-depth reward schedule, or null (all 0)
+ *   rank_caps    host [length] per-depth rank caps (>= 1), or null
+ *   adaptive_min_budget, confidence_threshold: on rounds whose mean greedy
+ *                log mass over the first 4 depths is >= log(threshold) the
+ *                budget becomes adaptive_min_budget (-1: off)
+ *   tiers        host [num_tiers] increasing tier sizes (<= 8 tiers): the
+ *                utility of tier b is the draft expected tokens of the first
+ *                b nodes (_prefix_tree / _draft_tree_expected_tokens,
+ *                continuous_tree_block_decode.py:560-586), NaN (and
+ *                SG_ERR_TREE) when the tree has fewer nodes
+ * Outputs (device): tokens [num_trees, budget] (node i >= 1 holds
+ * tokens[i - 1]), parents [num_trees, budget + 1] (root -1), depths and
+ * masses (prefix log mass incl. rewards) [num_trees, budget + 1],
+ * node_count [num_trees], utilities [num_trees, num_tiers] fp64 (input to
+ * sg_allocate_tiers_device).
+ */
+SG_API int sg_build_draft_trees(const double* log_q, const int64_t* ids, int32_t num_trees, int32_t length,
+                                int32_t width, const int32_t* budgets, int32_t budget, const double* rewards,
+                                const int32_t* rank_caps, int32_t adaptive_min_budget,
+                                double confidence_threshold, const int32_t* tiers, int32_t num_tiers,
+                                int64_t* tokens, int64_t* parents, int32_t* depths, double* masses,
+                                int32_t* node_count, double* utilities, int32_t* status, void* stream);
+
+/*
+ * sg_pack_tree_wave: the packed verify wave of the chosen tiers: request r
+ * takes rows row_offsets[r] .. row_offsets[r + 1] - 1 = its anchor token
+ * (anchor_tokens[r], the last generated token; parent -1) followed by the
+ * first allocation[r] nodes of its tree (parents as local row indices), the
+ * inputs of sg_verify_pass.  At most 1024 trees; a tier larger than the tree
+ * or a wave above max_rows sets SG_ERR_TREE (row_offsets then all 0).
+ */
+SG_API int sg_pack_tree_wave(const int64_t* tokens, const int64_t* parents, int32_t budget,
+                             const int32_t* node_count, const int32_t* allocation, const int64_t* anchor_tokens,
+                             int32_t num_trees, int64_t max_rows, int64_t* row_offsets, int64_t* wave_parents,
+                             int64_t* wave_tokens, int32_t* status, void* stream);
+
 /* Epilogues of sg_gemm_bf16. */
 enum sg_gemm_epilogue {
   SG_EPI_STORE_BF16 = 0, /* C bf16 [M, ldc] = acc */

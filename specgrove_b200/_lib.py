@@ -55,6 +55,18 @@ _SIGNATURES = {
     "sg_allocate_tiers": (ctypes.c_int, [
         c_int32, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_double, c_void_p, c_void_p, c_int32,
         c_void_p]),
+    "sg_allocate_tiers_device_workspace_bytes": (ctypes.c_size_t, [c_int32, c_int32]),
+    "sg_allocate_tiers_device": (ctypes.c_int, [
+        c_int32, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_double, c_void_p, c_void_p, c_int32,
+        c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_void_p]),
+    "sg_proposal_topk": (ctypes.c_int, [
+        c_void_p, c_int32, c_int64, c_int32, c_int32, c_int32, c_double, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "sg_build_draft_trees": (ctypes.c_int, [
+        c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_double,
+        c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "sg_pack_tree_wave": (ctypes.c_int, [
+        c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_int32, c_int64, c_void_p, c_void_p, c_void_p,
+        c_void_p, c_void_p]),
     "sg_lm_head_sample_workspace_bytes": (ctypes.c_size_t, [c_int32, c_int32, c_int32]),
     "sg_lm_head_sample": (ctypes.c_int, [
         c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, ctypes.c_float, c_void_p, c_void_p, c_uint64,

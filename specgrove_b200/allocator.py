@@ -85,6 +85,42 @@ def allocate_tree_budgets(weights: Sequence[float], budget_options: Sequence[int
     return tuple(int(v) for v in out)
 
 
+def allocate_tree_budgets_device(weights: torch.Tensor, budget_options: Sequence[int], utilities: torch.Tensor, *,
+                                 row_budget: int, fixed_row_equivalent: float | None = None,
+                                 row_cost_curve: Sequence[tuple[int, float]] | None = None,
+                                 status: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """``allocate_tree_budgets`` on the device for CUDA fp64 ``weights`` [R]
+    and ``utilities`` [R, T] (e.g. from the tree kernels): returns the int32
+    tier of each request as a CUDA tensor, enqueued on ``stream`` without a
+    host synchronisation.  Device-detected errors (a utility below 1, no
+    feasible wave) land in ``status`` (an int32 CUDA word, atomic max of the
+    codes) with every tier -1."""
+    R, T = weights.shape[0], len(budget_options)
+    if (weights.dtype != torch.float64 or utilities.dtype != torch.float64 or not weights.is_cuda
+            or utilities.shape != (R, T) or (fixed_row_equivalent is None) == (row_cost_curve is None)):
+        raise ValueError("device tier allocation needs CUDA fp64 weights [R] and utilities [R, T], and exactly "
+                         "one cost model")
+    weights = weights.contiguous()
+    utilities = utilities.contiguous()
+    opts = np.ascontiguousarray(budget_options, dtype=np.int32)
+    curve = list(row_cost_curve or [])
+    c_rows = np.ascontiguousarray([int(r) for r, _ in curve] or [0], dtype=np.int32)
+    c_cost = np.ascontiguousarray([float(c) for _, c in curve] or [0.0], dtype=np.float64)
+    fixed = math.nan if fixed_row_equivalent is None else float(fixed_row_equivalent)
+    lib = _lib.load()
+    ws_bytes = lib.sg_allocate_tiers_device_workspace_bytes(R, int(row_budget))
+    ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=weights.device)
+    out = torch.empty(R, dtype=torch.int32, device=weights.device)
+    st = lib.sg_allocate_tiers_device(R, weights.data_ptr(), T, opts.ctypes.data, utilities.data_ptr(),
+                                      int(row_budget), fixed, c_rows.ctypes.data, c_cost.ctypes.data, len(curve),
+                                      out.data_ptr(), _lib.ptr(status), ws.data_ptr(), ws_bytes,
+                                      _lib.stream_ptr(stream))
+    if st == _lib.SG_ERR_INVALID_ARGUMENT:
+        raise ValueError(lib.sg_last_error().decode())
+    _lib.check(st, "sg_allocate_tiers_device")
+    return out
+
+
 @dataclass
 class RequestScores:
     """One rank's allocator inputs for its requests."""

@@ -17,6 +17,7 @@
 // pointer (previous row total, option); allocations are rebuilt from back
 // pointers only to break exact ties.
 #include <cmath>
+#include <cstdio>
 #include <vector>
 
 #include "common.cuh"
@@ -67,31 +68,38 @@ void rebuild(const std::vector<std::vector<Cell>>& table, int steps, int rows, s
   }
 }
 
-int validate(const Problem& p) {
+// Checks of the problem's shape and cost model (host data in both entries).
+int validate_shape(const Problem& p, const char* who) {
+  char msg[160];
+  auto bad = [&](const char* what) {
+    std::snprintf(msg, sizeof(msg), "%s: %s", who, what);
+    return fail(SG_ERR_INVALID_ARGUMENT, msg);
+  };
   if (p.R < 1 || p.T < 1 || p.weights == nullptr || p.options == nullptr || p.utilities == nullptr)
-    return fail(SG_ERR_INVALID_ARGUMENT, "sg_allocate_tiers: empty problem");
-  if (p.options[0] < 1) return fail(SG_ERR_INVALID_ARGUMENT, "sg_allocate_tiers: tier options must be >= 1");
+    return bad("empty problem");
+  if (p.options[0] < 1) return bad("tier options must be >= 1");
   for (int k = 1; k < p.T; ++k)
-    if (p.options[k] <= p.options[k - 1])
-      return fail(SG_ERR_INVALID_ARGUMENT, "sg_allocate_tiers: tier options must be strictly increasing");
+    if (p.options[k] <= p.options[k - 1]) return bad("tier options must be strictly increasing");
   if (static_cast<int64_t>(p.budget) < static_cast<int64_t>(p.R) * (p.options[0] + 1))
-    return fail(SG_ERR_INVALID_ARGUMENT, "sg_allocate_tiers: row budget below one smallest tier per request");
+    return bad("row budget below one smallest tier per request");
   const bool has_curve = p.curve_points > 0;
-  if (has_curve == std::isfinite(p.fixed))
-    return fail(SG_ERR_INVALID_ARGUMENT, "sg_allocate_tiers: give either a fixed row equivalent or a cost curve");
-  if (!has_curve && !(p.fixed > 0.0))
-    return fail(SG_ERR_INVALID_ARGUMENT, "sg_allocate_tiers: fixed row equivalent must be positive");
+  if (has_curve == std::isfinite(p.fixed)) return bad("give either a fixed row equivalent or a cost curve");
+  if (!has_curve && !(p.fixed > 0.0)) return bad("fixed row equivalent must be positive");
   if (has_curve) {
-    if (p.curve_rows == nullptr || p.curve_cost == nullptr)
-      return fail(SG_ERR_INVALID_ARGUMENT, "sg_allocate_tiers: null cost curve");
+    if (p.curve_rows == nullptr || p.curve_cost == nullptr) return bad("null cost curve");
     for (int s = 0; s < p.curve_points; ++s) {
       if (p.curve_rows[s] < 1 || !std::isfinite(p.curve_cost[s]) || !(p.curve_cost[s] > 0.0))
-        return fail(SG_ERR_INVALID_ARGUMENT, "sg_allocate_tiers: cost curve points need rows >= 1, cost > 0");
+        return bad("cost curve points need rows >= 1, cost > 0");
       if (s > 0 && (p.curve_rows[s] <= p.curve_rows[s - 1] || p.curve_cost[s] < p.curve_cost[s - 1]))
-        return fail(SG_ERR_INVALID_ARGUMENT, "sg_allocate_tiers: cost curve must be increasing in rows, "
-                                             "non-decreasing in cost");
+        return bad("cost curve must be increasing in rows, non-decreasing in cost");
     }
   }
+  return SG_OK;
+}
+
+int validate(const Problem& p) {
+  int st = validate_shape(p, "sg_allocate_tiers");
+  if (st != SG_OK) return st;
   for (int i = 0; i < p.R; ++i) {
     if (!std::isfinite(p.weights[i]) || p.weights[i] < 0.0)
       return fail(SG_ERR_INVALID_ARGUMENT, "sg_allocate_tiers: weights must be finite and >= 0");
@@ -166,4 +174,321 @@ extern "C" int sg_allocate_tiers(int32_t num_requests, const double* weights, in
   rebuild(table, p.R, best, a);
   for (int i = 0; i < p.R; ++i) allocation[i] = p.options[a[i]];
   return SG_OK;
+}
+
+// ---------------------------------------------------------------------------
+// The same knapsack as one CTA on the device, for weights and utilities that
+// the tree kernels left in device memory (no host round trip per wave).
+//
+// Per request step every reachable row total is one thread's cell.  The host
+// loop visits (previous row total in first-reached order, option) pairs in
+// order and updates a cell with each pair that lands on it; a cell's
+// candidates are therefore processed in the order of their key
+// rank(previous) * T + option, and the next step's first-reached order is
+// the order of each cell's smallest key.  Ranks are rebuilt every step from a
+// bitmap of those keys, so the device visits candidates in exactly the host's
+// order and applies the same fp64 comparisons: allocations are identical.
+// ---------------------------------------------------------------------------
+namespace sg {
+namespace {
+
+constexpr int kAllocThreads = 1024;
+constexpr int kAllocMaxOptions = 8;
+constexpr int kAllocMaxBudget = 8192;
+constexpr int kAllocMaxCurve = 64;
+
+struct DeviceProblem {
+  int R, T, B;
+  int options[kAllocMaxOptions];
+  double fixed;
+  int curve_points;
+  int curve_rows[kAllocMaxCurve];
+  double curve_cost[kAllocMaxCurve];
+  const double* weights;    // device [R]
+  const double* utilities;  // device [R, T]
+  int32_t* allocation;      // device [R]
+  int32_t* status;          // device word (atomicMax of error codes), or null
+  int32_t* links;           // device [(R + 1) * (B + 1)]: previous row total * 8 + option, -1 unreached
+};
+
+__device__ double device_wave_cost(const DeviceProblem& p, int rows) {
+  if (p.curve_points == 0) return p.fixed + static_cast<double>(rows);
+  if (rows <= p.curve_rows[0]) return p.curve_cost[0];
+  for (int s = 0; s + 1 < p.curve_points; ++s) {
+    const int lr = p.curve_rows[s], rr = p.curve_rows[s + 1];
+    if (rows <= rr) {
+      const double fraction = static_cast<double>(rows - lr) / static_cast<double>(rr - lr);
+      const double span = p.curve_cost[s + 1] - p.curve_cost[s];
+      const double step = fraction * span;
+      return p.curve_cost[s] + step;
+    }
+  }
+  return p.curve_cost[p.curve_points - 1];
+}
+
+// Is allocation a (the one ending at row total ra after `steps` requests,
+// then option ka) lexicographically smaller than b (rb, then kb)?  Walks
+// both back-pointer chains together; the last difference seen is the first
+// in request order.
+__device__ bool allocation_less(const DeviceProblem& p, int steps, int ra, int ka, int rb, int kb) {
+  int da = ka, db = kb;
+  bool differ = ka != kb;
+  for (int s = steps; s > 0 && ra != rb; --s) {
+    const int la = p.links[static_cast<size_t>(s) * (p.B + 1) + ra];
+    const int lb = p.links[static_cast<size_t>(s) * (p.B + 1) + rb];
+    if ((la & 7) != (lb & 7)) {
+      da = la & 7;
+      db = lb & 7;
+      differ = true;
+    }
+    ra = la >> 3;
+    rb = lb >> 3;
+  }
+  return differ && da < db;
+}
+
+__device__ __forceinline__ void alloc_report(const DeviceProblem& p, int code) {
+  if (p.status != nullptr) atomicMax(p.status, code);
+}
+
+// Exclusive prefix sum of `count` ints in place (one CTA); returns the total.
+__device__ int block_exclusive_scan(int* v, int count, int* warp_sums) {
+  const int per = (count + kAllocThreads - 1) / kAllocThreads;
+  const int begin = min(count, static_cast<int>(threadIdx.x) * per), end = min(count, begin + per);
+  int local = 0;
+  for (int j = begin; j < end; ++j) local += v[j];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = local;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = warp_sums[lane];
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += t;
+    }
+    warp_sums[lane] = w;  // inclusive
+  }
+  __syncthreads();
+  int run = incl - local + (warp > 0 ? warp_sums[warp - 1] : 0);
+  const int total = warp_sums[31];
+  for (int j = begin; j < end; ++j) {
+    const int t = v[j];
+    v[j] = run;
+    run += t;
+  }
+  __syncthreads();
+  return total;
+}
+
+__global__ void __launch_bounds__(kAllocThreads) allocate_tiers_kernel(const DeviceProblem p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int cells = p.B + 1;
+  double* reward = reinterpret_cast<double*>(smem);           // [2][cells]
+  int* rank = reinterpret_cast<int*>(reward + 2 * cells);     // [2][cells]
+  const int key_words = (cells * p.T + 31) / 32;
+  uint32_t* bits = reinterpret_cast<uint32_t*>(rank + 2 * cells);  // [key_words]
+  int* word_base = reinterpret_cast<int*>(bits + key_words);       // [key_words]
+  __shared__ int warp_sums[32];
+  __shared__ int bad;
+  __shared__ double best_ratio[32];
+  __shared__ int best_rows[32];
+  const int tid = threadIdx.x;
+
+  if (tid == 0) bad = 0;
+  __syncthreads();
+  for (int j = tid; j < p.R * p.T; j += kAllocThreads) {
+    const double u = p.utilities[j];
+    if (!isfinite(u) || u < 1.0) bad = 1;
+  }
+  for (int i = tid; i < p.R; i += kAllocThreads) {
+    const double w = p.weights[i];
+    if (!isfinite(w) || w < 0.0) bad = 1;
+  }
+  for (int c = tid; c < cells; c += kAllocThreads) {
+    rank[c] = c == 0 ? 0 : -1;
+    reward[c] = 0.0;
+    p.links[c] = c == 0 ? -1 : -2;
+  }
+  __syncthreads();
+  if (bad) {
+    alloc_report(p, SG_ERR_INVALID_ARGUMENT);
+    for (int i = tid; i < p.R; i += kAllocThreads) p.allocation[i] = -1;
+    return;
+  }
+  int cur = 0;
+  for (int i = 0; i < p.R; ++i) {
+    const int* rank_prev = rank + cur * cells;
+    int* rank_next = rank + (cur ^ 1) * cells;
+    const double* reward_prev = reward + cur * cells;
+    double* reward_next = reward + (cur ^ 1) * cells;
+    int32_t* links_next = p.links + static_cast<size_t>(i + 1) * cells;
+    double earned[kAllocMaxOptions];
+    for (int k = 0; k < p.T; ++k) earned[k] = p.weights[i] * p.utilities[static_cast<size_t>(i) * p.T + k];
+    for (int j = tid; j < key_words; j += kAllocThreads) bits[j] = 0u;
+    __syncthreads();
+    for (int c = tid; c < cells; c += kAllocThreads) {
+      // candidates (key, previous row total, option), in key order
+      int keys[kAllocMaxOptions], used[kAllocMaxOptions], opt[kAllocMaxOptions];
+      int n = 0;
+      for (int k = 0; k < p.T; ++k) {
+        const int u = c - p.options[k] - 1;
+        if (u < 0 || rank_prev[u] < 0) continue;
+        const int key = rank_prev[u] * p.T + k;
+        int at = n++;
+        while (at > 0 && keys[at - 1] > key) {
+          keys[at] = keys[at - 1];
+          used[at] = used[at - 1];
+          opt[at] = opt[at - 1];
+          --at;
+        }
+        keys[at] = key;
+        used[at] = u;
+        opt[at] = k;
+      }
+      if (n == 0) {
+        rank_next[c] = -1;
+        links_next[c] = -2;
+        continue;
+      }
+      double best = reward_prev[used[0]] + earned[opt[0]];
+      int best_used = used[0], best_opt = opt[0];
+      for (int j = 1; j < n; ++j) {
+        const double r = reward_prev[used[j]] + earned[opt[j]];
+        bool take = r > best + 1e-12;
+        if (!take && fabs(r - best) <= 1e-12) take = allocation_less(p, i, used[j], opt[j], best_used, best_opt);
+        if (take) {
+          best = r;
+          best_used = used[j];
+          best_opt = opt[j];
+        }
+      }
+      reward_next[c] = best;
+      links_next[c] = best_used * 8 + best_opt;
+      rank_next[c] = keys[0];  // first-reached key; turned into a rank below
+      atomicOr(&bits[keys[0] >> 5], 1u << (keys[0] & 31));
+    }
+    __syncthreads();
+    for (int j = tid; j < key_words; j += kAllocThreads) word_base[j] = __popc(bits[j]);
+    __syncthreads();
+    const int reached = block_exclusive_scan(word_base, key_words, warp_sums);
+    if (reached == 0) {
+      alloc_report(p, SG_ERR_CAPACITY);
+      for (int r = tid; r < p.R; r += kAllocThreads) p.allocation[r] = -1;
+      return;
+    }
+    for (int c = tid; c < cells; c += kAllocThreads) {
+      const int key = rank_next[c];
+      if (key >= 0)
+        rank_next[c] = word_base[key >> 5] + __popc(bits[key >> 5] & ((1u << (key & 31)) - 1u));
+    }
+    __syncthreads();
+    cur ^= 1;
+  }
+  // largest reward / cost, ties to fewer rows
+  const int* rank_last = rank + cur * cells;
+  const double* reward_last = reward + cur * cells;
+  double my_ratio = 0.0;
+  int my_rows = -1;
+  for (int c = tid; c < cells; c += kAllocThreads) {
+    if (rank_last[c] < 0) continue;
+    const double ratio = reward_last[c] / device_wave_cost(p, c);
+    if (my_rows < 0 || ratio > my_ratio || (ratio == my_ratio && c < my_rows)) {
+      my_ratio = ratio;
+      my_rows = c;
+    }
+  }
+  const int lane = tid & 31, warp = tid >> 5;
+  for (int o = 16; o > 0; o >>= 1) {
+    const double r = __shfl_down_sync(0xffffffffu, my_ratio, o);
+    const int c = __shfl_down_sync(0xffffffffu, my_rows, o);
+    if (c >= 0 && (my_rows < 0 || r > my_ratio || (r == my_ratio && c < my_rows))) {
+      my_ratio = r;
+      my_rows = c;
+    }
+  }
+  if (lane == 0) {
+    best_ratio[warp] = my_ratio;
+    best_rows[warp] = my_rows;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double r = best_ratio[0];
+    int rows = best_rows[0];
+    for (int w = 1; w < kAllocThreads / 32; ++w) {
+      const int c = best_rows[w];
+      if (c >= 0 && (rows < 0 || best_ratio[w] > r || (best_ratio[w] == r && c < rows))) {
+        r = best_ratio[w];
+        rows = c;
+      }
+    }
+    for (int s = p.R; s > 0; --s) {
+      const int link = p.links[static_cast<size_t>(s) * cells + rows];
+      p.allocation[s - 1] = p.options[link & 7];
+      rows = link >> 3;
+    }
+  }
+}
+
+size_t allocate_smem_bytes(int T, int B) {
+  const size_t cells = static_cast<size_t>(B) + 1;
+  const size_t key_words = (cells * T + 31) / 32;
+  return cells * 2 * sizeof(double) + cells * 2 * sizeof(int) + key_words * 8;
+}
+
+}  // namespace
+}  // namespace sg
+
+extern "C" size_t sg_allocate_tiers_device_workspace_bytes(int32_t num_requests, int32_t row_budget) {
+  if (num_requests < 1 || row_budget < 0) return 0;
+  return static_cast<size_t>(num_requests + 1) * (static_cast<size_t>(row_budget) + 1) * sizeof(int32_t);
+}
+
+extern "C" int sg_allocate_tiers_device(int32_t num_requests, const double* weights, int32_t num_options,
+                                        const int32_t* options, const double* utilities, int32_t row_budget,
+                                        double fixed_row_equivalent, const int32_t* curve_rows,
+                                        const double* curve_cost, int32_t curve_points, int32_t* allocation,
+                                        int32_t* status, void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace sg;
+  if (allocation == nullptr || curve_points < 0)
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_allocate_tiers_device: bad output");
+  Problem hp{num_requests, num_options, row_budget, weights, options, utilities, fixed_row_equivalent,
+             curve_rows, curve_cost, curve_points};
+  int st = validate_shape(hp, "sg_allocate_tiers_device");
+  if (st != SG_OK) return st;
+  if (num_options > kAllocMaxOptions || row_budget > kAllocMaxBudget || curve_points > kAllocMaxCurve)
+    return fail(SG_ERR_UNSUPPORTED, "sg_allocate_tiers_device: at most 8 options, 8192 rows, 64 curve points");
+  const size_t need = sg_allocate_tiers_device_workspace_bytes(num_requests, row_budget);
+  if (workspace == nullptr || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 3u) != 0) {
+    set_error("sg_allocate_tiers_device: workspace of %zu bytes, %zu needed (4-byte aligned)", workspace_bytes, need);
+    return SG_ERR_WORKSPACE;
+  }
+  if ((reinterpret_cast<uintptr_t>(weights) & 7u) != 0 || (reinterpret_cast<uintptr_t>(utilities) & 7u) != 0 ||
+      (reinterpret_cast<uintptr_t>(allocation) & 3u) != 0 || (reinterpret_cast<uintptr_t>(status) & 3u) != 0)
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_allocate_tiers_device: misaligned pointer");
+  DeviceProblem p = {};
+  p.R = num_requests;
+  p.T = num_options;
+  p.B = row_budget;
+  for (int k = 0; k < num_options; ++k) p.options[k] = options[k];
+  p.fixed = fixed_row_equivalent;
+  p.curve_points = curve_points;
+  for (int s = 0; s < curve_points; ++s) {
+    p.curve_rows[s] = curve_rows[s];
+    p.curve_cost[s] = curve_cost[s];
+  }
+  p.weights = weights;
+  p.utilities = utilities;
+  p.allocation = allocation;
+  p.status = status;
+  p.links = static_cast<int32_t*>(workspace);
+  const size_t smem = allocate_smem_bytes(num_options, row_budget);
+  SG_CUDA_CHECK(cudaFuncSetAttribute(allocate_tiers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem)));
+  allocate_tiers_kernel<<<1, kAllocThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_launch("allocate_tiers_kernel");
 }

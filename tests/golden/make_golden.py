@@ -25,6 +25,11 @@ functions (no restatement):
                      (:706-795) on random problems (linear and measured-curve
                      cost models) and _draft_tree_expected_tokens (:560-568) on
                      probability_tree (tree.py:148-212) outputs.
+  draft_trees.npz    tree.probability_tree (tree.py:148-212) on softmax
+                     proposals (sampling.probabilities, sampling.py:29-36) of
+                     random fp32 logits: the top-k log masses it ranks, the
+                     tree, and _prefix_tree / _draft_tree_expected_tokens
+                     (continuous_tree_block_decode.py:560-586) per tier.
 
 The fixtures are small (tens of KB) and deterministic (seeded torch CPU RNG).
 """
@@ -325,6 +330,73 @@ def build_allocator(ref, gen):
     (OUT / "allocator.json").write_text(json.dumps({"problems": problems, "trees": trees}))
 
 
+def draft_tree_logits(seed: int, L: int, V: int, kind: str) -> torch.Tensor:
+    """The fp32 proposal logits of one draft-tree case (regenerated by the
+    tests from the stored seed; the fixture keeps a checksum)."""
+    logits = torch.randn((L, V), generator=torch.Generator().manual_seed(seed), dtype=torch.float32) * 3.0
+    if kind == "spine":
+        logits[:, 0] += 30.0
+    elif kind == "repeat":  # identical rows: exact ties between heap scores
+        logits[:] = logits[0]
+    return logits
+
+
+def build_draft_trees(ref, gen):
+    """Cases: (length, vocab, budget, temperature, reward schedule, rank caps,
+    adaptive (min budget, threshold), tiers, kind)."""
+    tree_mod, decode, sampling = ref.tree, ref.decode, ref.sampling
+    specs = [
+        (15, 4096, 60, 1.0, None, None, None, (16, 32, 60), "randn"),
+        (15, 4096, 128, 0.7, None, None, None, (16, 32, 64, 128), "randn"),
+        (15, 2048, 48, 1.0, (0.3,) * 15, None, None, (8, 48), "randn"),
+        (6, 1024, 40, 1.5, (0.5, 0.25, 0.0, -0.25, 0.1, 0.2), None, None, (10, 40), "randn"),
+        (15, 2048, 64, 1.0, None, (4,) * 15, None, (16, 64), "randn"),
+        (8, 512, 64, 1.0, None, (1, 2, 3, 4, 5, 6, 7, 8), None, (20,), "randn"),
+        (15, 2048, 64, 1.0, None, None, (16, 0.3), (16,), "spine"),
+        (15, 2048, 64, 1.0, None, None, (16, 0.9), (16, 64), "randn"),
+        (2, 8, 100, 1.0, None, None, None, (30, 72), "randn"),
+        (5, 256, 40, 1.0, None, None, None, (12, 40), "repeat"),
+        (15, 151936, 32, 1.0, None, None, None, (16, 32), "randn"),
+    ]
+    arrays = {"count": np.int64(len(specs))}
+    base_seed = int(torch.randint(0, 2**31 - 1, (1,), generator=gen))
+    for i, (L, V, budget, T, sched, caps, adaptive, tiers, kind) in enumerate(specs):
+        seed = base_seed + i
+        logits = draft_tree_logits(seed, L, V, kind)
+        q = sampling.probabilities(logits.to(torch.float64), T, torch.float64)
+        K = min(budget, V)
+        values, indices = torch.topk(q, K, dim=-1, sorted=True)
+        kwargs = {}
+        if sched is not None:
+            kwargs["depth_reward_schedule"] = sched
+        if caps is not None:
+            kwargs["rank_caps"] = caps
+        if adaptive is not None:
+            kwargs["adaptive_min_budget"], kwargs["confidence_threshold"] = adaptive
+        t = tree_mod.probability_tree(q, budget, **kwargs)
+        nodes = len(t.tokens)
+        util = [decode._draft_tree_expected_tokens(decode._prefix_tree(t, b)) if b <= nodes else np.nan
+                for b in tiers]
+        pre = f"c{i}_"
+        arrays[pre + "seed"] = np.int64(seed)
+        arrays[pre + "kind"] = np.array(kind)
+        arrays[pre + "logit_checksum"] = np.array([logits.double().sum().item(), logits.double().abs().max().item()])
+        arrays[pre + "meta"] = np.array([L, V, budget, K, -1 if adaptive is None else adaptive[0]], np.int64)
+        arrays[pre + "temperature"] = np.float64(T)
+        arrays[pre + "threshold"] = np.float64(np.nan if adaptive is None else adaptive[1])
+        arrays[pre + "rewards"] = np.array(sched if sched is not None else [], np.float64)
+        arrays[pre + "caps"] = np.array(caps if caps is not None else [], np.int64)
+        arrays[pre + "logs"] = values.log().numpy()
+        arrays[pre + "ids"] = indices.numpy().astype(np.int64)
+        arrays[pre + "tokens"] = np.array(t.tokens, np.int64)
+        arrays[pre + "parents"] = np.array(t.parents, np.int64)
+        arrays[pre + "depths"] = np.array(t.depths, np.int64)
+        arrays[pre + "masses"] = np.array(t.draft_prefix_log_masses, np.float64)
+        arrays[pre + "tiers"] = np.array(tiers, np.int64)
+        arrays[pre + "utilities"] = np.array(util, np.float64)
+    np.savez_compressed(OUT / "draft_trees.npz", **arrays)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the specgrove checkout")
@@ -349,6 +421,7 @@ def main():
     for i, c in enumerate(logits_cases):
         arrays[f"temperature_{i}"] = np.float64(c["temperature"])
     np.savez_compressed(OUT / "accept_logits.npz", **arrays)
+    build_draft_trees(ref, torch.Generator().manual_seed(20261203))
     for p in sorted(OUT.glob("*.*")):
         print(p.name, p.stat().st_size)
 

@@ -5,6 +5,7 @@ reference's functions directly.  Both oracle arithmetics must reproduce them:
 the exact 64.64 fixed-point sums the CUDA kernels use, and the sequential fp64
 running sum of the reference CPU rule.
 """
+import math
 from fractions import Fraction
 
 import numpy as np
@@ -230,3 +231,24 @@ def test_allocator_matches_reference(golden_dir):
         assert list(alloc) == p["allocation"]
     for t in z["trees"]:
         assert draft_tree_expected_tokens(t["masses"]) == pytest.approx(t["expected"], rel=1e-12)
+
+
+def test_draft_tree_oracle_matches_reference():
+    """oracle/draft_tree.py against probability_tree, _prefix_tree and
+    _draft_tree_expected_tokens run on the same proposals."""
+    from draft_tree_cases import load_cases
+    from oracle.draft_tree import best_first_tree, proposal_logs, tier_utility
+    for c in load_cases():
+        logs, ids = proposal_logs(c["logits"], c["temperature"], c["K"])
+        assert np.array_equal(ids, c["ids"])
+        assert np.max(np.abs(logs - c["logs"])) < 1e-12
+        # the tree is a pure function of the ranked log masses: exact
+        t = best_first_tree(c["logs"], c["ids"], c["budget"], c["rewards"], c["caps"], c["adaptive_min"],
+                            c["threshold"])
+        assert t.tokens == c["tokens"].tolist()
+        assert t.parents == c["parents"].tolist()
+        assert t.depths == c["depths"].tolist()
+        assert t.masses == c["masses"].tolist()
+        for b, u in zip(c["tiers"], c["utilities"]):
+            got = tier_utility(t, int(b))
+            assert (math.isnan(got) and math.isnan(u)) or got == u
