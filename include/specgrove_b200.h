@@ -230,17 +230,19 @@ SG_API int sg_allocate_tiers_device(int32_t num_requests, const double* weights,
 /*
  * Draft-tree construction on the device (the proposal step before a wave).
  *
- * sg_proposal_topk: per row of drafter logits [rows, row_stride] (bf16 or
- * fp32; a row = one (request, draft depth)), the k largest proposal masses
+ * sg_proposal_topk: per row of drafter logits (bf16 or fp32; a row = one
+ * (request, draft depth); row r is element offset (r / rows_per_group) *
+ * group_stride + (r % rows_per_group) * row_stride, e.g. block rows 1..L of
+ * [R, block, vocab] logits), the k largest proposal masses
  * of q = softmax(logits / T) in fp64 and their token ids, sorted by mass
  * (ties to the lower token id): log_q[rows, k] fp64, ids[rows, k] int64.
  * Replaces probabilities(logits, T, float64) + torch.topk(q, k) + log
  * (sampling.py:29-36, tree.py:183-184).  1 <= k <= min(1024, vocab), T > 0.
  * Non-finite logits set SG_ERR_PROBABILITY in *status.
  */
-SG_API int sg_proposal_topk(const void* logits, int32_t dtype, int64_t row_stride, int32_t rows, int32_t vocab,
-                            int32_t k, double temperature, double* log_q, int64_t* ids, int32_t* status,
-                            void* stream);
+SG_API int sg_proposal_topk(const void* logits, int32_t dtype, int64_t row_stride, int32_t rows_per_group,
+                            int64_t group_stride, int32_t rows, int32_t vocab, int32_t k, double temperature,
+                            double* log_q, int64_t* ids, int32_t* status, void* stream);
 
 /*
  * sg_build_draft_trees: the best-first prefix tree of every request
@@ -434,6 +436,61 @@ SG_API size_t sg_engine_workspace_bytes(void* engine);
  * (pack, target, select_commit stages).
  */
 SG_API int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stream);
+
+/* ------------------------------------------------------------------------
+ * The drafter step (DFlash block drafter, the step before each wave).
+ * ------------------------------------------------------------------------
+ * The drafter (third_party/ddtree_official/model/dflash.py:147-200) is a
+ * Qwen3 layer stack whose block rows (the request's last token, then
+ * block_size - 1 mask tokens, embedded with the TARGET's embedding) attend
+ * bidirectionally to each other and to the request's draft cache: the K/V
+ * of every context row, projected from the target features of the rows
+ * committed so far (fc, then hidden_norm; k_norm and RoPE on the keys).
+ * The model descriptor is an sg_model_desc of the drafter's layers with
+ * embed and lm_head pointing at the target's and final_norm the drafter's
+ * norm; the draft cache is an sg_arena_desc of the drafter's layers. */
+typedef struct {
+  const void* fc;              /* [hidden, num_feature_layers * hidden] bf16 */
+  const void* hidden_norm;     /* [hidden] bf16 */
+  int32_t num_feature_layers;  /* target layers concatenated per context row */
+  int32_t block_size;          /* rows per request block (16), <= 256 */
+  int64_t mask_token_id;       /* token of block rows 1 .. block_size - 1 */
+  int32_t max_update_rows;     /* largest number of context rows per call */
+} sg_draft_desc;
+
+/* One drafter step over R requests (the packed form of _propose_many with
+ * reuse_request_draft_cache, continuous_tree_block_decode.py:889-962). */
+typedef struct {
+  int32_t num_requests;
+  int32_t num_update_rows;        /* U = update_offsets[R] (host copy) */
+  const int64_t* slots;           /* [R] draft-cache slot */
+  const int64_t* cache_lengths;   /* [R] context rows already in the draft cache */
+  const int64_t* update_offsets;  /* [R + 1] rows of `features` per request */
+  const void* features;           /* bf16 [U, num_feature_layers * hidden], 16-byte
+                                     aligned (sg_wave_desc.features_kept of the
+                                     previous wave) */
+  const int64_t* anchor_tokens;   /* [R] last generated token (block row 0) */
+  void* logits_out;               /* bf16 [R, block_size, vocab]: the drafter's
+                                     logits of every block row (row 0, the
+                                     anchor's, is not a proposal) */
+  int64_t* lengths_out;           /* [R] cache_lengths + update rows */
+  int32_t* status;                /* optional device status word */
+} sg_draft_wave;
+
+/* Builds the drafter engine: TMA descriptors for the drafter's weights and
+ * the fc, and a workspace for max_requests * block_size block rows and
+ * max_update_rows context rows (cudaMalloc, freed by sg_engine_destroy). */
+SG_API int sg_draft_engine_create(const sg_model_desc* model, const sg_draft_desc* draft,
+                                  const sg_arena_desc* arena, int32_t max_requests, void** engine_out);
+
+/* One drafter step, enqueued on `stream` with no host synchronisation: the
+ * context rows' K/V (fc + hidden_norm, then every layer's k/v projection,
+ * k_norm, RoPE at positions cache_len ..) appended to the draft cache
+ * (committed: lengths_out), the block rows' forward with bidirectional
+ * attention over [cache, update, block], the drafter's final norm and the
+ * target's LM head into logits_out.  The block rows' own K/V live past the
+ * committed length only for this call (the reference crops them). */
+SG_API int sg_draft_pass(void* engine, const sg_draft_wave* wave, void* stream);
 
 /*
  * Final RMSNorm + LM head fused with softmax and sampling over caller-given

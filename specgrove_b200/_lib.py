@@ -60,7 +60,8 @@ _SIGNATURES = {
         c_int32, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_double, c_void_p, c_void_p, c_int32,
         c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_void_p]),
     "sg_proposal_topk": (ctypes.c_int, [
-        c_void_p, c_int32, c_int64, c_int32, c_int32, c_int32, c_double, c_void_p, c_void_p, c_void_p, c_void_p]),
+        c_void_p, c_int32, c_int64, c_int32, c_int64, c_int32, c_int32, c_int32, c_double, c_void_p, c_void_p,
+        c_void_p, c_void_p]),
     "sg_build_draft_trees": (ctypes.c_int, [
         c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_double,
         c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
@@ -122,7 +123,8 @@ def check(status: int, where: str) -> None:
 
 # Entry points taking struct descriptors; bound with their ctypes structures
 # in specgrove_b200.engine.
-STRUCT_SYMBOLS = ["sg_engine_create", "sg_engine_destroy", "sg_engine_workspace_bytes", "sg_verify_pass"]
+STRUCT_SYMBOLS = ["sg_engine_create", "sg_engine_destroy", "sg_engine_workspace_bytes", "sg_verify_pass",
+                  "sg_draft_engine_create", "sg_draft_pass"]
 
 
 def exported_symbols() -> list[str]:

@@ -113,7 +113,8 @@ __device__ int select_digit(const uint32_t* hist, int& need, int* scratch) {
 
 template <typename T>
 __global__ void __launch_bounds__(kTopkThreads) proposal_topk_kernel(const T* __restrict__ logits,
-                                                                     int64_t row_stride, int vocab, int k,
+                                                                     int64_t row_stride, int rows_per_group,
+                                                                     int64_t group_stride, int vocab, int k,
                                                                      double inv_t, double* __restrict__ log_q,
                                                                      int64_t* __restrict__ ids,
                                                                      int32_t* status) {
@@ -129,7 +130,9 @@ __global__ void __launch_bounds__(kTopkThreads) proposal_topk_kernel(const T* __
   __shared__ int eq_base;
   __shared__ int warp_eq[kTopkThreads / 32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const T* x = logits + static_cast<int64_t>(blockIdx.x) * row_stride;
+  const int group = static_cast<int>(blockIdx.x) / rows_per_group;
+  const int in_group = static_cast<int>(blockIdx.x) - group * rows_per_group;
+  const T* x = logits + static_cast<int64_t>(group) * group_stride + static_cast<int64_t>(in_group) * row_stride;
   double* out_q = log_q + static_cast<int64_t>(blockIdx.x) * k;
   int64_t* out_id = ids + static_cast<int64_t>(blockIdx.x) * k;
 
@@ -478,15 +481,17 @@ bool aligned_to(const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr
 }  // namespace
 }  // namespace sg
 
-extern "C" int sg_proposal_topk(const void* logits, int32_t dtype, int64_t row_stride, int32_t rows, int32_t vocab,
-                                int32_t k, double temperature, double* log_q, int64_t* ids, int32_t* status,
-                                void* stream) {
+extern "C" int sg_proposal_topk(const void* logits, int32_t dtype, int64_t row_stride, int32_t rows_per_group,
+                                int64_t group_stride, int32_t rows, int32_t vocab, int32_t k, double temperature,
+                                double* log_q, int64_t* ids, int32_t* status, void* stream) {
   using namespace sg;
   if (rows == 0) return SG_OK;
   if (logits == nullptr || log_q == nullptr || ids == nullptr)
     return fail(SG_ERR_INVALID_ARGUMENT, "sg_proposal_topk: null pointer");
-  if (rows < 0 || vocab < 1 || k < 1 || k > kTopkMax || k > vocab || row_stride < vocab)
-    return fail(SG_ERR_INVALID_ARGUMENT, "sg_proposal_topk: bad sizes (1 <= k <= min(1024, vocab))");
+  if (rows < 0 || vocab < 1 || k < 1 || k > kTopkMax || k > vocab || row_stride < vocab || rows_per_group < 1 ||
+      rows % rows_per_group != 0 || (rows > rows_per_group && group_stride < row_stride * rows_per_group))
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_proposal_topk: bad sizes (1 <= k <= min(1024, vocab), rows a "
+                                         "multiple of rows_per_group, groups not overlapping)");
   if (!(temperature > 0.0) || !std::isfinite(temperature))
     return fail(SG_ERR_INVALID_ARGUMENT, "sg_proposal_topk: temperature must be finite and > 0");
   if (dtype != SG_DTYPE_BF16 && dtype != SG_DTYPE_F32)
@@ -498,10 +503,12 @@ extern "C" int sg_proposal_topk(const void* logits, int32_t dtype, int64_t row_s
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == SG_DTYPE_BF16) {
     proposal_topk_kernel<__nv_bfloat16><<<rows, kTopkThreads, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(logits), row_stride, vocab, k, inv_t, log_q, ids, status);
+        static_cast<const __nv_bfloat16*>(logits), row_stride, rows_per_group, group_stride, vocab, k, inv_t, log_q,
+        ids, status);
   } else {
-    proposal_topk_kernel<float><<<rows, kTopkThreads, 0, s>>>(static_cast<const float*>(logits), row_stride, vocab,
-                                                              k, inv_t, log_q, ids, status);
+    proposal_topk_kernel<float><<<rows, kTopkThreads, 0, s>>>(static_cast<const float*>(logits), row_stride,
+                                                              rows_per_group, group_stride, vocab, k, inv_t, log_q,
+                                                              ids, status);
   }
   return check_launch("proposal_topk_kernel");
 }

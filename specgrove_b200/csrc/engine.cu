@@ -60,7 +60,31 @@ struct Engine {
   // their k-blocks are spread over up to twice as many CTAs.
   gemm::SplitWorkspace split = {nullptr, nullptr, 0};
   int sms = 0;
+  std::unique_ptr<struct DraftState> draft;  // set for a drafter engine
+  ~Engine();
 };
+
+// The drafter's extra weights and per-call buffers (sg_draft_engine_create).
+struct DraftState {
+  sg_draft_desc desc;
+  CUtensorMap fc_map;                 // B operand: fc [hidden, F * hidden]
+  CUtensorMap th_map;                 // A operand: normed context rows [max_update, hidden]
+  std::vector<CUtensorMap> kv_maps;   // B operand per layer: the k|v rows of the fused q|k|v weight
+  void* buffer = nullptr;
+  float* th32;                        // [max_update, hidden] fc output
+  __nv_bfloat16* th;                  // [max_update, hidden] hidden_norm(fc(features))
+  layers::RowMeta ctx_meta;           // context rows: position, tree, local, rope, arena_row
+  int64_t* block_offsets;             // [max_requests + 1]
+  int64_t* prefix;                    // [max_requests] cache rows + update rows
+  int64_t* block_tokens;              // [max_requests * block]
+  ~DraftState() {
+    if (buffer != nullptr) cudaFree(buffer);
+  }
+};
+
+Engine::~Engine() {
+  if (workspace != nullptr) cudaFree(workspace);
+}
 
 template <typename T>
 T* carve(uint8_t*& cursor, size_t count) {
@@ -155,17 +179,19 @@ int check_model(const sg_model_desc& m) {
 
 using sg::Engine;
 
-extern "C" int sg_engine_create(const sg_model_desc* model, const sg_arena_desc* arena, int32_t max_rows,
-                                int32_t max_requests, void** engine_out) {
-  using namespace sg;
-  if (model == nullptr || arena == nullptr || engine_out == nullptr)
+namespace sg {
+namespace {
+
+// Builds an engine (weights' tensor maps, workspace) for `model` over `arena`.
+int create_engine(const sg_model_desc* model, const sg_arena_desc* arena, int32_t max_rows, int32_t max_requests,
+                  std::unique_ptr<Engine>& e) {
+  if (model == nullptr || arena == nullptr)
     return fail(SG_ERR_INVALID_ARGUMENT, "sg_engine_create: null argument");
-  *engine_out = nullptr;
   int st = check_model(*model);
   if (st != SG_OK) return st;
   if (max_rows < 1 || max_requests < 1 || arena->storage == nullptr || arena->num_slots < 1 || arena->capacity < 1)
     return fail(SG_ERR_INVALID_ARGUMENT, "sg_engine_create: bad sizes");
-  std::unique_ptr<Engine> e(new Engine());
+  e.reset(new Engine());
   e->model = *model;
   e->layer_ptrs.assign(model->layers, model->layers + static_cast<size_t>(model->num_layers) * W_COUNT);
   e->model.layers = e->layer_ptrs.data();
@@ -232,33 +258,254 @@ extern "C" int sg_engine_create(const sg_model_desc* model, const sg_arena_desc*
   e->split.partial_tiles = gemm::split_partial_tiles(e->sms);
   e->split.partials = carve<float>(cur, e->split.partial_tiles * gemm::BM * gemm::BN);
   e->split.flags = carve<int>(cur, e->split.partial_tiles);
-  if (static_cast<size_t>(cur - static_cast<uint8_t*>(e->workspace)) > e->workspace_bytes) {
-    cudaFree(e->workspace);
+  if (static_cast<size_t>(cur - static_cast<uint8_t*>(e->workspace)) > e->workspace_bytes)
     return fail(SG_ERR_WORKSPACE, "sg_engine_create: workspace layout overflow");
-  }
   // Split flags start at zero; every split GEMM leaves them at zero.
-  if (cudaMemset(e->split.flags, 0, e->split.partial_tiles * sizeof(int)) != cudaSuccess) {
-    cudaFree(e->workspace);
+  if (cudaMemset(e->split.flags, 0, e->split.partial_tiles * sizeof(int)) != cudaSuccess)
     return fail(SG_ERR_CUDA, "sg_engine_create: cudaMemset of the split flags failed");
-  }
   if ((st = make_tmap_2d_bf16(&e->xn_map, e->xn, H, max_rows, H * 2, gemm::BK, gemm::BM)) != SG_OK) return st;
   if ((st = make_tmap_2d_bf16(&e->attn_map, e->attn, qw, max_rows, qw * 2, gemm::BK, gemm::BM)) != SG_OK) return st;
   if ((st = make_tmap_2d_bf16(&e->h_map, e->h, I, max_rows, I * 2, gemm::BK, gemm::BM)) != SG_OK) return st;
+  return SG_OK;
+}
+
+}  // namespace
+}  // namespace sg
+
+extern "C" int sg_engine_create(const sg_model_desc* model, const sg_arena_desc* arena, int32_t max_rows,
+                                int32_t max_requests, void** engine_out) {
+  using namespace sg;
+  if (engine_out == nullptr) return fail(SG_ERR_INVALID_ARGUMENT, "sg_engine_create: null argument");
+  *engine_out = nullptr;
+  std::unique_ptr<Engine> e;
+  const int st = create_engine(model, arena, max_rows, max_requests, e);
+  if (st != SG_OK) return st;
   *engine_out = e.release();
   return SG_OK;
 }
 
 extern "C" int sg_engine_destroy(void* engine) {
   if (engine == nullptr) return SG_OK;
-  Engine* e = static_cast<Engine*>(engine);
-  if (e->workspace != nullptr) cudaFree(e->workspace);
-  delete e;
+  delete static_cast<Engine*>(engine);
   return SG_OK;
 }
 
 extern "C" size_t sg_engine_workspace_bytes(void* engine) {
   return engine == nullptr ? 0 : static_cast<Engine*>(engine)->workspace_bytes;
 }
+
+namespace sg {
+namespace {
+
+// Per-call inputs of the decoder layer stack, shared by the verify pass and
+// the drafter step.  Request r owns packed rows row_offsets[r] ..
+// row_offsets[r + 1] - 1, after cache_len[r] rows of its arena slot; e->x
+// holds the embedded rows and e->meta their per-row metadata.
+struct StackArgs {
+  int R = 0, Q = 0;
+  const int64_t* row_offsets = nullptr;
+  const int64_t* slots = nullptr;
+  const int64_t* cache_len = nullptr;
+  int max_rows_per_request = 0;
+  int32_t* status = nullptr;
+  const sg_wave_desc* wave = nullptr;  // trace events (verify pass)
+  // drafter features (verify pass): layer l's residual stream into column
+  // block feature_slot[l] of features_out
+  const int* feature_slot = nullptr;
+  int nfeat = 0;
+  void* features_out = nullptr;
+  // drafter context rows: their K/V are projected from draft->th into the
+  // arena at draft->ctx_meta.arena_row in every layer, before its attention
+  const DraftState* draft = nullptr;
+  int ctx_rows = 0;
+};
+
+inline void trace_at(const StackArgs& a, int point, cudaStream_t stream) {
+  if (a.wave != nullptr) trace(*a.wave, point, stream);
+}
+
+int run_stack(Engine* e, const StackArgs& a, cudaStream_t stream) {
+  const sg_model_desc& m = e->model;
+  const int H = m.hidden, D = m.head_dim, I = m.intermediate;
+  const int nq = m.num_q_heads, nkv = m.num_kv_heads;
+  const int qkv_n = (nq + 2 * nkv) * D;
+  const int qw = nq * D;
+  const int Q = a.Q;
+  const int64_t plane_rows = e->arena.num_slots * e->arena.capacity;
+  const int64_t plane_stride = plane_rows * D;  // elements between kv heads
+  __nv_bfloat16* arena = static_cast<__nv_bfloat16*>(e->arena.storage);
+  const bool nf = norm_fused();
+  const int P = e->ss_parts;
+  const float inv_h = 1.0f / static_cast<float>(H);
+  int st;
+  if (nf && (st = layers::launch_norm_fold(e->x, static_cast<const __nv_bfloat16*>(e->layer_ptrs[W_IN_NORM]), H, Q,
+                                           e->xn, e->ssq, stream)) != SG_OK)
+    return st;
+  if ((st = layers::launch_attention_work(a.row_offsets, a.cache_len, a.R, nq / nkv, nkv, e->work, m.num_layers,
+                                         stream)) != SG_OK)
+    return st;
+  trace_at(a, 1, stream);
+  const gemm::Shape s_qkv = gemm::make_shape(Q, qkv_n, H);
+  const gemm::Shape s_o = gemm::make_shape(Q, H, qw);
+  const gemm::Shape s_gu = gemm::make_shape(Q, 2 * I, H);
+  const gemm::Shape s_down = gemm::make_shape(Q, H, I);
+  const gemm::Shape s_ctx = gemm::make_shape(a.ctx_rows, 2 * nkv * D, H);
+  // Shapes with at most half a wave of tiles (few packed rows) give each
+  // tile's k-blocks to two CTAs; everything else runs whole tiles, which
+  // measured faster (a tile split across CTA runs makes its owner wait).
+  auto small_wave = [&](const gemm::Shape& sh) -> const gemm::SplitWorkspace* {
+    return 2 * sh.tiles <= e->sms ? &e->split : nullptr;
+  };
+  for (int l = 0; l < m.num_layers; ++l) {
+    const void* const* lw = &e->layer_ptrs[static_cast<size_t>(l) * W_COUNT];
+    const LayerMaps& lm = e->maps[l];
+    __nv_bfloat16* k_plane0 = arena + static_cast<int64_t>(l) * 2 * nkv * plane_stride;
+    __nv_bfloat16* v_plane0 = k_plane0 + static_cast<int64_t>(nkv) * plane_stride;
+
+    if (a.draft != nullptr && a.ctx_rows > 0) {
+      // drafter context rows: k|v projection of hidden_norm(fc(features))
+      // with k_norm and RoPE, written at the rows' arena positions (no q)
+      const DraftState& d = *a.draft;
+      const auto* kn = static_cast<const __nv_bfloat16*>(lw[W_K_NORM]);
+      if (D == 128) {
+        gemm::EpiQkvPost<128>::Params pc{nullptr, 0, k_plane0, v_plane0, plane_stride, d.ctx_meta.arena_row,
+                                         d.ctx_meta.rope, kn, kn, 0, nkv, m.rms_eps, a.status, gemm::RowNorm{}};
+        st = gemm::launch<gemm::EpiQkvPost<128>>(d.th_map, d.kv_maps[l], s_ctx, pc, stream, small_wave(s_ctx));
+      } else {
+        gemm::EpiQkvPost<64>::Params pc{nullptr, 0, k_plane0, v_plane0, plane_stride, d.ctx_meta.arena_row,
+                                        d.ctx_meta.rope, kn, kn, 0, nkv, m.rms_eps, a.status, gemm::RowNorm{}};
+        st = gemm::launch<gemm::EpiQkvPost<64>>(d.th_map, d.kv_maps[l], s_ctx, pc, stream, small_wave(s_ctx));
+      }
+      if (st != SG_OK) return st;
+    }
+    if (!nf && (st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(lw[W_IN_NORM]), H, Q, m.rms_eps,
+                                            e->xn, stream)) != SG_OK)
+      return st;
+    if (l == 0) trace_at(a, 2, stream);
+    // input RMSNorm's row scale: sums from the fold kernel (layer 0, one part)
+    // or from the previous down projection's tiles
+    const gemm::RowNorm rn_in = nf ? gemm::RowNorm{e->ssq, l == 0 ? 1 : P, inv_h, m.rms_eps} : gemm::RowNorm{};
+    if (qkv_fused()) {
+      // q/k/v projection with q/k RMSNorm, RoPE and the KV-tail write in its epilogue
+      if (D == 128) {
+        gemm::EpiQkvPost<128>::Params pf{e->q, qw, k_plane0, v_plane0, plane_stride, e->meta.arena_row,
+                                         e->meta.rope, static_cast<const __nv_bfloat16*>(lw[W_Q_NORM]),
+                                         static_cast<const __nv_bfloat16*>(lw[W_K_NORM]), nq, nkv, m.rms_eps,
+                                         a.status, rn_in};
+        st = gemm::launch<gemm::EpiQkvPost<128>>(e->xn_map, lm.qkv, s_qkv, pf, stream, small_wave(s_qkv));
+      } else {
+        gemm::EpiQkvPost<64>::Params pf{e->q, qw, k_plane0, v_plane0, plane_stride, e->meta.arena_row,
+                                        e->meta.rope, static_cast<const __nv_bfloat16*>(lw[W_Q_NORM]),
+                                        static_cast<const __nv_bfloat16*>(lw[W_K_NORM]), nq, nkv, m.rms_eps,
+                                        a.status, rn_in};
+        st = gemm::launch<gemm::EpiQkvPost<64>>(e->xn_map, lm.qkv, s_qkv, pf, stream, small_wave(s_qkv));
+      }
+      if (st != SG_OK) return st;
+      if (l == 0) {
+        trace_at(a, 3, stream);
+        trace_at(a, 4, stream);
+      }
+    } else {
+      gemm::EpiStoreBf16::Params pq{e->qkv, qkv_n, a.status};
+      if ((st = gemm::launch<gemm::EpiStoreBf16>(e->xn_map, lm.qkv, s_qkv, pq, stream, small_wave(s_qkv))) != SG_OK)
+        return st;
+      if (l == 0) trace_at(a, 3, stream);
+      layers::QkvPost qp;
+      qp.qkv = e->qkv;
+      qp.q_norm = static_cast<const __nv_bfloat16*>(lw[W_Q_NORM]);
+      qp.k_norm = static_cast<const __nv_bfloat16*>(lw[W_K_NORM]);
+      qp.inv_freq = m.inv_freq;
+      qp.position = e->meta.position;
+      qp.tree = e->meta.tree;
+      qp.local = e->meta.local;
+      qp.slots = a.slots;
+      qp.cache_len = a.cache_len;
+      qp.q_out = e->q;
+      qp.k_plane0 = k_plane0;
+      qp.v_plane0 = v_plane0;
+      qp.plane_stride = plane_stride;
+      qp.capacity = e->arena.capacity;
+      qp.plane_rows = plane_rows;
+      qp.rope = e->meta.rope;
+      qp.arena_row = e->meta.arena_row;
+      qp.nq = nq;
+      qp.nkv = nkv;
+      qp.head_dim = D;
+      qp.rows = Q;
+      qp.eps = m.rms_eps;
+      qp.status = a.status;
+      if ((st = layers::launch_qkv_post(qp, stream)) != SG_OK) return st;
+      if (l == 0) trace_at(a, 4, stream);
+    }
+
+    attn::Params ap;
+    ap.q = e->q;
+    ap.out = e->attn;
+    ap.k0 = k_plane0;
+    ap.v0 = v_plane0;
+    ap.plane_stride = plane_stride;
+    ap.capacity = e->arena.capacity;
+    ap.plane_rows = plane_rows;
+    ap.num_rows = Q;
+    ap.row_offsets = a.row_offsets;
+    ap.slots = a.slots;
+    ap.cache_len = a.cache_len;
+    ap.anc = e->meta.anc;
+    ap.nq = nq;
+    ap.nkv = nkv;
+    ap.group = nq / nkv;
+    ap.plane_k0 = l * 2 * nkv;
+    ap.plane_v0 = l * 2 * nkv + nkv;
+    ap.items = e->work.items;
+    ap.num_items = e->work.num_items;
+    ap.work_counter = e->work.counters + l;
+    ap.status = a.status;
+    ap.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
+    if ((st = attn::launch(e->kv_map, ap, a.R, a.max_rows_per_request, D, stream)) != SG_OK) return st;
+    if (l == 0) trace_at(a, 5, stream);
+
+    gemm::EpiResidual::Params po{e->x, H, nullptr, 0, a.status};
+    if (nf) {  // fold the post-attention RMSNorm into this epilogue and the gate/up GEMM
+      po.xw = e->xn;
+      po.ldw = H;
+      po.norm_w = static_cast<const __nv_bfloat16*>(lw[W_POST_NORM]);
+      po.ssq = e->ssq;
+      po.ss_parts = P;
+    }
+    if ((st = gemm::launch<gemm::EpiResidual>(e->attn_map, lm.o, s_o, po, stream, small_wave(s_o))) != SG_OK)
+      return st;
+    if (l == 0) trace_at(a, 6, stream);
+    if (!nf && (st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(lw[W_POST_NORM]), H, Q,
+                                            m.rms_eps, e->xn, stream)) != SG_OK)
+      return st;
+    if (l == 0) trace_at(a, 7, stream);
+    gemm::EpiSwiGlu::Params pg{e->h, I, a.status,
+                               nf ? gemm::RowNorm{e->ssq, P, inv_h, m.rms_eps} : gemm::RowNorm{}};
+    if ((st = gemm::launch<gemm::EpiSwiGlu>(e->xn_map, lm.gate_up, s_gu, pg, stream, small_wave(s_gu))) != SG_OK)
+      return st;
+    if (l == 0) trace_at(a, 8, stream);
+    // the residual stream after this layer is hidden_states[l + 1]; the last
+    // layer's entry is the final-normed stream, copied after the final norm
+    __nv_bfloat16* feat = nullptr;
+    if (a.feature_slot != nullptr && a.feature_slot[l] >= 0 && l + 1 < m.num_layers)
+      feat = static_cast<__nv_bfloat16*>(a.features_out) + static_cast<int64_t>(a.feature_slot[l]) * H;
+    gemm::EpiResidual::Params pd{e->x, H, feat, static_cast<int64_t>(a.nfeat) * H, a.status};
+    if (nf && l + 1 < m.num_layers) {  // fold the next layer's input RMSNorm
+      pd.xw = e->xn;
+      pd.ldw = H;
+      pd.norm_w = static_cast<const __nv_bfloat16*>(e->layer_ptrs[static_cast<size_t>(l + 1) * W_COUNT + W_IN_NORM]);
+      pd.ssq = e->ssq;
+      pd.ss_parts = P;
+    }
+    if ((st = gemm::launch<gemm::EpiResidual>(e->h_map, lm.down, s_down, pd, stream, small_wave(s_down))) != SG_OK)
+      return st;
+    if (l == 0) trace_at(a, 9, stream);
+  }
+  return SG_OK;
+}
+
+}  // namespace
+}  // namespace sg
 
 extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stream_ptr) {
   using namespace sg;
@@ -297,12 +544,9 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
   SG_CUDA_CHECK(cudaGetDevice(&dev));
   if (dev != e->device) return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: engine belongs to another device");
 
-  const int H = m.hidden, D = m.head_dim, I = m.intermediate;
-  const int nq = m.num_q_heads, nkv = m.num_kv_heads;
-  const int qkv_n = (nq + 2 * nkv) * D;
-  const int qw = nq * D;
+  const int H = m.hidden, D = m.head_dim;
+  const int nkv = m.num_kv_heads;
   const int64_t plane_rows = e->arena.num_slots * e->arena.capacity;
-  const int64_t plane_stride = plane_rows * D;  // elements between kv heads
   __nv_bfloat16* arena = static_cast<__nv_bfloat16*>(e->arena.storage);
   int st;
 
@@ -317,151 +561,20 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
                                  stream)) != SG_OK)
     return st;
   const bool nf = norm_fused();
-  const int P = e->ss_parts;
   const float inv_h = 1.0f / static_cast<float>(H);
-  if (nf && (st = layers::launch_norm_fold(e->x, static_cast<const __nv_bfloat16*>(e->layer_ptrs[W_IN_NORM]), H, Q,
-                                           e->xn, e->ssq, stream)) != SG_OK)
-    return st;
-
-  if ((st = layers::launch_attention_work(w.row_offsets, w.cache_lengths, R, nq / nkv, nkv, e->work, m.num_layers,
-                                         stream)) != SG_OK)
-    return st;
-  trace(w, 1, stream);
-  const gemm::Shape s_qkv = gemm::make_shape(Q, qkv_n, H);
-  const gemm::Shape s_o = gemm::make_shape(Q, H, qw);
-  const gemm::Shape s_gu = gemm::make_shape(Q, 2 * I, H);
-  const gemm::Shape s_down = gemm::make_shape(Q, H, I);
-  // Shapes with at most half a wave of tiles (few packed rows) give each
-  // tile's k-blocks to two CTAs; everything else runs whole tiles, which
-  // measured faster (a tile split across CTA runs makes its owner wait).
-  auto small_wave = [&](const gemm::Shape& sh) -> const gemm::SplitWorkspace* {
-    return 2 * sh.tiles <= e->sms ? &e->split : nullptr;
-  };
-  for (int l = 0; l < m.num_layers; ++l) {
-    const void* const* lw = &e->layer_ptrs[static_cast<size_t>(l) * W_COUNT];
-    const LayerMaps& lm = e->maps[l];
-    __nv_bfloat16* k_plane0 = arena + static_cast<int64_t>(l) * 2 * nkv * plane_stride;
-    __nv_bfloat16* v_plane0 = k_plane0 + static_cast<int64_t>(nkv) * plane_stride;
-
-    if (!nf && (st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(lw[W_IN_NORM]), H, Q, m.rms_eps,
-                                            e->xn, stream)) != SG_OK)
-      return st;
-    if (l == 0) trace(w, 2, stream);
-    // input RMSNorm's row scale: sums from the fold kernel (layer 0, one part)
-    // or from the previous down projection's tiles
-    const gemm::RowNorm rn_in = nf ? gemm::RowNorm{e->ssq, l == 0 ? 1 : P, inv_h, m.rms_eps} : gemm::RowNorm{};
-    if (qkv_fused()) {
-      // q/k/v projection with q/k RMSNorm, RoPE and the KV-tail write in its epilogue
-      if (D == 128) {
-        gemm::EpiQkvPost<128>::Params pf{e->q, qw, k_plane0, v_plane0, plane_stride, e->meta.arena_row,
-                                         e->meta.rope, static_cast<const __nv_bfloat16*>(lw[W_Q_NORM]),
-                                         static_cast<const __nv_bfloat16*>(lw[W_K_NORM]), nq, nkv, m.rms_eps,
-                                         w.status, rn_in};
-        st = gemm::launch<gemm::EpiQkvPost<128>>(e->xn_map, lm.qkv, s_qkv, pf, stream, small_wave(s_qkv));
-      } else {
-        gemm::EpiQkvPost<64>::Params pf{e->q, qw, k_plane0, v_plane0, plane_stride, e->meta.arena_row,
-                                        e->meta.rope, static_cast<const __nv_bfloat16*>(lw[W_Q_NORM]),
-                                        static_cast<const __nv_bfloat16*>(lw[W_K_NORM]), nq, nkv, m.rms_eps,
-                                        w.status, rn_in};
-        st = gemm::launch<gemm::EpiQkvPost<64>>(e->xn_map, lm.qkv, s_qkv, pf, stream, small_wave(s_qkv));
-      }
-      if (st != SG_OK) return st;
-      if (l == 0) {
-        trace(w, 3, stream);
-        trace(w, 4, stream);
-      }
-    } else {
-    gemm::EpiStoreBf16::Params pq{e->qkv, qkv_n, w.status};
-    if ((st = gemm::launch<gemm::EpiStoreBf16>(e->xn_map, lm.qkv, s_qkv, pq, stream, small_wave(s_qkv))) != SG_OK) return st;
-    if (l == 0) trace(w, 3, stream);
-
-    layers::QkvPost qp;
-    qp.qkv = e->qkv;
-    qp.q_norm = static_cast<const __nv_bfloat16*>(lw[W_Q_NORM]);
-    qp.k_norm = static_cast<const __nv_bfloat16*>(lw[W_K_NORM]);
-    qp.inv_freq = m.inv_freq;
-    qp.position = e->meta.position;
-    qp.tree = e->meta.tree;
-    qp.local = e->meta.local;
-    qp.slots = w.slots;
-    qp.cache_len = w.cache_lengths;
-    qp.q_out = e->q;
-    qp.k_plane0 = k_plane0;
-    qp.v_plane0 = v_plane0;
-    qp.plane_stride = plane_stride;
-    qp.capacity = e->arena.capacity;
-    qp.plane_rows = plane_rows;
-    qp.rope = e->meta.rope;
-    qp.arena_row = e->meta.arena_row;
-    qp.nq = nq;
-    qp.nkv = nkv;
-    qp.head_dim = D;
-    qp.rows = Q;
-    qp.eps = m.rms_eps;
-    qp.status = w.status;
-    if ((st = layers::launch_qkv_post(qp, stream)) != SG_OK) return st;
-    if (l == 0) trace(w, 4, stream);
-    }
-
-    attn::Params ap;
-    ap.q = e->q;
-    ap.out = e->attn;
-    ap.k0 = k_plane0;
-    ap.v0 = v_plane0;
-    ap.plane_stride = plane_stride;
-    ap.capacity = e->arena.capacity;
-    ap.plane_rows = plane_rows;
-    ap.num_rows = Q;
-    ap.row_offsets = w.row_offsets;
-    ap.slots = w.slots;
-    ap.cache_len = w.cache_lengths;
-    ap.anc = e->meta.anc;
-    ap.nq = nq;
-    ap.nkv = nkv;
-    ap.group = nq / nkv;
-    ap.plane_k0 = l * 2 * nkv;
-    ap.plane_v0 = l * 2 * nkv + nkv;
-    ap.items = e->work.items;
-    ap.num_items = e->work.num_items;
-    ap.work_counter = e->work.counters + l;
-    ap.status = w.status;
-    ap.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
-    if ((st = attn::launch(e->kv_map, ap, R, w.max_rows_per_request, D, stream)) != SG_OK) return st;
-    if (l == 0) trace(w, 5, stream);
-
-    gemm::EpiResidual::Params po{e->x, H, nullptr, 0, w.status};
-    if (nf) {  // fold the post-attention RMSNorm into this epilogue and the gate/up GEMM
-      po.xw = e->xn;
-      po.ldw = H;
-      po.norm_w = static_cast<const __nv_bfloat16*>(lw[W_POST_NORM]);
-      po.ssq = e->ssq;
-      po.ss_parts = P;
-    }
-    if ((st = gemm::launch<gemm::EpiResidual>(e->attn_map, lm.o, s_o, po, stream, small_wave(s_o))) != SG_OK) return st;
-    if (l == 0) trace(w, 6, stream);
-    if (!nf && (st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(lw[W_POST_NORM]), H, Q,
-                                            m.rms_eps, e->xn, stream)) != SG_OK)
-      return st;
-    if (l == 0) trace(w, 7, stream);
-    gemm::EpiSwiGlu::Params pg{e->h, I, w.status, nf ? gemm::RowNorm{e->ssq, P, inv_h, m.rms_eps} : gemm::RowNorm{}};
-    if ((st = gemm::launch<gemm::EpiSwiGlu>(e->xn_map, lm.gate_up, s_gu, pg, stream, small_wave(s_gu))) != SG_OK) return st;
-    if (l == 0) trace(w, 8, stream);
-    // the residual stream after this layer is hidden_states[l + 1]; the last
-    // layer's entry is the final-normed stream, copied after the final norm
-    __nv_bfloat16* feat = nullptr;
-    if (feature_slot[l] >= 0 && l + 1 < m.num_layers)
-      feat = static_cast<__nv_bfloat16*>(w.features_out) + static_cast<int64_t>(feature_slot[l]) * H;
-    gemm::EpiResidual::Params pd{e->x, H, feat, static_cast<int64_t>(nfeat) * H, w.status};
-    if (nf && l + 1 < m.num_layers) {  // fold the next layer's input RMSNorm
-      pd.xw = e->xn;
-      pd.ldw = H;
-      pd.norm_w = static_cast<const __nv_bfloat16*>(e->layer_ptrs[static_cast<size_t>(l + 1) * W_COUNT + W_IN_NORM]);
-      pd.ssq = e->ssq;
-      pd.ss_parts = P;
-    }
-    if ((st = gemm::launch<gemm::EpiResidual>(e->h_map, lm.down, s_down, pd, stream, small_wave(s_down))) != SG_OK) return st;
-    if (l == 0) trace(w, 9, stream);
-  }
+  StackArgs sa;
+  sa.R = R;
+  sa.Q = Q;
+  sa.row_offsets = w.row_offsets;
+  sa.slots = w.slots;
+  sa.cache_len = w.cache_lengths;
+  sa.max_rows_per_request = w.max_rows_per_request;
+  sa.status = w.status;
+  sa.wave = &w;
+  sa.feature_slot = feature_slot.data();
+  sa.nfeat = nfeat;
+  sa.features_out = w.features_out;
+  if ((st = run_stack(e, sa, stream)) != SG_OK) return st;
   trace(w, 10, stream);
   if (w.hidden_out != nullptr)
     SG_CUDA_CHECK(cudaMemcpyAsync(w.hidden_out, e->x, static_cast<size_t>(Q) * H * 4, cudaMemcpyDeviceToDevice,
@@ -531,4 +644,148 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
   }
   trace(w, 15, stream);
   return SG_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Drafter step (DFlash block drafter, dflash.py:147-200, as the decoder calls
+// it with a persistent per-request draft cache,
+// continuous_tree_block_decode.py:889-962).
+// ---------------------------------------------------------------------------
+extern "C" int sg_draft_engine_create(const sg_model_desc* model, const sg_draft_desc* draft,
+                                      const sg_arena_desc* arena, int32_t max_requests, void** engine_out) {
+  using namespace sg;
+  if (draft == nullptr || engine_out == nullptr)
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_draft_engine_create: null argument");
+  *engine_out = nullptr;
+  if (draft->fc == nullptr || draft->hidden_norm == nullptr || draft->num_feature_layers < 1 ||
+      draft->block_size < 1 || draft->block_size > layers::kMaxTreeRows || draft->max_update_rows < 1 ||
+      max_requests < 1)
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_draft_engine_create: bad drafter description");
+  const int64_t block_rows = static_cast<int64_t>(max_requests) * draft->block_size;
+  const int max_rows = static_cast<int>(std::max<int64_t>(block_rows, draft->max_update_rows));
+  std::unique_ptr<Engine> e;
+  int st = create_engine(model, arena, max_rows, max_requests, e);
+  if (st != SG_OK) return st;
+  const sg_model_desc& m = e->model;
+  const int H = m.hidden, D = m.head_dim, F = draft->num_feature_layers;
+  const int qw = m.num_q_heads * D, kvw = 2 * m.num_kv_heads * D;
+  if (kvw % 32 != 0) return fail(SG_ERR_UNSUPPORTED, "sg_draft_engine_create: k|v width % 32 != 0");
+  std::unique_ptr<DraftState> d(new DraftState());
+  d->desc = *draft;
+  if ((st = make_tmap_2d_bf16(&d->fc_map, draft->fc, static_cast<uint64_t>(F) * H, H,
+                              static_cast<uint64_t>(F) * H * 2, gemm::BK, gemm::BN)) != SG_OK)
+    return st;
+  d->kv_maps.resize(m.num_layers);
+  for (int l = 0; l < m.num_layers; ++l) {
+    const uint8_t* qkv = static_cast<const uint8_t*>(e->layer_ptrs[static_cast<size_t>(l) * W_COUNT + W_QKV]);
+    if ((st = make_tmap_2d_bf16(&d->kv_maps[l], qkv + static_cast<size_t>(qw) * H * 2, H, kvw,
+                                static_cast<uint64_t>(H) * 2, gemm::BK, gemm::BN)) != SG_OK)
+      return st;
+  }
+  const size_t U = draft->max_update_rows;
+  size_t bytes = 0;
+  bytes += U * H * 4 + 256;                                   // th32
+  bytes += U * H * 2 + 256;                                   // th
+  bytes += U * 4 * 3 + 3 * 256;                               // ctx position, tree, local
+  bytes += U * (D / 2) * 8 + 256;                             // ctx rope
+  bytes += U * 8 + 256;                                       // ctx arena rows
+  bytes += (static_cast<size_t>(max_requests) + 1) * 8 + 256; // block offsets
+  bytes += static_cast<size_t>(max_requests) * 8 + 256;       // prefix lengths
+  bytes += static_cast<size_t>(block_rows) * 8 + 256;         // block tokens
+  SG_CUDA_CHECK(cudaMalloc(&d->buffer, bytes));
+  uint8_t* cur = static_cast<uint8_t*>(d->buffer);
+  d->th32 = carve<float>(cur, U * H);
+  d->th = carve<__nv_bfloat16>(cur, U * H);
+  d->ctx_meta = layers::RowMeta{};
+  d->ctx_meta.position = carve<int32_t>(cur, U);
+  d->ctx_meta.tree = carve<int32_t>(cur, U);
+  d->ctx_meta.local = carve<int32_t>(cur, U);
+  d->ctx_meta.rope = carve<float2>(cur, U * (D / 2));
+  d->ctx_meta.arena_row = carve<int64_t>(cur, U);
+  d->block_offsets = carve<int64_t>(cur, static_cast<size_t>(max_requests) + 1);
+  d->prefix = carve<int64_t>(cur, max_requests);
+  d->block_tokens = carve<int64_t>(cur, block_rows);
+  if (static_cast<size_t>(cur - static_cast<uint8_t*>(d->buffer)) > bytes)
+    return fail(SG_ERR_WORKSPACE, "sg_draft_engine_create: buffer layout overflow");
+  if ((st = make_tmap_2d_bf16(&d->th_map, d->th, H, U, static_cast<uint64_t>(H) * 2, gemm::BK, gemm::BM)) != SG_OK)
+    return st;
+  e->draft = std::move(d);
+  *engine_out = e.release();
+  return SG_OK;
+}
+
+extern "C" int sg_draft_pass(void* engine, const sg_draft_wave* wave, void* stream_ptr) {
+  using namespace sg;
+  if (engine == nullptr || wave == nullptr) return fail(SG_ERR_INVALID_ARGUMENT, "sg_draft_pass: null argument");
+  Engine* e = static_cast<Engine*>(engine);
+  if (!e->draft) return fail(SG_ERR_INVALID_ARGUMENT, "sg_draft_pass: not a drafter engine (sg_draft_engine_create)");
+  DraftState& d = *e->draft;
+  const sg_draft_wave& w = *wave;
+  const sg_model_desc& m = e->model;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const int R = w.num_requests, U = w.num_update_rows, B = d.desc.block_size;
+  if (R < 1 || R > e->max_requests || static_cast<int64_t>(R) * B > e->max_rows || U < 0 ||
+      U > d.desc.max_update_rows)
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_draft_pass: sizes out of range");
+  if (w.slots == nullptr || w.cache_lengths == nullptr || w.update_offsets == nullptr ||
+      w.anchor_tokens == nullptr || w.logits_out == nullptr || (U > 0 && w.features == nullptr))
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_draft_pass: null wave array");
+  if ((U > 0 && (reinterpret_cast<uintptr_t>(w.features) & 15u) != 0) ||
+      (reinterpret_cast<uintptr_t>(w.logits_out) & 15u) != 0)
+    return fail(SG_ERR_INVALID_ARGUMENT, "sg_draft_pass: features and logits_out must be 16-byte aligned");
+  int dev = 0;
+  SG_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev != e->device) return fail(SG_ERR_INVALID_ARGUMENT, "sg_draft_pass: engine belongs to another device");
+  const int H = m.hidden, D = m.head_dim, F = d.desc.num_feature_layers;
+  const int Q = R * B;
+  const int64_t plane_rows = e->arena.num_slots * e->arena.capacity;
+  int st;
+  // context rows of a malformed request keep tree -1 (no arena row)
+  if (U > 0) SG_CUDA_CHECK(cudaMemsetAsync(d.ctx_meta.tree, 0xFF, static_cast<size_t>(U) * 4, stream));
+  if ((st = layers::launch_draft_meta(w.update_offsets, w.cache_lengths, w.anchor_tokens, d.desc.mask_token_id, R, B,
+                                      U, e->meta, d.ctx_meta, d.block_offsets, d.prefix, d.block_tokens,
+                                      w.lengths_out, w.status, stream)) != SG_OK)
+    return st;
+  // block rows after the committed context, context rows at cache_len ..
+  if ((st = layers::launch_row_rope(e->meta, m.inv_freq, D, Q, w.slots, d.prefix, e->arena.capacity, plane_rows,
+                                    w.status, stream)) != SG_OK)
+    return st;
+  if ((st = layers::launch_row_rope(d.ctx_meta, m.inv_freq, D, U, w.slots, w.cache_lengths, e->arena.capacity,
+                                    plane_rows, w.status, stream)) != SG_OK)
+    return st;
+  if ((st = layers::launch_embed(d.block_tokens, static_cast<const __nv_bfloat16*>(m.embed), m.vocab, H, Q, e->x,
+                                 w.status, stream)) != SG_OK)
+    return st;
+  if (U > 0) {
+    // target_hidden = hidden_norm(fc(features))
+    CUtensorMap feat_map;
+    if ((st = make_tmap_2d_bf16(&feat_map, w.features, static_cast<uint64_t>(F) * H, U,
+                                static_cast<uint64_t>(F) * H * 2, gemm::BK, gemm::BM)) != SG_OK)
+      return st;
+    const gemm::Shape s_fc = gemm::make_shape(U, H, F * H);
+    gemm::EpiStoreF32::Params pf{d.th32, H, w.status};
+    if ((st = gemm::launch<gemm::EpiStoreF32>(feat_map, d.fc_map, s_fc, pf, stream,
+                                              2 * s_fc.tiles <= e->sms ? &e->split : nullptr)) != SG_OK)
+      return st;
+    if ((st = layers::launch_rmsnorm(d.th32, static_cast<const __nv_bfloat16*>(d.desc.hidden_norm), H, U, m.rms_eps,
+                                     d.th, stream)) != SG_OK)
+      return st;
+  }
+  StackArgs sa;
+  sa.R = R;
+  sa.Q = Q;
+  sa.row_offsets = d.block_offsets;
+  sa.slots = w.slots;
+  sa.cache_len = d.prefix;
+  sa.max_rows_per_request = B;
+  sa.status = w.status;
+  sa.draft = &d;
+  sa.ctx_rows = U;
+  if ((st = run_stack(e, sa, stream)) != SG_OK) return st;
+  // drafter's final norm, target's LM head: bf16 logits of every block row
+  if ((st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(m.final_norm), H, Q, m.rms_eps, e->xn,
+                                   stream)) != SG_OK)
+    return st;
+  gemm::EpiStoreBf16::Params pl{static_cast<__nv_bfloat16*>(w.logits_out), m.vocab, w.status};
+  return gemm::launch<gemm::EpiStoreBf16>(e->xn_map, e->lm_map, gemm::make_shape(Q, m.vocab, H), pl, stream);
 }

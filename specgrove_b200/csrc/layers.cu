@@ -577,6 +577,59 @@ int launch_row_rope(const RowMeta& meta, const float* inv_freq, int head_dim, in
   return check_launch("row_rope_kernel");
 }
 
+__global__ void __launch_bounds__(256) draft_meta_kernel(const int64_t* __restrict__ update_offsets,
+                                                         const int64_t* __restrict__ cache_len,
+                                                         const int64_t* __restrict__ anchors, int64_t mask_token,
+                                                         int num_requests, int block, int update_rows,
+                                                         RowMeta bm, RowMeta cm, int64_t* __restrict__ block_offsets,
+                                                         int64_t* __restrict__ prefix_len,
+                                                         int64_t* __restrict__ block_tokens,
+                                                         int64_t* __restrict__ lengths_out, int32_t* status) {
+  const int t = blockIdx.x;
+  int64_t u0 = update_offsets[t], u1 = update_offsets[t + 1];
+  if (u0 < 0 || u1 < u0 || u1 > update_rows || (t == num_requests - 1 && u1 != update_rows)) {
+    if (threadIdx.x == 0) report(status, SG_ERR_TREE);
+    u0 = u1 = 0;
+  }
+  const int64_t prefix = cache_len[t] + (u1 - u0);
+  for (int j = threadIdx.x; j < block; j += blockDim.x) {
+    const int64_t q = static_cast<int64_t>(t) * block + j;
+    uint32_t* anc = bm.anc + q * kAncWords;
+    for (int w = 0; w < kAncWords; ++w) {
+      const int lo = 32 * w;
+      anc[w] = block >= lo + 32 ? 0xFFFFFFFFu : (block > lo ? (1u << (block - lo)) - 1u : 0u);
+    }
+    bm.position[q] = static_cast<int32_t>(prefix + j);
+    bm.tree[q] = t;
+    bm.local[q] = j;
+    bm.request_id[q] = t;
+    block_tokens[q] = j == 0 ? anchors[t] : mask_token;
+  }
+  for (int64_t i = u0 + threadIdx.x; i < u1; i += blockDim.x) {
+    cm.position[i] = static_cast<int32_t>(cache_len[t] + (i - u0));
+    cm.tree[i] = t;
+    cm.local[i] = static_cast<int32_t>(i - u0);
+  }
+  if (threadIdx.x == 0) {
+    block_offsets[t] = static_cast<int64_t>(t) * block;
+    if (t == num_requests - 1) block_offsets[num_requests] = static_cast<int64_t>(num_requests) * block;
+    prefix_len[t] = prefix;
+    if (lengths_out != nullptr) lengths_out[t] = prefix;
+  }
+}
+
+int launch_draft_meta(const int64_t* update_offsets, const int64_t* cache_len, const int64_t* anchors,
+                      int64_t mask_token, int num_requests, int block, int update_rows, RowMeta block_meta,
+                      RowMeta ctx_meta, int64_t* block_offsets, int64_t* prefix_len, int64_t* block_tokens,
+                      int64_t* lengths_out, int32_t* status, cudaStream_t stream) {
+  if (num_requests <= 0) return SG_OK;
+  if (block < 1 || block > kMaxTreeRows) return fail(SG_ERR_UNSUPPORTED, "draft_meta: block size must be 1..256");
+  draft_meta_kernel<<<num_requests, 256, 0, stream>>>(update_offsets, cache_len, anchors, mask_token, num_requests,
+                                                      block, update_rows, block_meta, ctx_meta, block_offsets,
+                                                      prefix_len, block_tokens, lengths_out, status);
+  return check_launch("draft_meta_kernel");
+}
+
 int launch_embed(const int64_t* tokens, const __nv_bfloat16* embed, int64_t vocab, int hidden, int rows, float* x,
                  int32_t* status, cudaStream_t stream) {
   if (rows <= 0) return SG_OK;

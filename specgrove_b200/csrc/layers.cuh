@@ -44,6 +44,17 @@ struct AttentionWork {
 int launch_attention_work(const int64_t* row_offsets, const int64_t* cache_len, int num_trees, int group,
                           int num_kv_heads, AttentionWork work, int num_layers, cudaStream_t stream);
 
+// Per-row metadata of a drafter step.  Request t's block rows t*B .. t*B+B-1
+// see each other (all bits of the block set: the block is bidirectional) at
+// positions prefix_t + j, prefix_t = cache_len[t] + its update rows; its
+// context rows update_offsets[t] .. update_offsets[t+1]-1 sit at positions
+// cache_len[t] + i.  Writes the block rows' offsets, prefix lengths and
+// input tokens (anchor, then mask tokens) and lengths_out = prefix.
+int launch_draft_meta(const int64_t* update_offsets, const int64_t* cache_len, const int64_t* anchors,
+                      int64_t mask_token, int num_requests, int block, int update_rows, RowMeta block_meta,
+                      RowMeta ctx_meta, int64_t* block_offsets, int64_t* prefix_len, int64_t* block_tokens,
+                      int64_t* lengths_out, int32_t* status, cudaStream_t stream);
+
 int launch_embed(const int64_t* tokens, const __nv_bfloat16* embed, int64_t vocab, int hidden, int rows,
                  float* x, int32_t* status, cudaStream_t stream);
 

@@ -37,20 +37,25 @@ def _status(device) -> torch.Tensor:
 def proposal_topk(logits: torch.Tensor, temperature: float, k: int, status: torch.Tensor | None = None,
                   stream=None) -> tuple[torch.Tensor, torch.Tensor]:
     """Top-k fp64 log proposal masses and int64 ids of every row of CUDA
-    bf16/fp32 ``logits`` [..., V] (rows = all leading dims)."""
-    if logits.dtype not in (torch.bfloat16, torch.float32) or not logits.is_cuda:
-        raise ValueError("proposal logits must be CUDA bf16 or fp32")
+    bf16/fp32 ``logits`` [V], [rows, V] or [groups, rows, V] (unit stride
+    over V; the 3-D form may be a strided view, e.g. block rows 1..L of the
+    drafter's [R, block, V] logits, read in place)."""
+    if logits.dtype not in (torch.bfloat16, torch.float32) or not logits.is_cuda or logits.dim() > 3:
+        raise ValueError("proposal logits must be CUDA bf16 or fp32 with at most 3 dims")
+    if logits.stride(-1) != 1:
+        logits = logits.contiguous()
     V = logits.shape[-1]
-    flat = logits.reshape(-1, V)
-    if flat.stride(-1) != 1:
-        flat = flat.contiguous()
-    rows = flat.shape[0]
+    view = logits.reshape(1, -1, V) if logits.dim() < 3 else logits
+    if view.stride(-1) != 1:
+        view = view.contiguous()
+    groups, per, _ = view.shape
+    rows = groups * per
     log_q = torch.empty((rows, k), dtype=torch.float64, device=logits.device)
     ids = torch.empty((rows, k), dtype=torch.int64, device=logits.device)
     lib = _lib.load()
-    st = lib.sg_proposal_topk(flat.data_ptr(), SG_DTYPE_BF16 if logits.dtype == torch.bfloat16 else SG_DTYPE_F32,
-                              flat.stride(0), rows, V, int(k), float(temperature), log_q.data_ptr(), ids.data_ptr(),
-                              _lib.ptr(status), _lib.stream_ptr(stream))
+    st = lib.sg_proposal_topk(view.data_ptr(), SG_DTYPE_BF16 if logits.dtype == torch.bfloat16 else SG_DTYPE_F32,
+                              view.stride(1), per, view.stride(0), rows, V, int(k), float(temperature),
+                              log_q.data_ptr(), ids.data_ptr(), _lib.ptr(status), _lib.stream_ptr(stream))
     if st == _lib.SG_ERR_INVALID_ARGUMENT:
         raise ValueError(lib.sg_last_error().decode())
     _lib.check(st, "sg_proposal_topk")
@@ -144,6 +149,9 @@ class WavePlan:
     parents: torch.Tensor      # [max_rows]
     tokens: torch.Tensor       # [max_rows]
     status: torch.Tensor       # int32 device word (0 = ok)
+    log_q: torch.Tensor | None = None  # [R, length, k] ranked log proposal masses
+    ids: torch.Tensor | None = None    # [R, length, k] their token ids
+    draft_logits: torch.Tensor | None = None  # [R, block, V] when planned by B200Drafter.propose
 
 
 def plan_wave(draft_logits: torch.Tensor, temperature: float, tiers: Sequence[int], weights: torch.Tensor,
@@ -166,4 +174,4 @@ def plan_wave(draft_logits: torch.Tensor, temperature: float, tiers: Sequence[in
                                               row_cost_curve=row_cost_curve, status=status, stream=stream)
     offsets, parents, tokens = pack_tree_wave(trees, allocation, anchor_tokens, row_budget, status=status,
                                               stream=stream)
-    return WavePlan(trees, allocation, offsets, parents, tokens, status)
+    return WavePlan(trees, allocation, offsets, parents, tokens, status, log_q, ids)

@@ -30,6 +30,12 @@ functions (no restatement):
                      random fp32 logits: the top-k log masses it ranks, the
                      tree, and _prefix_tree / _draft_tree_expected_tokens
                      (continuous_tree_block_decode.py:560-586) per tier.
+  dflash_step.npz    third_party/ddtree_official/model/dflash.py
+                     DFlashDraftModel (tiny configuration, weights of
+                     tests/dflash_case.py) over two drafter steps per request
+                     with a DynamicCache cropped to the context rows, as
+                     dflash.py:230-241 and the decoder drive it: block logits
+                     through the LM head and the cached context K/V.
 
 The fixtures are small (tens of KB) and deterministic (seeded torch CPU RNG).
 """
@@ -397,6 +403,55 @@ def build_draft_trees(ref, gen):
     np.savez_compressed(OUT / "draft_trees.npz", **arrays)
 
 
+def build_dflash_step(reference: Path):
+    sys.path.insert(0, str(reference / "code" / "natural" / "third_party" / "ddtree_official"))
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    from model.dflash import DFlashDraftModel
+    from transformers import DynamicCache, Qwen3Config
+    import dflash_case as case
+    c = case.CONFIG
+    cfg = Qwen3Config(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["intermediate"],
+                      num_hidden_layers=c["num_layers"], num_attention_heads=c["num_q_heads"],
+                      num_key_value_heads=c["num_kv_heads"], head_dim=c["head_dim"], rms_norm_eps=c["rms_eps"],
+                      rope_theta=c["rope_theta"], max_position_embeddings=256, attention_bias=False)
+    cfg.dflash_config = {"target_layer_ids": list(range(c["feature_layers"])), "mask_token_id": c["mask_token"]}
+    cfg.block_size = c["block"]
+    cfg.num_target_layers = 8
+    cfg._attn_implementation = "eager"
+    model = DFlashDraftModel(cfg).float().eval()
+    w, features = case.make_weights_and_inputs()
+    sd = {"fc.weight": w["fc"], "hidden_norm.weight": w["hidden_norm"], "norm.weight": w["norm"]}
+    hf = {"in_norm": "input_layernorm", "q": "self_attn.q_proj", "k": "self_attn.k_proj", "v": "self_attn.v_proj",
+          "q_norm": "self_attn.q_norm", "k_norm": "self_attn.k_norm", "o": "self_attn.o_proj",
+          "post_norm": "post_attention_layernorm", "gate": "mlp.gate_proj", "up": "mlp.up_proj",
+          "down": "mlp.down_proj"}
+    for l in range(c["num_layers"]):
+        for ours, theirs in hf.items():
+            sd[f"layers.{l}.{theirs}.weight"] = w[f"layers.{l}.{ours}"]
+    missing, unexpected = model.load_state_dict(sd, strict=False)
+    assert not unexpected and all("rotary" in k for k in missing), (missing, unexpected)
+    embed = torch.nn.Embedding.from_pretrained(w["embed"])
+    arrays = {}
+    for r, steps in enumerate(case.UPDATES):
+        cache = DynamicCache()
+        start = 0
+        for s_i, u in enumerate(steps):
+            feats = features[r][s_i]
+            block_ids = torch.tensor([[case.ANCHORS[r][s_i]] + [c["mask_token"]] * (c["block"] - 1)])
+            positions = torch.arange(start, start + u + c["block"])[None]
+            with torch.no_grad():
+                hidden = model(target_hidden=feats[None], noise_embedding=embed(block_ids), position_ids=positions,
+                               past_key_values=cache, use_cache=True, is_causal=False)
+                logits = hidden[0] @ w["lm_head"].T
+            start += u
+            cache.crop(start)
+            arrays[f"r{r}_s{s_i}_logits"] = logits.numpy()
+        for l in range(c["num_layers"]):
+            arrays[f"r{r}_k{l}"] = cache.layers[l].keys[0].numpy()
+            arrays[f"r{r}_v{l}"] = cache.layers[l].values[0].numpy()
+    np.savez_compressed(OUT / "dflash_step.npz", **arrays)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the specgrove checkout")
@@ -422,6 +477,7 @@ def main():
         arrays[f"temperature_{i}"] = np.float64(c["temperature"])
     np.savez_compressed(OUT / "accept_logits.npz", **arrays)
     build_draft_trees(ref, torch.Generator().manual_seed(20261203))
+    build_dflash_step(Path(args.reference))
     for p in sorted(OUT.glob("*.*")):
         print(p.name, p.stat().st_size)
 

@@ -252,3 +252,25 @@ def test_draft_tree_oracle_matches_reference():
         for b, u in zip(c["tiers"], c["utilities"]):
             got = tier_utility(t, int(b))
             assert (math.isnan(got) and math.isnan(u)) or got == u
+
+
+def test_dflash_oracle_matches_reference():
+    """oracle/draft_forward.py against the reference DFlashDraftModel over two
+    cached drafter steps per request: block logits and cached context K/V."""
+    import torch
+    import dflash_case as case
+    from oracle.draft_forward import dflash_step
+    c = case.CONFIG
+    z = np.load(case.GOLDEN)
+    w, features = case.make_weights_and_inputs()
+    for r, steps in enumerate(case.UPDATES):
+        ck, cv = [], []
+        for s_i, _ in enumerate(steps):
+            logits, ck, cv = dflash_step(w, c["num_layers"], c["num_q_heads"], c["num_kv_heads"], c["head_dim"],
+                                         features[r][s_i], ck, cv, case.ANCHORS[r][s_i], c["mask_token"], c["block"],
+                                         case.inv_freq(), c["rms_eps"])
+            want = z[f"r{r}_s{s_i}_logits"]
+            assert np.max(np.abs(logits.numpy() - want)) < 1e-4 * max(1.0, np.abs(want).max())
+        for l in range(c["num_layers"]):
+            assert np.max(np.abs(ck[l].numpy() - z[f"r{r}_k{l}"])) < 1e-5
+            assert np.max(np.abs(cv[l].numpy() - z[f"r{r}_v{l}"])) < 1e-5
