@@ -21,7 +21,13 @@ far larger than L2, so no flush is needed.  At N = 1 the same line nests the
 configuration-2 acceptance sweep and the configuration-3 (Qwen3-4B shape)
 pass, measured in the same run.
 `verify4b` is configuration 3 (Qwen3-4B shape, 16 requests, 512 rows);
-`accept` is the kernel-isolated acceptance sweep (configuration 2).
+`accept` is the kernel-isolated acceptance sweep (configuration 2);
+`draft` prints only the nested drafter block (below).
+
+Also nested at N = 1: `draft`, the step before each wave at the
+configuration-4 geometry (DFlash drafter of Qwen3-8B shape over the 64
+requests' draft caches, then the on-device wave plan: proposals, trees, tier
+knapsack, packed wave), and at every N `config5`, the open-loop serving run.
 
 `--impl reference` times the reference's CPU path (restated in oracle/: torch
 fp32 target pass with the packed tree mask, fp32 softmax, the reference's
@@ -515,6 +521,8 @@ def run_verify(args, world, rank):
         del wl
         torch.cuda.empty_cache()
         nested = nested_configs(args, world, rank) if world == 1 else {}
+        if world == 1:
+            nested["draft"] = measure_draft(args, world, rank, weights)
         nested["config5"] = measure_serving(args, world, rank, weights)
         line["nested"] = nested
     return line
@@ -585,6 +593,107 @@ def measure_serving(args, world, rank, weights=None):
             "collective": "per-wave NCCL all_gather_into_tensor of allocator scores + clock/load/done header"
                           if world > 1 else "none (one rank)",
             "gpu_launches": _lib.launch_count() - launches0, "clocks": clocks.summary()}
+
+
+def measure_draft(args, world, rank, weights):
+    """The step before each wave at the configuration-4 geometry: the DFlash
+    drafter of Qwen3-8B shape (5 layers, block 16) over 64 requests whose
+    draft caches hold L_i ~ U[1024, 4096] context rows (synthetic K/V), each
+    appending 1-4 new context rows (the previous wave's kept rows), then the
+    on-device wave plan from block rows 1..15: top-128 proposals per depth,
+    128-node best-first trees, tier utilities for {16, 32, 64, 128}, the
+    2048-row tier knapsack and the packed wave.  Device-timed with events."""
+    from specgrove_b200 import _lib
+    from specgrove_b200.allocator import allocate_tree_budgets_device
+    from specgrove_b200.draft_tree import build_draft_trees, pack_tree_wave, plan_wave, proposal_topk
+    from specgrove_b200.drafter import QWEN3_8B_DFLASH, B200Drafter, DraftWeights
+    shape = QWEN3_8B_DFLASH
+    dw = DraftWeights.random(shape, weights, seed=99)
+    R, B, V, H = 64, shape.block_size, shape.vocab, shape.hidden
+    g = torch.Generator().manual_seed(4321)
+    prefix = torch.randint(1024, 4097, (R,), generator=g)
+    upd = torch.randint(1, 5, (R,), generator=g)
+    U = int(upd.sum())
+    capacity = 4096 + 4 + B + 12
+    drafter = B200Drafter(dw, num_slots=R, capacity=capacity, max_requests=R, max_update_rows=U)
+    drafter.arena.storage.normal_(0.0, 1.0, generator=torch.Generator(device="cuda").manual_seed(5 + rank))
+    dev = "cuda"
+    slots = torch.arange(R, device=dev)
+    cache_len = prefix.to(dev)
+    offsets = torch.cat([torch.zeros(1, dtype=torch.long), upd.cumsum(0)]).to(dev)
+    feats = (torch.randn((U, shape.num_feature_layers * H), generator=g) * 2).to(torch.bfloat16).to(dev)
+    anchors = torch.randint(0, V, (R,), generator=g).to(dev)
+    logits = torch.empty((R, B, V), dtype=torch.bfloat16, device=dev)
+    tiers = [16, 32, 64, 128]
+    wts = (1.0 + torch.rand(R, generator=g, dtype=torch.float64)).to(dev)
+
+    def draft():
+        drafter.draft_device(slots, cache_len, offsets, feats, anchors, U, logits_out=logits)
+
+    def plan():
+        return plan_wave(logits[:, 1:B], 1.0, tiers, wts, anchors, row_budget=2048, row_cost_curve=SERVE_COST_CURVE)
+
+    def timed(fn, steps):
+        ev = make_events(2)
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        ev[0].record()
+        for _ in range(steps):
+            fn()
+        ev[1].record()
+        torch.cuda.synchronize()
+        return ev[0].elapsed_time(ev[1]) / steps
+
+    steps = max(3, args.steps)
+    launches0 = _lib.launch_count()
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        draft_ms = timed(draft, steps)
+        plan_ms = timed(plan, steps)
+        topk_ms = timed(lambda: proposal_topk(logits[:, 1:B], 1.0, 128), steps)
+        both_ms = timed(lambda: (draft(), plan()), steps)
+        launches = (_lib.launch_count() - launches0) / (4 * (steps + args.warmup))
+        lq, ids = proposal_topk(logits[:, 1:B], 1.0, 128)
+        trees_ms = timed(lambda: build_draft_trees(lq, ids, 128, tiers=tiers), steps)
+        trees = build_draft_trees(lq, ids, 128, tiers=tiers)
+        alloc_ms = timed(lambda: allocate_tree_budgets_device(wts, tiers, trees.utilities, row_budget=2048,
+                                                              row_cost_curve=SERVE_COST_CURVE), steps)
+        alloc = allocate_tree_budgets_device(wts, tiers, trees.utilities, row_budget=2048,
+                                             row_cost_curve=SERVE_COST_CURVE)
+        pack_ms = timed(lambda: pack_tree_wave(trees, alloc, anchors, 2048), steps)
+    p = plan()
+    torch.cuda.synchronize()
+    if int(drafter.status.item()) != 0 or int(p.status.item()) != 0:
+        raise RuntimeError(f"drafter status {int(drafter.status.item())}, plan status {int(p.status.item())}")
+    s = shape
+    qkvo = H * (s.num_q_heads + 2 * s.num_kv_heads) * s.head_dim + s.num_q_heads * s.head_dim * H
+    per_layer = qkvo + 3 * H * s.intermediate
+    Q = R * B
+    gemm_flops = 2 * (Q * s.num_layers * per_layer + U * (s.num_feature_layers * H * H +
+                      s.num_layers * 2 * s.num_kv_heads * s.head_dim * H) + Q * H * V)
+    keys = float(((prefix + upd + B) * B).sum())
+    attn_flops = 4 * s.num_q_heads * s.head_dim * s.num_layers * keys
+    flops = gemm_flops + attn_flops
+    hbm, _, tf_sustained, peak_kind = peaks()
+    topk_bytes = R * (B - 1) * V * 2
+    result = {
+        "workload": "DFlash drafter (Qwen3-8B shape, 5 layers, block 16) over 64 requests, draft caches "
+                    "U[1024,4096] + 1-4 new context rows, then top-128 proposals x 15 depths, 128-node trees, "
+                    "tiers {16,32,64,128}, 2048-row knapsack, packed wave",
+        "draft_ms": draft_ms, "plan_ms": plan_ms, "draft_plus_plan_ms": both_ms,
+        "plan_parts_ms": {"proposal_topk": topk_ms, "trees": trees_ms, "allocate": alloc_ms, "pack": pack_ms},
+        "draft_pass": {"tflop": flops / 1e12, "achieved_tflops": flops / (draft_ms * 1e-3) / 1e12,
+                       "frac_of_sustained": flops / (draft_ms * 1e-3) / 1e12 / tf_sustained,
+                       "peak": f"{tf_sustained} TFLOP/s sustained bf16 ({peak_kind})"},
+        "proposal_topk": {"algorithmic_gb": topk_bytes / 1e9,
+                          "achieved_gbs": topk_bytes / (topk_ms * 1e-3) / 1e9,
+                          "frac_of_hbm": topk_bytes / (topk_ms * 1e-3) / 1e9 / hbm,
+                          "peak": f"{hbm} GB/s ({peak_kind})"},
+        "gpu_launches_per_call": launches, "clocks": clocks.summary()}
+    drafter.close()
+    del drafter, dw
+    torch.cuda.empty_cache()
+    return result
 
 
 def nested_configs(args, world, rank):
@@ -902,7 +1011,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="verify", choices=["verify", "verify4b", "accept"])
+    ap.add_argument("--workload", default="verify", choices=["verify", "verify4b", "accept", "draft"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-nested", action="store_true", help="skip the nested configuration-2/3/5 blocks")
     ap.add_argument("--serve-requests", type=int, default=256, help="configuration-5 request count")
@@ -924,6 +1033,13 @@ def main():
             line = run_reference(args, world, rank)
         elif args.workload == "accept":
             line = run_accept(args, world, rank)
+        elif args.workload == "draft":
+            # the nested drafter + wave-plan block alone (development runs)
+            from specgrove_b200.engine import QWEN3_8B, ModelShape, Weights
+            s = QWEN3_8B
+            target = Weights.random(ModelShape(1, s.hidden, s.num_q_heads, s.num_kv_heads, s.head_dim,
+                                               s.intermediate, s.vocab), seed=1234)
+            line = {"workload": "draft", "draft": measure_draft(args, world, rank, target)}
         else:
             line = run_verify(args, world, rank)
         if rank == 0 and line is not None:

@@ -112,7 +112,7 @@ __device__ int select_digit(const uint32_t* hist, int& need, int* scratch) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kTopkThreads) proposal_topk_kernel(const T* __restrict__ logits,
+__global__ void __launch_bounds__(kTopkThreads, 2) proposal_topk_kernel(const T* __restrict__ logits,
                                                                      int64_t row_stride, int rows_per_group,
                                                                      int64_t group_stride, int vocab, int k,
                                                                      double inv_t, double* __restrict__ log_q,
@@ -147,15 +147,26 @@ __global__ void __launch_bounds__(kTopkThreads) proposal_topk_kernel(const T* __
     const int shift = kKeyBits - 8 * (digit + 1);
     for (int i = tid; i < 256; i += kTopkThreads) hist[i] = 0u;
     __syncthreads();
-    for (int i = tid; i < vocab; i += kTopkThreads) {
-      const T v = x[i];
+    // whole warps iterate together so that equal bins of a warp can be
+    // counted with one shared-memory atomic (a row's leading digits fall in
+    // a handful of bins: per-element atomics would serialise on them)
+    for (int base = 0; base < vocab; base += kTopkThreads) {
+      const int i = base + tid;
+      const bool in = i < vocab;
+      const T v = in ? x[i] : T{};
       const uint32_t key = order_key(v);
-      if (digit == 0) {
+      if (in && digit == 0) {
         my_max = max(my_max, key);
         bad |= !finite_value(v);
       }
-      if (digit == 1) my_sum += exp_nonpositive((to_double(v) - lmax) * inv_t, exp_table);
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      if (in && digit == 1) my_sum += exp_nonpositive((to_double(v) - lmax) * inv_t, exp_table);
+      const bool counted = in && (key & mask) == prefix;
+      const unsigned active = __ballot_sync(0xffffffffu, counted);
+      if (counted) {
+        const uint32_t bin = (key >> shift) & 255u;
+        const unsigned same = __match_any_sync(active, bin);
+        if (lane == __ffs(same) - 1) atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(same)));
+      }
     }
     if (digit == 0) {
       // row maximum (the largest key) for the normaliser pass
