@@ -634,6 +634,7 @@ def measure_draft(args, world, rank, weights):
         return plan_wave(logits[:, 1:B], 1.0, tiers, wts, anchors, row_budget=2048, row_cost_curve=SERVE_COST_CURVE)
 
     def timed(fn, steps):
+        """Eager calls: host enqueue included (Python, ctypes, allocations)."""
         ev = make_events(2)
         for _ in range(args.warmup):
             fn()
@@ -645,22 +646,47 @@ def measure_draft(args, world, rank, weights):
         torch.cuda.synchronize()
         return ev[0].elapsed_time(ev[1]) / steps
 
+    def graphed(fn, steps):
+        """The calls captured once in a CUDA graph and replayed: device time
+        of the kernels, without the host's per-call enqueue work."""
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(args.warmup):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        for _ in range(args.warmup):
+            graph.replay()
+        ev = make_events(2)
+        ev[0].record()
+        for _ in range(steps):
+            graph.replay()
+        ev[1].record()
+        torch.cuda.synchronize()
+        del graph
+        return ev[0].elapsed_time(ev[1]) / steps
+
     steps = max(3, args.steps)
     launches0 = _lib.launch_count()
+    lq, ids = proposal_topk(logits[:, 1:B], 1.0, 128)
+    trees = build_draft_trees(lq, ids, 128, tiers=tiers)
+    alloc = allocate_tree_budgets_device(wts, tiers, trees.utilities, row_budget=2048,
+                                         row_cost_curve=SERVE_COST_CURVE)
     with ClockSampler(torch.cuda.current_device()) as clocks:
-        draft_ms = timed(draft, steps)
-        plan_ms = timed(plan, steps)
-        topk_ms = timed(lambda: proposal_topk(logits[:, 1:B], 1.0, 128), steps)
-        both_ms = timed(lambda: (draft(), plan()), steps)
-        launches = (_lib.launch_count() - launches0) / (4 * (steps + args.warmup))
-        lq, ids = proposal_topk(logits[:, 1:B], 1.0, 128)
-        trees_ms = timed(lambda: build_draft_trees(lq, ids, 128, tiers=tiers), steps)
-        trees = build_draft_trees(lq, ids, 128, tiers=tiers)
-        alloc_ms = timed(lambda: allocate_tree_budgets_device(wts, tiers, trees.utilities, row_budget=2048,
-                                                              row_cost_curve=SERVE_COST_CURVE), steps)
-        alloc = allocate_tree_budgets_device(wts, tiers, trees.utilities, row_budget=2048,
-                                             row_cost_curve=SERVE_COST_CURVE)
-        pack_ms = timed(lambda: pack_tree_wave(trees, alloc, anchors, 2048), steps)
+        draft_ms = graphed(draft, steps)
+        plan_ms = graphed(plan, steps)
+        both_ms = graphed(lambda: (draft(), plan()), steps)
+        eager_ms = timed(lambda: (draft(), plan()), steps)
+        launches = (_lib.launch_count() - launches0) / (4 * (steps + args.warmup) + 3)
+        topk_ms = graphed(lambda: proposal_topk(logits[:, 1:B], 1.0, 128), steps)
+        trees_ms = graphed(lambda: build_draft_trees(lq, ids, 128, tiers=tiers), steps)
+        alloc_ms = graphed(lambda: allocate_tree_budgets_device(wts, tiers, trees.utilities, row_budget=2048,
+                                                                row_cost_curve=SERVE_COST_CURVE), steps)
+        pack_ms = graphed(lambda: pack_tree_wave(trees, alloc, anchors, 2048), steps)
     p = plan()
     torch.cuda.synchronize()
     if int(drafter.status.item()) != 0 or int(p.status.item()) != 0:
@@ -680,7 +706,10 @@ def measure_draft(args, world, rank, weights):
         "workload": "DFlash drafter (Qwen3-8B shape, 5 layers, block 16) over 64 requests, draft caches "
                     "U[1024,4096] + 1-4 new context rows, then top-128 proposals x 15 depths, 128-node trees, "
                     "tiers {16,32,64,128}, 2048-row knapsack, packed wave",
+        "timing": "CUDA-graph replays (device time); eager_draft_plus_plan_ms: the same calls enqueued from "
+                  "Python each step",
         "draft_ms": draft_ms, "plan_ms": plan_ms, "draft_plus_plan_ms": both_ms,
+        "eager_draft_plus_plan_ms": eager_ms,
         "plan_parts_ms": {"proposal_topk": topk_ms, "trees": trees_ms, "allocate": alloc_ms, "pack": pack_ms},
         "draft_pass": {"tflop": flops / 1e12, "achieved_tflops": flops / (draft_ms * 1e-3) / 1e12,
                        "frac_of_sustained": flops / (draft_ms * 1e-3) / 1e12 / tf_sustained,

@@ -213,7 +213,7 @@ SG_API int sg_allocate_tiers(int32_t num_requests, const double* weights, int32_
  * produced (sg_build_draft_trees), so a wave is planned without a host round
  * trip.  weights, utilities and allocation are DEVICE pointers (8-, 8-, 4-byte
  * aligned); options and the cost curve are host arrays, checked on the host
- * like sg_allocate_tiers.  At most 8 options, row_budget <= 8192, 64 curve
+ * like sg_allocate_tiers.  At most 8 options, row_budget <= 4096, 64 curve
  * points (SG_ERR_UNSUPPORTED otherwise).  workspace: device, 4-byte aligned,
  * sg_allocate_tiers_device_workspace_bytes(num_requests, row_budget) bytes
  * (per step and row total: the back pointer).  A weight or utility out of

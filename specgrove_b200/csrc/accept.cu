@@ -614,8 +614,9 @@ __global__ void follow_kernel(const int64_t* __restrict__ posterior, const int64
 template <int CLUSTER, bool BULK>
 int launch_accept(const AcceptParams& p, size_t smem, cudaStream_t stream) {
   auto kernel = accept_probs_kernel<CLUSTER, BULK>;
-  SG_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(smem)));
+  static std::atomic<int> limits[kMaxDevices];
+  const int st = ensure_dynamic_smem(kernel, smem, limits);
+  if (st != SG_OK) return st;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.num_trees) * CLUSTER, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);

@@ -300,7 +300,9 @@ __global__ void __launch_bounds__(kLThreads) accept_logits_kernel(const LogitsPa
 template <int C, typename T>
 int launch_logits(const LogitsParams& p, size_t smem, cudaStream_t s) {
   auto kernel = accept_logits_kernel<C, T>;
-  SG_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  static std::atomic<int> limits[kMaxDevices];
+  const int st = ensure_dynamic_smem(kernel, smem, limits);
+  if (st != SG_OK) return st;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.num_trees) * C, 1, 1);
   cfg.blockDim = dim3(kLThreads, 1, 1);

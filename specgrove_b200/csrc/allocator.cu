@@ -16,6 +16,7 @@
 // The table holds, per request step and row total, the reward and a back
 // pointer (previous row total, option); allocations are rebuilt from back
 // pointers only to break exact ties.
+#include <climits>
 #include <cmath>
 #include <cstdio>
 #include <vector>
@@ -188,13 +189,18 @@ extern "C" int sg_allocate_tiers(int32_t num_requests, const double* weights, in
 // the order of each cell's smallest key.  Ranks are rebuilt every step from a
 // bitmap of those keys, so the device visits candidates in exactly the host's
 // order and applies the same fp64 comparisons: allocations are identical.
+// The lexicographic tie rule compares two allocations that end in the same
+// cell; every reached cell also keeps the lexicographic rank of its
+// allocation among the step's allocations (rank of the key lex(previous) * T
+// + option, rebuilt by the same bitmap count), so a tie is two comparisons of
+// ranks and options instead of a walk along the back pointers.
 // ---------------------------------------------------------------------------
 namespace sg {
 namespace {
 
-constexpr int kAllocThreads = 1024;
+constexpr int kAllocThreads = 512;
 constexpr int kAllocMaxOptions = 8;
-constexpr int kAllocMaxBudget = 8192;
+constexpr int kAllocMaxBudget = 4096;
 constexpr int kAllocMaxCurve = 64;
 
 struct DeviceProblem {
@@ -226,82 +232,55 @@ __device__ double device_wave_cost(const DeviceProblem& p, int rows) {
   return p.curve_cost[p.curve_points - 1];
 }
 
-// Is allocation a (the one ending at row total ra after `steps` requests,
-// then option ka) lexicographically smaller than b (rb, then kb)?  Walks
-// both back-pointer chains together; the last difference seen is the first
-// in request order.
-__device__ bool allocation_less(const DeviceProblem& p, int steps, int ra, int ka, int rb, int kb) {
-  int da = ka, db = kb;
-  bool differ = ka != kb;
-  for (int s = steps; s > 0 && ra != rb; --s) {
-    const int la = p.links[static_cast<size_t>(s) * (p.B + 1) + ra];
-    const int lb = p.links[static_cast<size_t>(s) * (p.B + 1) + rb];
-    if ((la & 7) != (lb & 7)) {
-      da = la & 7;
-      db = lb & 7;
-      differ = true;
-    }
-    ra = la >> 3;
-    rb = lb >> 3;
-  }
-  return differ && da < db;
-}
-
 __device__ __forceinline__ void alloc_report(const DeviceProblem& p, int code) {
   if (p.status != nullptr) atomicMax(p.status, code);
 }
 
-// Exclusive prefix sum of `count` ints in place (one CTA); returns the total.
-__device__ int block_exclusive_scan(int* v, int count, int* warp_sums) {
-  const int per = (count + kAllocThreads - 1) / kAllocThreads;
-  const int begin = min(count, static_cast<int>(threadIdx.x) * per), end = min(count, begin + per);
+// Warp 0 turns the key bitmap into per-word exclusive prefix counts
+// (word_base) and returns the total through *total (read after a barrier).
+__device__ void scan_bits(const uint32_t* bits, int key_words, int* word_base, int* total) {
+  const int lane = threadIdx.x & 31;
+  const int per = (key_words + 31) / 32;
+  const int begin = min(key_words, lane * per), end = min(key_words, begin + per);
   int local = 0;
-  for (int j = begin; j < end; ++j) local += v[j];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int j = begin; j < end; ++j) local += __popc(bits[j]);
   int incl = local;
   for (int o = 1; o < 32; o <<= 1) {
     const int t = __shfl_up_sync(0xffffffffu, incl, o);
     if (lane >= o) incl += t;
   }
-  if (lane == 31) warp_sums[warp] = incl;
-  __syncthreads();
-  if (warp == 0) {
-    int w = warp_sums[lane];
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(0xffffffffu, w, o);
-      if (lane >= o) w += t;
-    }
-    warp_sums[lane] = w;  // inclusive
-  }
-  __syncthreads();
-  int run = incl - local + (warp > 0 ? warp_sums[warp - 1] : 0);
-  const int total = warp_sums[31];
+  int run = incl - local;
   for (int j = begin; j < end; ++j) {
-    const int t = v[j];
-    v[j] = run;
-    run += t;
+    word_base[j] = run;
+    run += __popc(bits[j]);
   }
-  __syncthreads();
-  return total;
+  if (lane == 31) *total = incl;
 }
 
+template <int TT>
 __global__ void __launch_bounds__(kAllocThreads) allocate_tiers_kernel(const DeviceProblem p) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int cells = p.B + 1;
-  double* reward = reinterpret_cast<double*>(smem);           // [2][cells]
-  int* rank = reinterpret_cast<int*>(reward + 2 * cells);     // [2][cells]
-  const int key_words = (cells * p.T + 31) / 32;
-  uint32_t* bits = reinterpret_cast<uint32_t*>(rank + 2 * cells);  // [key_words]
-  int* word_base = reinterpret_cast<int*>(bits + key_words);       // [key_words]
-  __shared__ int warp_sums[32];
+  constexpr int T = TT;  // options (a template parameter: exact unrolling)
+  double* reward = reinterpret_cast<double*>(smem);                // [2][cells]
+  int* rank = reinterpret_cast<int*>(reward + 2 * cells);          // [2][cells] first-reached rank
+  int* lex = rank + 2 * cells;                                     // [2][cells] lexicographic rank
+  const int key_words = (cells * T + 31) / 32;
+  uint32_t* bits = reinterpret_cast<uint32_t*>(lex + 2 * cells);   // [2][key_words] first-reached keys
+  uint32_t* lbits = bits + 2 * key_words;                          // [2][key_words] lexicographic keys
+  int* word_base = reinterpret_cast<int*>(lbits + 2 * key_words);  // [key_words]
+  int* lword_base = word_base + key_words;                         // [key_words]
+  __shared__ double earned_s[2][kAllocMaxOptions];
   __shared__ int bad;
+  __shared__ int reached;
+  __shared__ int lreached;
   __shared__ double best_ratio[32];
   __shared__ int best_rows[32];
   const int tid = threadIdx.x;
 
   if (tid == 0) bad = 0;
   __syncthreads();
-  for (int j = tid; j < p.R * p.T; j += kAllocThreads) {
+  for (int j = tid; j < p.R * T; j += kAllocThreads) {
     const double u = p.utilities[j];
     if (!isfinite(u) || u < 1.0) bad = 1;
   }
@@ -311,9 +290,12 @@ __global__ void __launch_bounds__(kAllocThreads) allocate_tiers_kernel(const Dev
   }
   for (int c = tid; c < cells; c += kAllocThreads) {
     rank[c] = c == 0 ? 0 : -1;
+    lex[c] = 0;
     reward[c] = 0.0;
     p.links[c] = c == 0 ? -1 : -2;
   }
+  for (int j = tid; j < 4 * key_words; j += kAllocThreads) bits[j] = 0u;
+  if (tid < T) earned_s[0][tid] = p.weights[0] * p.utilities[tid];
   __syncthreads();
   if (bad) {
     alloc_report(p, SG_ERR_INVALID_ARGUMENT);
@@ -324,58 +306,100 @@ __global__ void __launch_bounds__(kAllocThreads) allocate_tiers_kernel(const Dev
   for (int i = 0; i < p.R; ++i) {
     const int* rank_prev = rank + cur * cells;
     int* rank_next = rank + (cur ^ 1) * cells;
+    const int* lex_prev = lex + cur * cells;
+    int* lex_next = lex + (cur ^ 1) * cells;
+    uint32_t* lbits_now = lbits + (i & 1) * key_words;
+    uint32_t* lbits_other = lbits + ((i & 1) ^ 1) * key_words;
     const double* reward_prev = reward + cur * cells;
     double* reward_next = reward + (cur ^ 1) * cells;
+    uint32_t* bits_now = bits + (i & 1) * key_words;
+    uint32_t* bits_other = bits + ((i & 1) ^ 1) * key_words;
     int32_t* links_next = p.links + static_cast<size_t>(i + 1) * cells;
-    double earned[kAllocMaxOptions];
-    for (int k = 0; k < p.T; ++k) earned[k] = p.weights[i] * p.utilities[static_cast<size_t>(i) * p.T + k];
-    for (int j = tid; j < key_words; j += kAllocThreads) bits[j] = 0u;
-    __syncthreads();
+    // the next step's earned rewards load while this step runs
+    if (tid < T && i + 1 < p.R)
+      earned_s[(i + 1) & 1][tid] = p.weights[i + 1] * p.utilities[static_cast<size_t>(i + 1) * T + tid];
+    double earned[T];
+    int opts[T];
+#pragma unroll
+    for (int k = 0; k < T; ++k) {
+      earned[k] = earned_s[i & 1][k];
+      opts[k] = p.options[k];
+    }
+    // the other bitmap was read by the previous step's rank conversion,
+    // which ended with a barrier: clear it for the next step
+    for (int j = tid; j < key_words; j += kAllocThreads) {
+      bits_other[j] = 0u;
+      lbits_other[j] = 0u;
+    }
     for (int c = tid; c < cells; c += kAllocThreads) {
-      // candidates (key, previous row total, option), in key order
-      int keys[kAllocMaxOptions], used[kAllocMaxOptions], opt[kAllocMaxOptions];
-      int n = 0;
-      for (int k = 0; k < p.T; ++k) {
-        const int u = c - p.options[k] - 1;
-        if (u < 0 || rank_prev[u] < 0) continue;
-        const int key = rank_prev[u] * p.T + k;
-        int at = n++;
-        while (at > 0 && keys[at - 1] > key) {
-          keys[at] = keys[at - 1];
-          used[at] = used[at - 1];
-          opt[at] = opt[at - 1];
-          --at;
-        }
-        keys[at] = key;
-        used[at] = u;
-        opt[at] = k;
+      // candidate k: previous row total c - options[k] - 1, key rank * T + k
+      int key[T];
+#pragma unroll
+      for (int k = 0; k < T; ++k) {
+        const int u = c - opts[k] - 1;
+        key[k] = (u >= 0 && rank_prev[u] >= 0) ? rank_prev[u] * T + k : INT_MAX;
       }
-      if (n == 0) {
+      // visit candidates in increasing key order (the host's order)
+      double best = 0.0;
+      int best_used = -1, best_opt = -1, first_key = INT_MAX;
+      unsigned done = 0u;
+#pragma unroll
+      for (int step = 0; step < T; ++step) {
+        int kmin = -1, vmin = INT_MAX;
+#pragma unroll
+        for (int k = 0; k < T; ++k)
+          if (!((done >> k) & 1u) && key[k] < vmin) {
+            vmin = key[k];
+            kmin = k;
+          }
+        if (kmin < 0) break;
+        done |= 1u << kmin;
+        int u = 0;
+        double e = 0.0;
+#pragma unroll
+        for (int k = 0; k < T; ++k)
+          if (k == kmin) {
+            u = c - opts[k] - 1;
+            e = earned[k];
+          }
+        const double r = reward_prev[u] + e;
+        if (best_used < 0) {
+          best = r;
+          best_used = u;
+          best_opt = kmin;
+          first_key = vmin;
+          continue;
+        }
+        bool take = r > best + 1e-12;
+        if (!take && fabs(r - best) <= 1e-12) {
+          // lexicographic order of (allocation of u, kmin) and (allocation
+          // of best_used, best_opt): the prefixes' ranks, then the options
+          const int la = lex_prev[u], lb = lex_prev[best_used];
+          take = la < lb || (la == lb && kmin < best_opt);
+        }
+        if (take) {
+          best = r;
+          best_used = u;
+          best_opt = kmin;
+        }
+      }
+      if (best_used < 0) {
         rank_next[c] = -1;
         links_next[c] = -2;
         continue;
       }
-      double best = reward_prev[used[0]] + earned[opt[0]];
-      int best_used = used[0], best_opt = opt[0];
-      for (int j = 1; j < n; ++j) {
-        const double r = reward_prev[used[j]] + earned[opt[j]];
-        bool take = r > best + 1e-12;
-        if (!take && fabs(r - best) <= 1e-12) take = allocation_less(p, i, used[j], opt[j], best_used, best_opt);
-        if (take) {
-          best = r;
-          best_used = used[j];
-          best_opt = opt[j];
-        }
-      }
       reward_next[c] = best;
       links_next[c] = best_used * 8 + best_opt;
-      rank_next[c] = keys[0];  // first-reached key; turned into a rank below
-      atomicOr(&bits[keys[0] >> 5], 1u << (keys[0] & 31));
+      rank_next[c] = first_key;  // first-reached key; turned into a rank below
+      atomicOr(&bits_now[first_key >> 5], 1u << (first_key & 31));
+      const int lkey = lex_prev[best_used] * T + best_opt;  // unique per cell
+      lex_next[c] = lkey;
+      atomicOr(&lbits_now[lkey >> 5], 1u << (lkey & 31));
     }
     __syncthreads();
-    for (int j = tid; j < key_words; j += kAllocThreads) word_base[j] = __popc(bits[j]);
+    if (tid < 32) scan_bits(bits_now, key_words, word_base, &reached);
+    else if (tid < 64) scan_bits(lbits_now, key_words, lword_base, &lreached);
     __syncthreads();
-    const int reached = block_exclusive_scan(word_base, key_words, warp_sums);
     if (reached == 0) {
       alloc_report(p, SG_ERR_CAPACITY);
       for (int r = tid; r < p.R; r += kAllocThreads) p.allocation[r] = -1;
@@ -383,8 +407,11 @@ __global__ void __launch_bounds__(kAllocThreads) allocate_tiers_kernel(const Dev
     }
     for (int c = tid; c < cells; c += kAllocThreads) {
       const int key = rank_next[c];
-      if (key >= 0)
-        rank_next[c] = word_base[key >> 5] + __popc(bits[key >> 5] & ((1u << (key & 31)) - 1u));
+      if (key >= 0) {
+        rank_next[c] = word_base[key >> 5] + __popc(bits_now[key >> 5] & ((1u << (key & 31)) - 1u));
+        const int lkey = lex_next[c];
+        lex_next[c] = lword_base[lkey >> 5] + __popc(lbits_now[lkey >> 5] & ((1u << (lkey & 31)) - 1u));
+      }
     }
     __syncthreads();
     cur ^= 1;
@@ -437,7 +464,7 @@ __global__ void __launch_bounds__(kAllocThreads) allocate_tiers_kernel(const Dev
 size_t allocate_smem_bytes(int T, int B) {
   const size_t cells = static_cast<size_t>(B) + 1;
   const size_t key_words = (cells * T + 31) / 32;
-  return cells * 2 * sizeof(double) + cells * 2 * sizeof(int) + key_words * 8;
+  return cells * 2 * sizeof(double) + cells * 4 * sizeof(int) + key_words * 4 * 4 + key_words * 2 * 4;
 }
 
 }  // namespace
@@ -461,7 +488,7 @@ extern "C" int sg_allocate_tiers_device(int32_t num_requests, const double* weig
   int st = validate_shape(hp, "sg_allocate_tiers_device");
   if (st != SG_OK) return st;
   if (num_options > kAllocMaxOptions || row_budget > kAllocMaxBudget || curve_points > kAllocMaxCurve)
-    return fail(SG_ERR_UNSUPPORTED, "sg_allocate_tiers_device: at most 8 options, 8192 rows, 64 curve points");
+    return fail(SG_ERR_UNSUPPORTED, "sg_allocate_tiers_device: at most 8 options, 4096 rows, 64 curve points");
   const size_t need = sg_allocate_tiers_device_workspace_bytes(num_requests, row_budget);
   if (workspace == nullptr || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 3u) != 0) {
     set_error("sg_allocate_tiers_device: workspace of %zu bytes, %zu needed (4-byte aligned)", workspace_bytes, need);
@@ -487,8 +514,21 @@ extern "C" int sg_allocate_tiers_device(int32_t num_requests, const double* weig
   p.status = status;
   p.links = static_cast<int32_t*>(workspace);
   const size_t smem = allocate_smem_bytes(num_options, row_budget);
-  SG_CUDA_CHECK(cudaFuncSetAttribute(allocate_tiers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(smem)));
-  allocate_tiers_kernel<<<1, kAllocThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
-  return check_launch("allocate_tiers_kernel");
+  static std::atomic<int> limits[kAllocMaxOptions + 1][kMaxDevices];
+  auto run = [&](auto kernel) -> int {
+    const int s = ensure_dynamic_smem(kernel, smem, limits[num_options]);
+    if (s != SG_OK) return s;
+    kernel<<<1, kAllocThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
+    return check_launch("allocate_tiers_kernel");
+  };
+  switch (num_options) {
+    case 1: return run(allocate_tiers_kernel<1>);
+    case 2: return run(allocate_tiers_kernel<2>);
+    case 3: return run(allocate_tiers_kernel<3>);
+    case 4: return run(allocate_tiers_kernel<4>);
+    case 5: return run(allocate_tiers_kernel<5>);
+    case 6: return run(allocate_tiers_kernel<6>);
+    case 7: return run(allocate_tiers_kernel<7>);
+    default: return run(allocate_tiers_kernel<8>);
+  }
 }

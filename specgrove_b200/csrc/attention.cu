@@ -650,14 +650,9 @@ template <int D, int KST, int VST>
 int launch_tm(const CUtensorMap& map, const Params& p, int num_requests, cudaStream_t stream) {
   using L = TmLayout<D, KST, VST>;
   auto kernel = tree_attention_tm_kernel<D, KST, VST>;
-  static int configured = 0;
-  int dev = 0;
-  SG_CUDA_CHECK(cudaGetDevice(&dev));
-  if (!(configured & (1 << dev))) {
-    SG_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(L::SMEM)));
-    configured |= 1 << dev;
-  }
+  static std::atomic<int> limits[kMaxDevices];
+  const int st = ensure_dynamic_smem(kernel, L::SMEM, limits);
+  if (st != SG_OK) return st;
   if (p.items == nullptr || p.num_items == nullptr || p.work_counter == nullptr)
     return fail(SG_ERR_INVALID_ARGUMENT, "tree attention: missing work list");
   // One CTA per SM; every (request, kv head) has at least one item.

@@ -50,6 +50,24 @@ int device_sm_count();
 // (kernel attributes, static scratch addresses) handle.
 constexpr int kMaxDevices = 64;
 
+// Raises `kernel`'s dynamic shared-memory limit on the current device to at
+// least `bytes`, calling cudaFuncSetAttribute only when the recorded limit
+// (limits[device], one array per kernel) is lower; so repeated launches (and
+// launches inside CUDA graph capture) make no attribute call.
+template <typename Kernel>
+int ensure_dynamic_smem(Kernel kernel, size_t bytes, std::atomic<int>* limits) {
+  int dev = 0;
+  SG_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(SG_ERR_UNSUPPORTED, "device index beyond the per-device caches");
+  const int want = static_cast<int>(bytes);
+  if (limits[dev].load(std::memory_order_acquire) >= want) return SG_OK;
+  SG_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, want));
+  int cur = limits[dev].load(std::memory_order_relaxed);
+  while (cur < want && !limits[dev].compare_exchange_weak(cur, want, std::memory_order_acq_rel)) {
+  }
+  return SG_OK;
+}
+
 // ---------------------------------------------------------------------------
 // Programmatic dependent launch.  A kernel launched with launch_pdl may start
 // while the previous kernel in the stream is still finishing: it triggers its
