@@ -104,15 +104,18 @@ bool qkv_fused() {
   return fused;
 }
 
-// SG_NORM_FUSED=0 runs the input and post-attention RMSNorms as kernels
-// instead of folding them into the neighbouring GEMM epilogues (the residual
-// epilogue writes bf16(x * w) and per-tile sums of squares, the next GEMM
-// scales each row by rsqrt(mean(x^2) + eps)).  The folded form needs the
-// fused q/k/v epilogue.
+// SG_NORM_FUSED=1 folds the input and post-attention RMSNorms into the
+// neighbouring GEMM epilogues (the residual epilogue writes bf16(x * w) and
+// per-tile sums of squares, the next GEMM scales each row by
+// rsqrt(mean(x^2) + eps)) instead of running them as kernels.  Off by
+// default: it measured even on the 2048-row wave and 5% slower on the
+// 512-row wave, whose residual GEMMs run split over two CTAs per tile with
+// the heavier epilogue on the owner's critical path.  The folded form needs
+// the fused q/k/v epilogue.
 bool norm_fused() {
   static const bool fused = [] {
     const char* v = std::getenv("SG_NORM_FUSED");
-    return v == nullptr || v[0] != '0';
+    return v != nullptr && v[0] == '1';
   }();
   return fused && qkv_fused();
 }
