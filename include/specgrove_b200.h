@@ -475,6 +475,10 @@ typedef struct {
                                      anchor's, is not a proposal) */
   int64_t* lengths_out;           /* [R] cache_lengths + update rows */
   int32_t* status;                /* optional device status word */
+  int32_t context_only;           /* 1: only append the context rows' K/V
+                                     (prefill of the draft cache alongside the
+                                     target's prefill chunks); no block rows,
+                                     logits_out and anchor_tokens unused */
 } sg_draft_wave;
 
 /* Builds the drafter engine: TMA descriptors for the drafter's weights and

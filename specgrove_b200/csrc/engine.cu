@@ -730,11 +730,12 @@ extern "C" int sg_draft_pass(void* engine, const sg_draft_wave* wave, void* stre
   if (R < 1 || R > e->max_requests || static_cast<int64_t>(R) * B > e->max_rows || U < 0 ||
       U > d.desc.max_update_rows)
     return fail(SG_ERR_INVALID_ARGUMENT, "sg_draft_pass: sizes out of range");
+  const bool ctx_only = w.context_only != 0;
   if (w.slots == nullptr || w.cache_lengths == nullptr || w.update_offsets == nullptr ||
-      w.anchor_tokens == nullptr || w.logits_out == nullptr || (U > 0 && w.features == nullptr))
+      (!ctx_only && (w.anchor_tokens == nullptr || w.logits_out == nullptr)) || (U > 0 && w.features == nullptr))
     return fail(SG_ERR_INVALID_ARGUMENT, "sg_draft_pass: null wave array");
   if ((U > 0 && (reinterpret_cast<uintptr_t>(w.features) & 15u) != 0) ||
-      (reinterpret_cast<uintptr_t>(w.logits_out) & 15u) != 0)
+      (!ctx_only && (reinterpret_cast<uintptr_t>(w.logits_out) & 15u) != 0))
     return fail(SG_ERR_INVALID_ARGUMENT, "sg_draft_pass: features and logits_out must be 16-byte aligned");
   int dev = 0;
   SG_CUDA_CHECK(cudaGetDevice(&dev));
@@ -745,19 +746,19 @@ extern "C" int sg_draft_pass(void* engine, const sg_draft_wave* wave, void* stre
   int st;
   // context rows of a malformed request keep tree -1 (no arena row)
   if (U > 0) SG_CUDA_CHECK(cudaMemsetAsync(d.ctx_meta.tree, 0xFF, static_cast<size_t>(U) * 4, stream));
-  if ((st = layers::launch_draft_meta(w.update_offsets, w.cache_lengths, w.anchor_tokens, d.desc.mask_token_id, R, B,
-                                      U, e->meta, d.ctx_meta, d.block_offsets, d.prefix, d.block_tokens,
-                                      w.lengths_out, w.status, stream)) != SG_OK)
+  if ((st = layers::launch_draft_meta(w.update_offsets, w.cache_lengths, ctx_only ? w.slots : w.anchor_tokens,
+                                      d.desc.mask_token_id, R, B, U, e->meta, d.ctx_meta, d.block_offsets, d.prefix,
+                                      d.block_tokens, w.lengths_out, w.status, stream)) != SG_OK)
     return st;
   // block rows after the committed context, context rows at cache_len ..
-  if ((st = layers::launch_row_rope(e->meta, m.inv_freq, D, Q, w.slots, d.prefix, e->arena.capacity, plane_rows,
-                                    w.status, stream)) != SG_OK)
+  if (!ctx_only && (st = layers::launch_row_rope(e->meta, m.inv_freq, D, Q, w.slots, d.prefix, e->arena.capacity,
+                                                 plane_rows, w.status, stream)) != SG_OK)
     return st;
   if ((st = layers::launch_row_rope(d.ctx_meta, m.inv_freq, D, U, w.slots, w.cache_lengths, e->arena.capacity,
                                     plane_rows, w.status, stream)) != SG_OK)
     return st;
-  if ((st = layers::launch_embed(d.block_tokens, static_cast<const __nv_bfloat16*>(m.embed), m.vocab, H, Q, e->x,
-                                 w.status, stream)) != SG_OK)
+  if (!ctx_only && (st = layers::launch_embed(d.block_tokens, static_cast<const __nv_bfloat16*>(m.embed), m.vocab, H,
+                                              Q, e->x, w.status, stream)) != SG_OK)
     return st;
   if (U > 0) {
     // target_hidden = hidden_norm(fc(features))
@@ -773,6 +774,31 @@ extern "C" int sg_draft_pass(void* engine, const sg_draft_wave* wave, void* stre
     if ((st = layers::launch_rmsnorm(d.th32, static_cast<const __nv_bfloat16*>(d.desc.hidden_norm), H, U, m.rms_eps,
                                      d.th, stream)) != SG_OK)
       return st;
+  }
+  if (ctx_only) {
+    // the context rows' k|v in every layer (the block is not run)
+    if (U == 0) return SG_OK;
+    const int nkv = m.num_kv_heads;
+    const int64_t plane_stride = plane_rows * D;
+    __nv_bfloat16* arena = static_cast<__nv_bfloat16*>(e->arena.storage);
+    const gemm::Shape s_ctx = gemm::make_shape(U, 2 * nkv * D, H);
+    const gemm::SplitWorkspace* split = 2 * s_ctx.tiles <= e->sms ? &e->split : nullptr;
+    for (int l = 0; l < m.num_layers; ++l) {
+      __nv_bfloat16* k_plane0 = arena + static_cast<int64_t>(l) * 2 * nkv * plane_stride;
+      __nv_bfloat16* v_plane0 = k_plane0 + static_cast<int64_t>(nkv) * plane_stride;
+      const auto* kn = static_cast<const __nv_bfloat16*>(e->layer_ptrs[static_cast<size_t>(l) * W_COUNT + W_K_NORM]);
+      if (D == 128) {
+        gemm::EpiQkvPost<128>::Params pc{nullptr, 0, k_plane0, v_plane0, plane_stride, d.ctx_meta.arena_row,
+                                         d.ctx_meta.rope, kn, kn, 0, nkv, m.rms_eps, w.status, gemm::RowNorm{}};
+        st = gemm::launch<gemm::EpiQkvPost<128>>(d.th_map, d.kv_maps[l], s_ctx, pc, stream, split);
+      } else {
+        gemm::EpiQkvPost<64>::Params pc{nullptr, 0, k_plane0, v_plane0, plane_stride, d.ctx_meta.arena_row,
+                                        d.ctx_meta.rope, kn, kn, 0, nkv, m.rms_eps, w.status, gemm::RowNorm{}};
+        st = gemm::launch<gemm::EpiQkvPost<64>>(d.th_map, d.kv_maps[l], s_ctx, pc, stream, split);
+      }
+      if (st != SG_OK) return st;
+    }
+    return SG_OK;
   }
   StackArgs sa;
   sa.R = R;

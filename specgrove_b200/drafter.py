@@ -65,7 +65,7 @@ class _DraftWave(ctypes.Structure):
     _fields_ = [("num_requests", ctypes.c_int32), ("num_update_rows", ctypes.c_int32), ("slots", ctypes.c_void_p),
                 ("cache_lengths", ctypes.c_void_p), ("update_offsets", ctypes.c_void_p),
                 ("features", ctypes.c_void_p), ("anchor_tokens", ctypes.c_void_p), ("logits_out", ctypes.c_void_p),
-                ("lengths_out", ctypes.c_void_p), ("status", ctypes.c_void_p)]
+                ("lengths_out", ctypes.c_void_p), ("status", ctypes.c_void_p), ("context_only", ctypes.c_int32)]
 
 
 def _bind(lib):
@@ -207,9 +207,24 @@ class B200Drafter:
         wave = _DraftWave(R, int(num_update_rows), slots.data_ptr(), cache_lengths.data_ptr(),
                           update_offsets.data_ptr(), None if features is None else features.data_ptr(),
                           anchor_tokens.data_ptr(), logits_out.data_ptr(),
-                          None if lengths_out is None else lengths_out.data_ptr(), self.status.data_ptr())
+                          None if lengths_out is None else lengths_out.data_ptr(), self.status.data_ptr(), 0)
         check(self.lib.sg_draft_pass(self.handle, ctypes.byref(wave), _lib.stream_ptr(stream)), "sg_draft_pass")
         return logits_out
+
+    def append_context(self, slots: torch.Tensor, cache_lengths: torch.Tensor, update_offsets: torch.Tensor,
+                       features: torch.Tensor, num_update_rows: int, *, lengths_out: torch.Tensor | None = None,
+                       stream=None) -> None:
+        """Append context rows to the draft caches without running the block
+        (the draft cache's prefill, chunk by chunk with the target's)."""
+        if num_update_rows == 0:
+            return
+        if features.dtype != torch.bfloat16 or not features.is_contiguous():
+            raise ValueError("features must be contiguous bf16 [U, F * hidden]")
+        R = int(slots.shape[0])
+        wave = _DraftWave(R, int(num_update_rows), slots.data_ptr(), cache_lengths.data_ptr(),
+                          update_offsets.data_ptr(), features.data_ptr(), None, None,
+                          None if lengths_out is None else lengths_out.data_ptr(), self.status.data_ptr(), 1)
+        check(self.lib.sg_draft_pass(self.handle, ctypes.byref(wave), _lib.stream_ptr(stream)), "sg_draft_pass")
 
     def draft(self, slots: Sequence[int], features: Sequence[torch.Tensor], anchor_tokens: Sequence[int],
               stream=None) -> torch.Tensor:

