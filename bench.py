@@ -535,9 +535,15 @@ SERVE_COST_CURVE = [(16, 2.0), (256, 5.5), (512, 9.0), (1024, 17.5), (2048, 34.7
 
 def measure_serving(args, world, rank, weights=None):
     """Configuration 5: open-loop serving of the Qwen3-8B shape, requests
-    partitioned over the ranks, one verify pass per wave with the per-wave
-    NCCL allgather of allocator scores.  The makespan is the CUDA-event span
-    of the whole serving loop on each rank (max over ranks)."""
+    partitioned over the ranks, with the per-wave NCCL allgather of allocator
+    scores.  Default mode `spec`: the full speculative step (real chunked
+    prefill of each admitted prompt into the target's arena and the draft
+    cache, then per wave the DFlash drafter, the on-device wave plan and one
+    verify pass); mode `synthetic`: synthetic prompt KV and host-built trees,
+    one verify pass per wave.  The makespan is the CUDA-event span of the
+    whole serving loop on each rank (max over ranks)."""
+    if args.serve_mode == "spec":
+        return measure_serving_spec(args, world, rank, weights)
     from specgrove_b200 import _lib
     from specgrove_b200.allocator import ScoreExchange
     from specgrove_b200.engine import QWEN3_8B, B200Engine, Wave, Weights
@@ -593,6 +599,102 @@ def measure_serving(args, world, rank, weights=None):
             "collective": "per-wave NCCL all_gather_into_tensor of allocator scores + clock/load/done header"
                           if world > 1 else "none (one rank)",
             "gpu_launches": _lib.launch_count() - launches0, "clocks": clocks.summary()}
+
+
+def measure_serving_spec(args, world, rank, weights=None):
+    from specgrove_b200 import _lib
+    from specgrove_b200.allocator import ScoreExchange
+    from specgrove_b200.drafter import QWEN3_8B_DFLASH, QWEN3_8B_DFLASH_FEATURE_LAYERS, B200Drafter, DraftWeights
+    from specgrove_b200.engine import QWEN3_8B, B200Engine, Weights
+    from specgrove_b200.serving import SpecServer, make_prompts, make_requests
+    from specgrove_b200.speculative import SpecDecoder
+    shape = QWEN3_8B
+    weights = weights or Weights.random(shape, seed=1234)
+    dweights = DraftWeights.random(QWEN3_8B_DFLASH, weights, seed=4321)
+    tiers = [16, 32, 64, 128]
+    n_req, rate, max_new = args.serve_requests, 8.0 * world, 256
+    requests = make_requests(n_req, rate, (256, 8192), tiers, shape.vocab, seed=5)
+    prompts = make_prompts(requests, shape.vocab, seed=6)
+    slots = 64
+    capacity = 8192 + max_new + max(tiers) + 16
+    target = B200Engine(weights, num_slots=slots, capacity=capacity, max_rows=2048, max_requests=slots)
+    drafter = B200Drafter(dweights, num_slots=slots, capacity=capacity, max_requests=slots, max_update_rows=2048)
+    decoder = SpecDecoder(target, drafter, QWEN3_8B_DFLASH_FEATURE_LAYERS, tiers=[t - 1 for t in tiers],
+                          row_budget=2048, temperature=1.0, row_cost_curve=SERVE_COST_CURVE, seed=1_000_000 * rank)
+    exchange = ScoreExchange(slots, len(tiers), "cuda")
+    server = SpecServer(requests, decoder, prompts, rank=rank, world=world, exchange=exchange,
+                        num_tiers=len(tiers), max_new_tokens=max_new)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = _lib.launch_count()
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        start.record()
+        stats = server.run()
+        stop.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    span_ms = start.elapsed_time(stop)
+    makespan = max_over_ranks(span_ms, world)
+    tokens = sum_over_ranks(stats.tokens, world)
+    waves = max_over_ranks(stats.waves, world)
+    lat = sorted(stats.finish_times)
+    prompt_tokens = sum(r.prompt_len for r in requests if r.rank == rank)
+    target.close()
+    drafter.close()
+    del target, drafter, decoder
+    torch.cuda.empty_cache()
+    return {"workload": f"config5: Qwen3-8B shape + DFlash drafter (5 layers, block 16), {n_req} requests, Poisson "
+                        f"{8.0:g} req/s per GPU, prompts log-uniform [256, 8192] (random tokens, prefilled into the "
+                        f"target arena and the draft cache on admission), {max_new} tokens each, tiers "
+                        "{16,32,64,128}, service weights U{1,2,4}, 2048-row budget per GPU, least-loaded admission; "
+                        "each wave = drafter + on-device plan + verify",
+            "mode": "spec", "metric": METRIC, "value": tokens / (makespan / 1000.0), "unit": UNIT, "n_gpus": world,
+            "makespan_ms": makespan, "tokens": tokens, "waves_max_rank": waves,
+            "prompt_tokens_rank0": prompt_tokens, "decoder_steps_rank0": stats.waves,
+            "rows_committed_rank0": stats.rows, "rows_per_wave_rank0": stats.rows_verified / max(1, stats.waves),
+            "prefill_ms_rank0": stats.admit_ms, "step_ms_rank0": stats.step_ms,
+            "step_ms_per_wave_rank0": stats.step_ms / max(1, stats.waves), "host_ms_rank0": stats.host_ms,
+            "requests_rank0": stats.requests, "exchanges": stats.exchanges,
+            "latency_s_rank0": {"p50": lat[len(lat) // 2] if lat else None, "max": lat[-1] if lat else None},
+            "collective": "per-wave NCCL all_gather_into_tensor of allocator scores + clock/load/done header"
+                          if world > 1 else "none (one rank)",
+            "gpu_launches": _lib.launch_count() - launches0, "clocks": clocks.summary()}
+
+
+def measure_plan(args):
+    """The on-device wave plan alone (a small, profiler-sized case): 64
+    requests x 15 draft positions x the Qwen3 vocabulary of N(0, 2.5^2) bf16
+    logits, top-128 proposals, 128-node trees, tiers {16, 32, 64, 128}, the
+    2048-row knapsack on the serving cost curve and the packed wave."""
+    from specgrove_b200 import _lib
+    from specgrove_b200.draft_tree import plan_wave
+    R, D, V = 64, 15, 151936
+    g = torch.Generator(device="cuda").manual_seed(17)
+    logits = (torch.randn((R, D, V), generator=g, device="cuda") * 2.5).to(torch.bfloat16)
+    anchors = torch.randint(0, V, (R,), generator=g, device="cuda")
+    wts = 1.0 + torch.rand(R, generator=g, device="cuda", dtype=torch.float64)
+    tiers = [16, 32, 64, 128]
+
+    def once():
+        return plan_wave(logits, 1.0, tiers, wts, anchors, row_budget=2048, row_cost_curve=SERVE_COST_CURVE)
+
+    for _ in range(args.warmup):
+        once()
+    torch.cuda.synchronize()
+    launches0 = _lib.launch_count()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        plan = once()
+    stop.record()
+    torch.cuda.synchronize()
+    if int(plan.status.max()) != 0:
+        raise RuntimeError(f"plan status {plan.status.tolist()}")
+    return {"workload": "plan: 64 requests x 15 positions x 151936 vocab (bf16 N(0, 2.5^2)), top-128, 128-node "
+                        "trees, tiers {16,32,64,128}, 2048-row knapsack, packed wave",
+            "ms_per_plan_eager": start.elapsed_time(stop) / args.steps, "steps": args.steps,
+            "gpu_launches": _lib.launch_count() - launches0, "rows": int(plan.row_offsets[-1])}
 
 
 def measure_draft(args, world, rank, weights):
@@ -1040,10 +1142,12 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--workload", default="verify", choices=["verify", "verify4b", "accept", "draft"])
+    ap.add_argument("--workload", default="verify", choices=["verify", "verify4b", "accept", "draft", "serve", "plan"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-nested", action="store_true", help="skip the nested configuration-2/3/5 blocks")
     ap.add_argument("--serve-requests", type=int, default=256, help="configuration-5 request count")
+    ap.add_argument("--serve-mode", default="spec", choices=["spec", "synthetic"],
+                    help="configuration 5: full speculative step with real prefill, or synthetic KV + host trees")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: build the model with this many layers (not a benchmark number)")
     args = ap.parse_args()
@@ -1069,6 +1173,11 @@ def main():
             target = Weights.random(ModelShape(1, s.hidden, s.num_q_heads, s.num_kv_heads, s.head_dim,
                                                s.intermediate, s.vocab), seed=1234)
             line = {"workload": "draft", "draft": measure_draft(args, world, rank, target)}
+        elif args.workload == "plan":
+            line = measure_plan(args)
+        elif args.workload == "serve":
+            # the nested configuration-5 block alone (development runs)
+            line = {"workload": "serve", "config5": measure_serving(args, world, rank)}
         else:
             line = run_verify(args, world, rank)
         if rank == 0 and line is not None:

@@ -26,6 +26,13 @@ across one process per GPU:
   plus the bonus token each wave); the loop ends when every rank is done and
   every arrival has been assigned.  All ranks take the same number of
   exchanges.
+
+``SpecServer`` runs the same loop on the full speculative step
+(``speculative.SpecDecoder``): an admitted request's prompt is prefilled into
+the target's arena and the draft cache (real prefill, not synthetic KV), and
+every wave is one drafter pass, the on-device wave plan (trees, tier
+knapsack with the critical-path weights of the global terms) and one verify
+pass.
 """
 from __future__ import annotations
 
@@ -91,6 +98,9 @@ class ServeStats:
     requests: int = 0
     exchanges: int = 0
     host_ms: float = 0.0
+    admit_ms: float = 0.0          # SpecServer: prefill of admitted prompts (host clock; the call synchronizes)
+    step_ms: float = 0.0           # SpecServer: speculative steps (host clock; the call synchronizes)
+    rows_verified: int = 0         # SpecServer: rows of the verify waves
     finish_times: list = field(default_factory=list)
 
 
@@ -193,4 +203,108 @@ class OpenLoopServer:
             active = still
             wave += 1
             stats.host_ms += (self.clock() - h1) * 1000
+        return stats
+
+
+def make_prompts(requests: Sequence[ServeRequest], vocab: int, seed: int = 0) -> dict[int, list[int]]:
+    """Seeded random prompt tokens of each request's prompt length."""
+    g = torch.Generator().manual_seed(seed)
+    return {r.rid: torch.randint(0, vocab, (r.prompt_len,), generator=g).tolist() for r in requests}
+
+
+class SpecServer:
+    """One rank's open-loop serving loop over a ``SpecDecoder`` (the decoder
+    owns the arena slots; a queued request is admitted when one is free)."""
+
+    def __init__(self, requests: Sequence[ServeRequest], decoder, prompts: dict, *, rank: int, world: int,
+                 exchange: ScoreExchange, num_tiers: int, max_new_tokens: int, criticality_weight: float = 1.0,
+                 clock: Callable = time.perf_counter, idle_sleep_s: float = 5e-4, max_admit_per_wave: int = 8):
+        self.requests = sorted(requests, key=lambda r: r.arrival)
+        self.decoder = decoder
+        self.prompts = prompts
+        self.rank, self.world = rank, world
+        self.exchange = exchange
+        self.num_tiers = num_tiers
+        self.max_new = max_new_tokens
+        self.criticality = criticality_weight
+        self.clock = clock
+        self.idle_sleep_s = idle_sleep_s
+        self.max_admit = max_admit_per_wave
+
+    def run(self) -> ServeStats:
+        from .speculative import SpecRequest
+        stats = ServeStats()
+        t0 = self.clock()
+        active: list[tuple[ServeRequest, SpecRequest]] = []
+        queue: list[ServeRequest] = []
+        assigned = 0
+        wave = 0
+        while True:
+            h0 = self.clock()
+            now = h0 - t0
+            scores = RequestScores(progress=[len(s.generated) for _, s in active],
+                                   ages=[wave - r.admitted_wave for r, _ in active],
+                                   service_weights=[r.service_weight for r, _ in active],
+                                   utilities=[[1.0] * self.num_tiers for _ in active])
+            done = not active and not queue
+            self.exchange.pack(scores, header=[now, len(active) + len(queue), 1.0 if done else 0.0])
+            g = self.exchange.exchange().cpu()
+            stats.exchanges += 1
+            if bool((g[:, 0, 3] > 0).all()) and assigned == len(self.requests):
+                break
+            gclock = float(g[:, 0, 1].max())
+            loads = g[:, 0, 2].tolist()
+            while assigned < len(self.requests) and self.requests[assigned].arrival <= gclock:
+                r = self.requests[assigned]
+                r.rank = min(range(self.world), key=lambda k: (loads[k], k))
+                loads[r.rank] += 1
+                if r.rank == self.rank:
+                    queue.append(r)
+                assigned += 1
+            admit = []
+            while queue and len(self.decoder.free_slots) > len(admit) and len(admit) < self.max_admit:
+                r = queue.pop(0)
+                r.admitted_wave = wave
+                admit.append((r, SpecRequest(r.rid, self.prompts[r.rid], self.max_new,
+                                             weight=r.service_weight)))
+            stats.host_ms += (self.clock() - h0) * 1000
+            if admit:
+                a0 = self.clock()
+                self.decoder.admit([s for _, s in admit])
+                stats.admit_ms += (self.clock() - a0) * 1000
+                for r, s in admit:
+                    r.slot = s.slot
+                    r.generated = len(s.generated)
+                    stats.tokens += len(s.generated)
+                active.extend(admit)
+            if not active:
+                time.sleep(self.idle_sleep_s)
+                continue
+            h1 = self.clock()
+            lead, oldest = ScoreExchange.global_terms(g)
+            weights = critical_path_weights([len(s.generated) for _, s in active],
+                                            [wave - r.admitted_wave for r, _ in active], self.criticality,
+                                            self.max_new, max(lead, 0), max(oldest, 1))
+            for (r, s), w in zip(active, weights):
+                s.weight = w * r.service_weight
+            stats.host_ms += (self.clock() - h1) * 1000
+            rows_before = sum(self.decoder.target.arena.lengths[s.slot] for _, s in active)
+            verified = self.decoder.rows_verified
+            s0 = self.clock()
+            stats.tokens += self.decoder.step()
+            stats.step_ms += (self.clock() - s0) * 1000
+            stats.rows_verified += self.decoder.rows_verified - verified
+            stats.rows += sum(self.decoder.target.arena.lengths[s.slot] for _, s in active) - rows_before
+            stats.waves += 1
+            still = []
+            for r, s in active:
+                r.generated = len(s.generated)
+                if s.done:
+                    r.finish = self.clock() - t0
+                    stats.finish_times.append(r.finish - r.arrival)
+                    stats.requests += 1
+                else:
+                    still.append((r, s))
+            active = still
+            wave += 1
         return stats

@@ -98,6 +98,7 @@ class SpecDecoder:
         self.free_slots = list(range(target.arena.num_slots))
         self.running: list[SpecRequest] = []
         self.steps = 0
+        self.rows_verified = 0
 
     # -------------------------------------------------------------- admission
     def admit(self, requests: Sequence[SpecRequest]) -> None:
@@ -108,8 +109,9 @@ class SpecDecoder:
         for r in requests:
             if not self.free_slots:
                 raise RuntimeError("no free slot")
-            if len(r.prompt) + r.max_new_tokens + t.max_rows > t.arena.capacity:
-                raise ValueError("prompt + new tokens do not fit the slot capacity")
+            need = len(r.prompt) + r.max_new_tokens + max(self.tiers[-1] + 1, d.shape.block_size)
+            if need > min(t.arena.capacity, d.arena.capacity):
+                raise ValueError("prompt + new tokens + one tree do not fit the slot capacity")
             r.slot = self.free_slots.pop(0)
             t.arena.lengths[r.slot] = 0
             d.arena.lengths[r.slot] = 0
@@ -186,6 +188,7 @@ class SpecDecoder:
                          row_cost_curve=self.row_cost_curve)
         offsets = plan.row_offsets.cpu().tolist()
         Q = offsets[-1]
+        self.rows_verified += Q
         tlens = [t.arena.lengths[s] for s in slots]
         buf = torch.cat([plan.row_offsets, plan.parents[:Q], plan.tokens[:Q], slots_t, tlen_t, tlen_t, rid_t])
         wave = _PlannedWave(slots, tlens, offsets, self.tiers[-1] + 1, self.depth)

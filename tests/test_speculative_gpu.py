@@ -78,3 +78,23 @@ def test_first_token_is_the_prefill_draw():
     engine.verify_device(wave.to("cuda"), seed=5, temperature=1.0, commit=False, posterior=post)
     torch.cuda.synchronize()
     assert req.generated[0] == int(post[-1])
+
+
+def test_spec_server_serves_every_request():
+    """One rank's open-loop server on the speculative loop: every arrival is
+    admitted (real prefill), served to exactly max_new_tokens and releases its
+    slot; the score exchange runs once per loop iteration."""
+    from specgrove_b200.allocator import ScoreExchange
+    from specgrove_b200.serving import SpecServer, make_prompts, make_requests
+    dec = build(seed=9)
+    requests = make_requests(7, 2000.0, (16, 200), [4, 8], SHAPE.vocab, seed=4)
+    prompts = make_prompts(requests, SHAPE.vocab, seed=8)
+    server = SpecServer(requests, dec, prompts, rank=0, world=1, exchange=ScoreExchange(4, 2, "cuda"), num_tiers=2,
+                        max_new_tokens=24, max_admit_per_wave=3)
+    stats = server.run()
+    assert stats.requests == 7
+    assert stats.tokens == 7 * 24
+    assert all(r.generated == 24 and r.finish is not None for r in requests)
+    assert sorted(dec.free_slots) == [0, 1, 2, 3]
+    assert not dec.running
+    assert stats.exchanges >= stats.waves
