@@ -638,6 +638,9 @@ tree_attention_tm_kernel(const __grid_constant__ CUtensorMap kv_map, const Param
     }
     if (!ok) give_up();
   }
+  // Roles ran on one lane of warps 0-2: reconverge each warp before the CTA
+  // barrier that precedes freeing TMEM.
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

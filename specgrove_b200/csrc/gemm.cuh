@@ -20,6 +20,10 @@
 // adds the partials in k order (a fixed order, so results are reproducible),
 // then runs the fused epilogue and resets the flags.  All CTAs of the grid
 // (one per SM) are resident together, and every flag wait is bounded.
+// An owner segment always ends its CTA's run, so when its accumulator is
+// complete the operand ring is idle: the partials come into it by bulk copy
+// (half a tile of every contributor per round) and the owner adds them from
+// shared memory.
 #pragma once
 
 #include "sm100.cuh"
@@ -182,6 +186,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
   uint64_t* tempty = bars + 2 * STAGES + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* pbar = bars + 2 * STAGES + 5;  // stream-K partials -> operand ring
+  uint64_t* cbar = bars + 2 * STAGES + 6;  // the owner's 128 threads are done with a round of the ring
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -196,6 +202,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 128);
     }
+    mbar_init(pbar, 1);
+    mbar_init(cbar, 128);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tensormap(&tma_a);
@@ -334,25 +342,56 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
           }
           __threadfence();
           // acc += partials in k order, written back to TMEM for the epilogue.
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            float v[32];
-            tmem_ld32(taddr + c * 32, v);
-            for (int slot = 0; slot < g.ncontrib; ++slot) {
-              const float4* src = reinterpret_cast<const float4*>(
-                                      sp.partials + static_cast<size_t>(sk_tile * sp.max_slots + slot) * (BM * BN)) +
-                                  r;
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                const float4 pq = __ldcg(src + (c * 8 + q) * BM);
-                v[q * 4] += pq.x;
-                v[q * 4 + 1] += pq.y;
-                v[q * 4 + 2] += pq.z;
-                v[q * 4 + 3] += pq.w;
+          // Round h brings columns [128h, 128h + 128) of every contributor
+          // (quads 32h .. 32h + 31: 64 KB contiguous per partial) into the
+          // idle ring; thread 0 of the epilogue warps issues the copies.
+          constexpr uint32_t kHalf = BM * (BN / 2) * sizeof(float);
+          const float4* ring4 = reinterpret_cast<const float4*>(smem);
+          const bool issuer = threadIdx.x == 64;
+          for (int h = 0; h < 2 && ready; ++h) {
+            if (issuer) {
+              if (h > 0 && !mbar_wait(cbar, 0u)) {  // round 0 fully read
+                fail_wait();
+                ready = false;
+                break;
               }
+              if (h == 0) fence_proxy_async_global();  // the contributors' stores precede the bulk reads
+              mbar_arrive_expect_tx(pbar, static_cast<uint32_t>(g.ncontrib) * kHalf);
+              for (int slot = 0; slot < g.ncontrib; ++slot)
+                bulk_g2s(smem + slot * kHalf,
+                         reinterpret_cast<const uint8_t*>(sp.partials +
+                                                          static_cast<size_t>(sk_tile * sp.max_slots + slot) *
+                                                              (BM * BN)) +
+                             h * kHalf,
+                         kHalf, pbar);
             }
-            tmem_st32(taddr + c * 32, v);
+            if (!mbar_wait(pbar, static_cast<uint32_t>(h))) {
+              fail_wait();
+              ready = false;
+              break;
+            }
+#pragma unroll 1
+            for (int c = 0; c < BN / 64; ++c) {
+              float v[32];
+              const uint32_t col = static_cast<uint32_t>((h * (BN / 64) + c) * 32);
+              tmem_ld32(taddr + col, v);
+              for (int slot = 0; slot < g.ncontrib; ++slot) {
+                const float4* src = ring4 + slot * (kHalf / 16) + r;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                  const float4 pq = src[(c * 8 + q) * BM];
+                  v[q * 4] += pq.x;
+                  v[q * 4 + 1] += pq.y;
+                  v[q * 4 + 2] += pq.z;
+                  v[q * 4 + 3] += pq.w;
+                }
+              }
+              tmem_st32(taddr + col, v);
+            }
+            fence_proxy_async_smem();  // this thread's reads of the ring precede the next round's copies
+            mbar_arrive(cbar);
           }
+          if (!ready) break;
           tmem_wait_st();
           // Each owner thread counts itself past the flag (128 -> 256); the
           // last one resets it to 0 for the next launch, so no owner thread
@@ -370,6 +409,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       if (acc == 0) acc_phase ^= 1u;
     }
   }
+  // Roles ran on one lane of warps 0 and 1: reconverge each warp before the
+  // CTA barrier; warp 1 frees TMEM only once the epilogue warps have arrived.
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
