@@ -22,9 +22,36 @@
 #include "attention.cuh"
 #include "gemm.cuh"
 #include "layers.cuh"
+#include "lm_head.cuh"
 
 namespace sg {
 
+// SG_QKV_FUSED=0 runs the q/k norm + RoPE + KV write as its own kernel after
+// a plain q/k/v GEMM (the two forms compute the same values; the switch is
+// for A/B timing).
+bool qkv_fused() {
+  static const bool fused = [] {
+    const char* v = std::getenv("SG_QKV_FUSED");
+    return v == nullptr || v[0] != '0';
+  }();
+  return fused;
+}
+
+// SG_NORM_FUSED=1 folds the input and post-attention RMSNorms into the
+// neighbouring GEMM epilogues (the residual epilogue writes bf16(x * w) and
+// per-tile sums of squares, the next GEMM scales each row by
+// rsqrt(mean(x^2) + eps)) instead of running them as kernels.  Off by
+// default: it measured even on the 2048-row wave and 5% slower on the
+// 512-row wave, whose residual GEMMs run split over two CTAs per tile with
+// the heavier epilogue on the owner's critical path.  The folded form needs
+// the fused q/k/v epilogue.
+bool norm_fused() {
+  static const bool fused = [] {
+    const char* v = std::getenv("SG_NORM_FUSED");
+    return v != nullptr && v[0] == '1';
+  }();
+  return fused && qkv_fused();
+}
 
 namespace {
 
@@ -93,32 +120,6 @@ T* carve(uint8_t*& cursor, size_t count) {
   return reinterpret_cast<T*>(p);
 }
 
-// SG_QKV_FUSED=0 runs the q/k norm + RoPE + KV write as its own kernel after
-// a plain q/k/v GEMM (the two forms compute the same values; the switch is
-// for A/B timing).
-bool qkv_fused() {
-  static const bool fused = [] {
-    const char* v = std::getenv("SG_QKV_FUSED");
-    return v == nullptr || v[0] != '0';
-  }();
-  return fused;
-}
-
-// SG_NORM_FUSED=1 folds the input and post-attention RMSNorms into the
-// neighbouring GEMM epilogues (the residual epilogue writes bf16(x * w) and
-// per-tile sums of squares, the next GEMM scales each row by
-// rsqrt(mean(x^2) + eps)) instead of running them as kernels.  Off by
-// default: it measured even on the 2048-row wave and 5% slower on the
-// 512-row wave, whose residual GEMMs run split over two CTAs per tile with
-// the heavier epilogue on the owner's critical path.  The folded form needs
-// the fused q/k/v epilogue.
-bool norm_fused() {
-  static const bool fused = [] {
-    const char* v = std::getenv("SG_NORM_FUSED");
-    return v != nullptr && v[0] == '1';
-  }();
-  return fused && qkv_fused();
-}
 
 inline void trace(const sg_wave_desc& w, int point, cudaStream_t stream) {
   if (w.trace_events != nullptr && w.trace_events[point] != nullptr)

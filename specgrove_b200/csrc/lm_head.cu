@@ -60,11 +60,13 @@ int lm_head_run(const float* x, const void* final_norm, const void* lm_head, int
   float4* partials = reinterpret_cast<float4*>(static_cast<uint8_t*>(scratch) + 256 +
                                                align256(static_cast<size_t>(rows) * hidden * 2));
   const int tiles = (vocab + gemm::BN - 1) / gemm::BN;
-  // the final RMSNorm folded into the LM head (as in sg_verify_pass): xn =
-  // bf16(x * final_norm), each row's logits scaled by rsqrt(mean(x^2) + eps)
-  float* ssq = normed != nullptr ? nullptr
-                                 : reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(partials) +
-                                                            align256(static_cast<size_t>(rows) * tiles * 16));
+  // the final RMSNorm in the pass's form: a kernel writing normalised bf16
+  // rows, or (folded) xn = bf16(x * final_norm) with each row's logits scaled
+  // by rsqrt(mean(x^2) + eps)
+  const bool fold = normed == nullptr && norm_fused();
+  float* ssq = !fold ? nullptr
+                     : reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(partials) +
+                                                align256(static_cast<size_t>(rows) * tiles * 16));
   CUtensorMap a_map, b_map;
   int st;
   if ((st = make_tmap_2d_bf16(&a_map, xn, hidden, rows, static_cast<uint64_t>(hidden) * 2, gemm::BK, gemm::BM)) !=
@@ -77,8 +79,12 @@ int lm_head_run(const float* x, const void* final_norm, const void* lm_head, int
   // written earlier in this call (all rows x hidden normalised values, all
   // rows x tiles partials).
   SG_CUDA_CHECK(cudaMemsetAsync(status, 0, sizeof(int32_t), s));
-  if (normed == nullptr &&
+  if (fold &&
       (st = layers::launch_norm_fold(x, static_cast<const __nv_bfloat16*>(final_norm), hidden, rows, xn, ssq, s)) !=
+          SG_OK)
+    return st;
+  if (normed == nullptr && !fold &&
+      (st = layers::launch_rmsnorm(x, static_cast<const __nv_bfloat16*>(final_norm), hidden, rows, rms_eps, xn, s)) !=
           SG_OK)
     return st;
   gemm::EpiLmHead::Params pl;

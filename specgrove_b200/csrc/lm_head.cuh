@@ -9,6 +9,14 @@
 
 namespace sg {
 
+// Form of the RMSNorms of the verify pass (engine.cu): false (the default)
+// runs them as kernels that write normalised bf16 rows; true (SG_NORM_FUSED=1)
+// folds them into GEMM epilogues (bf16(x * w) rows, each row's GEMM output
+// scaled by rsqrt(mean(x^2) + eps)).  The stand-alone sampler follows the
+// same form for the final norm, so it draws what the pass draws.
+bool qkv_fused();
+bool norm_fused();
+
 // Scratch bytes for `rows` rows: a 256-byte status word, the normalised rows
 // (bf16) and the per-(row, vocab tile) partials (float4), 256-byte aligned.
 size_t lm_head_scratch_need(int rows, int hidden, int vocab);

@@ -7,12 +7,13 @@ prefill of arrivals (:1556-1602), one ``_propose_many`` per wave
 verifier and commit (:1748-2129), and the feature gather that becomes each
 request's next draft update (:2144-2183).  Here:
 
-* ``admit``: the target prefills each prompt in chain-shaped chunks
-  (``sg_verify_pass`` without commit, exporting the drafter's feature layers
-  for every prompt row) and the drafter appends the same rows to its draft
-  cache (``sg_draft_pass`` in context-only mode), so both caches end at the
-  prompt length; the last prompt row's sampled posterior is the first
-  generated token.
+* ``admit``: the target prefills each prompt in chain-shaped chunks of at
+  most 256 rows, as many chunks per wave as its row budget holds (several
+  consecutive chunks of one prompt included; ``sg_verify_pass`` without
+  commit, exporting the drafter's feature layers for every prompt row) and
+  the drafter appends the same rows to its draft cache (``sg_draft_pass`` in
+  context-only mode), so both caches end at the prompt length; the last
+  prompt row's sampled posterior is the first generated token.
 * ``step``: one ``sg_draft_pass`` over every running request (the kept rows'
   features of its previous verify as the update, its last token as the
   block's anchor), ``plan_wave`` on the device (proposals, trees, tier
@@ -103,8 +104,8 @@ class SpecDecoder:
     # -------------------------------------------------------------- admission
     def admit(self, requests: Sequence[SpecRequest]) -> None:
         """Prefill the target and the draft cache of each request (chain
-        chunks of at most ``chunk`` rows, waves of at most ``max_rows`` rows)
-        and sample its first token."""
+        chunks of at most ``chunk`` rows, waves of at most ``max_rows`` rows
+        and the drafter's update rows) and sample its first token."""
         t, d = self.target, self.drafter
         for r in requests:
             if not self.free_slots:
@@ -118,33 +119,47 @@ class SpecDecoder:
         remaining = {r.slot: list(r.prompt) for r in requests}
         by_slot = {r.slot: r for r in requests}
         while any(remaining.values()):
-            trees, slots, lens, rows = [], [], [], 0
+            # A wave takes up to max_rows prompt rows.  A long prompt goes in
+            # as several consecutive chain chunks of one slot in the same wave:
+            # chunk k's rows sit at cache positions after chunk k - 1's, whose
+            # K/V the pass writes into the arena (q/k/v epilogue) before any
+            # attention reads them, so chunk k sees them as prefix.
+            trees, slots, lens, dlens, rows = [], [], [], [], 0
+            limit = min(t.max_rows, d.max_update_rows)
+            extra = {}
             for r in requests:
                 rem = remaining[r.slot]
-                if not rem or rows + min(self.chunk, len(rem)) > t.max_rows or len(trees) >= t.max_requests:
-                    continue
-                part = rem[:self.chunk]
-                del rem[:self.chunk]
-                trees.append(([-1] + list(range(len(part) - 1)), part))
-                slots.append(r.slot)
-                lens.append(t.arena.lengths[r.slot])
-                rows += len(part)
+                while rem and len(trees) < t.max_requests:
+                    take = min(self.chunk, len(rem), limit - rows)
+                    if take <= 0:
+                        break
+                    part = rem[:take]
+                    del rem[:take]
+                    off = extra.get(r.slot, 0)
+                    trees.append(([-1] + list(range(len(part) - 1)), part))
+                    slots.append(r.slot)
+                    lens.append(t.arena.lengths[r.slot] + off)
+                    dlens.append(d.arena.lengths[r.slot] + off)
+                    extra[r.slot] = off + take
+                    rows += take
             wave = Wave(trees, slots, lens, request_ids=[by_slot[s].request_id for s in slots])
             dw = wave.to(t.device)
             Q = wave.num_rows
             t.verify_device(dw, seed=self.seed, temperature=self.temperature, commit=False,
                             posterior=self.posterior, feature_layers=self.feature_layers,
                             features_out=self.features)
-            dlens = torch.tensor([d.arena.lengths[s] for s in slots], dtype=torch.long, device=t.device)
-            d.append_context(dw.slots, dlens, dw.row_offsets, self.features[:Q], Q)
-            for i, s in enumerate(slots):
-                n = len(trees[i][0])
+            d.append_context(dw.slots, torch.tensor(dlens, dtype=torch.long, device=t.device), dw.row_offsets,
+                             self.features[:Q], Q)
+            for s, n in extra.items():
                 t.arena.lengths[s] += n
                 d.arena.lengths[s] += n
-            last = [(s, wave.row_offsets[i + 1] - 1) for i, s in enumerate(slots) if not remaining[s]]
+            last = {}
+            for i, s in enumerate(slots):
+                if not remaining[s]:
+                    last[s] = wave.row_offsets[i + 1] - 1      # the slot's last chunk in this wave
             if last:
-                picks = self.posterior[torch.tensor([q for _, q in last], device=t.device)].cpu().tolist()
-                for (s, _), tok in zip(last, picks):
+                picks = self.posterior[torch.tensor(list(last.values()), device=t.device)].cpu().tolist()
+                for s, tok in zip(last, picks):
                     by_slot[s].generated = [int(tok)]
         self._check_status("admission")
         self.running.extend(requests)

@@ -98,3 +98,34 @@ def test_spec_server_serves_every_request():
     assert sorted(dec.free_slots) == [0, 1, 2, 3]
     assert not dec.running
     assert stats.exchanges >= stats.waves
+
+
+def test_multi_chunk_prefill_wave_matches_chunk_per_wave():
+    """A 700-token prompt prefilled as three chain chunks of one slot in a
+    single wave writes the same target and draft-cache K/V (bf16 rounding of
+    a different attention tiling aside) and samples the same greedy first
+    token as one chunk per wave."""
+    prompt = torch.randint(0, 4000, (700,), generator=torch.Generator().manual_seed(9)).tolist()
+
+    def run(max_rows):
+        target_w = Weights.random(SHAPE, seed=11, std=0.08)
+        draft_w = DraftWeights.random(DSHAPE, target_w, seed=12, std=0.08)
+        target = B200Engine(target_w, num_slots=2, capacity=1024, max_rows=max_rows, max_requests=4)
+        drafter = B200Drafter(draft_w, num_slots=2, capacity=1024, max_requests=4, max_update_rows=1024)
+        dec = SpecDecoder(target, drafter, FEATURES, tiers=[3, 7], row_budget=32, temperature=0.0,
+                          fixed_row_equivalent=8.0, seed=3)
+        req = SpecRequest(7, prompt, max_new_tokens=4)
+        dec.admit([req])
+        torch.cuda.synchronize()
+        s = req.slot
+        cap = target.arena.capacity
+        kv_t = target.arena.storage[:, :, :, s * cap:s * cap + 700].float().cpu()
+        kv_d = drafter.arena.storage[:, :, :, s * cap:s * cap + 700].float().cpu()
+        return req.generated[0], kv_t, kv_d, target.arena.lengths[s], drafter.arena.lengths[s]
+
+    one_wave = run(1024)      # 256 + 256 + 188 rows in one wave
+    per_wave = run(256)       # one 256-row chunk per wave
+    assert one_wave[3] == per_wave[3] == 700 and one_wave[4] == per_wave[4] == 700
+    for a, b in ((one_wave[1], per_wave[1]), (one_wave[2], per_wave[2])):
+        assert (a - b).abs().max().item() <= 2e-2 * b.abs().max().item()
+    assert one_wave[0] == per_wave[0]
