@@ -107,12 +107,15 @@ class SpecDecoder:
         chunks of at most ``chunk`` rows, waves of at most ``max_rows`` rows
         and the drafter's update rows) and sample its first token."""
         t, d = self.target, self.drafter
+        if len(requests) > len(self.free_slots):
+            raise RuntimeError(f"{len(requests)} requests but {len(self.free_slots)} free slots")
         for r in requests:
-            if not self.free_slots:
-                raise RuntimeError("no free slot")
+            if not r.prompt or r.max_new_tokens < 1:
+                raise ValueError("a request needs a non-empty prompt and max_new_tokens >= 1")
             need = len(r.prompt) + r.max_new_tokens + max(self.tiers[-1] + 1, d.shape.block_size)
             if need > min(t.arena.capacity, d.arena.capacity):
                 raise ValueError("prompt + new tokens + one tree do not fit the slot capacity")
+        for r in requests:
             r.slot = self.free_slots.pop(0)
             t.arena.lengths[r.slot] = 0
             d.arena.lengths[r.slot] = 0
@@ -162,7 +165,12 @@ class SpecDecoder:
                 for s, tok in zip(last, picks):
                     by_slot[s].generated = [int(tok)]
         self._check_status("admission")
-        self.running.extend(requests)
+        for r in requests:
+            if len(r.generated) >= r.max_new_tokens:   # the first token was the last
+                r.done = True
+                self.free_slots.append(r.slot)
+            else:
+                self.running.append(r)
 
     # ------------------------------------------------------------------ step
     def step(self) -> int:
@@ -184,8 +192,8 @@ class SpecDecoder:
         U = offs[-1]
         feats = None
         if U:
-            idx = torch.cat([torch.arange(a, b, device=dev) for a, b in starts if b > a])
-            feats = self.kept.index_select(0, idx).contiguous()
+            idx = torch.tensor([i for a, b in starts for i in range(a, b)], dtype=torch.long).to(dev)
+            feats = self.kept.index_select(0, idx)
         dlens = [d.arena.lengths[s] for s in slots]
         meta = torch.tensor(slots + dlens + offs + [r.generated[-1] for r in reqs] +
                             [t.arena.lengths[s] for s in slots] + [r.request_id for r in reqs],
