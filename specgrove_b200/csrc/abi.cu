@@ -32,6 +32,11 @@ bool pdl_enabled() {
   return enabled;
 }
 
+L2Window& l2_window() {
+  static thread_local L2Window w;
+  return w;
+}
+
 int device_sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;

@@ -90,6 +90,17 @@ __device__ __forceinline__ void pdl_wait() {
 
 bool pdl_enabled();  // SG_PDL=0 disables programmatic dependent launch
 
+// L2 residency window: while set (on this host thread), every launch_pdl
+// kernel marks its accesses to [base, base + bytes) as persisting in L2 (the
+// rest of the window's misses stream), so a buffer that each layer reads and
+// writes survives the layer's weight and K/V streams in the L2 set-aside.
+struct L2Window {
+  const void* base = nullptr;
+  size_t bytes = 0;
+  float hit_ratio = 0.f;
+};
+L2Window& l2_window();
+
 template <typename... Params, typename... Args>
 int launch_pdl(const char* name, void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
                cudaStream_t stream, Args&&... args) {
@@ -98,11 +109,25 @@ int launch_pdl(const char* name, void (*kernel)(Params...), dim3 grid, dim3 bloc
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  const L2Window& win = l2_window();
+  if (win.bytes != 0) {
+    attr[n].id = cudaLaunchAttributeAccessPolicyWindow;
+    attr[n].val.accessPolicyWindow.base_ptr = const_cast<void*>(win.base);
+    attr[n].val.accessPolicyWindow.num_bytes = win.bytes;
+    attr[n].val.accessPolicyWindow.hitRatio = win.hit_ratio;
+    attr[n].val.accessPolicyWindow.hitProp = cudaAccessPropertyPersisting;
+    attr[n].val.accessPolicyWindow.missProp = cudaAccessPropertyStreaming;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = n;
   cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
   if (err != cudaSuccess) {
     set_error("%s launch failed: %s", name, cudaGetErrorString(err));

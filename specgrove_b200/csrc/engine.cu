@@ -15,6 +15,7 @@
 //   append_packed_sequence (:2121)   -> in-place arena commit
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <memory>
 #include <vector>
@@ -45,6 +46,19 @@ bool qkv_fused() {
 // 512-row wave, whose residual GEMMs run split over two CTAs per tile with
 // the heavier epilogue on the owner's critical path.  The folded form needs
 // the fused q/k/v epilogue.
+// The pass's fp32 residual stream (read and written by every residual GEMM
+// epilogue and norm of every layer) is kept persisting in L2: an access-policy
+// window on every kernel of the pass over an L2 set-aside of this process's
+// context, so the layer's weight and K/V streams do not evict it (about 1% of
+// the configuration-4 pass).  SG_L2_PERSIST=0 turns it off.
+bool l2_persist() {
+  static const bool on = [] {
+    const char* v = std::getenv("SG_L2_PERSIST");
+    return v == nullptr || v[0] != '0';
+  }();
+  return on;
+}
+
 bool norm_fused() {
   static const bool fused = [] {
     const char* v = std::getenv("SG_NORM_FUSED");
@@ -74,6 +88,8 @@ struct Engine {
   void* workspace = nullptr;
   size_t workspace_bytes = 0;
   float* x;
+  size_t l2_window_bytes = 0;  // residual-stream bytes kept persisting in L2 (0: off)
+  size_t l2_setaside = 0;      // the context's persisting L2 set-aside
   __nv_bfloat16 *xn, *qkv, *q, *attn, *h;
   float* ssq;      // [max_rows][ss_parts] row sums of squares of the residual (folded RMSNorms)
   int ss_parts;    // column tiles of the residual GEMMs
@@ -235,6 +251,24 @@ int create_engine(const sg_model_desc* model, const sg_arena_desc* arena, int32_
   SG_CUDA_CHECK(cudaMalloc(&e->workspace, e->workspace_bytes));
   uint8_t* cur = static_cast<uint8_t*>(e->workspace);
   e->x = carve<float>(cur, static_cast<size_t>(max_rows) * H);
+  if (l2_persist()) {
+    // Set aside L2 for the fp32 residual stream (this process's context
+    // only; never shrinks a larger set-aside made earlier in the process).
+    int dev = 0, max_persist = 0, max_window = 0;
+    SG_CUDA_CHECK(cudaGetDevice(&dev));
+    SG_CUDA_CHECK(cudaDeviceGetAttribute(&max_persist, cudaDevAttrMaxPersistingL2CacheSize, dev));
+    SG_CUDA_CHECK(cudaDeviceGetAttribute(&max_window, cudaDevAttrMaxAccessPolicyWindowSize, dev));
+    const size_t want = std::min(static_cast<size_t>(max_rows) * H * sizeof(float), static_cast<size_t>(max_window));
+    size_t cur_limit = 0;
+    SG_CUDA_CHECK(cudaDeviceGetLimit(&cur_limit, cudaLimitPersistingL2CacheSize));
+    const size_t setaside = std::min(want, static_cast<size_t>(max_persist));
+    if (cur_limit < setaside) SG_CUDA_CHECK(cudaDeviceSetLimit(cudaLimitPersistingL2CacheSize, setaside));
+    SG_CUDA_CHECK(cudaDeviceGetLimit(&cur_limit, cudaLimitPersistingL2CacheSize));
+    if (want > 0 && cur_limit > 0) {
+      e->l2_window_bytes = want;
+      e->l2_setaside = cur_limit;
+    }
+  }
   e->xn = carve<__nv_bfloat16>(cur, static_cast<size_t>(max_rows) * H);
   e->qkv = carve<__nv_bfloat16>(cur, static_cast<size_t>(max_rows) * qkv_n);
   e->q = carve<__nv_bfloat16>(cur, static_cast<size_t>(max_rows) * qw);
@@ -531,6 +565,16 @@ extern "C" int sg_verify_pass(void* engine, const sg_wave_desc* wave, void* stre
     return fail(SG_ERR_INVALID_ARGUMENT, "sg_verify_pass: temperature must be finite and >= 0 (0 = greedy)");
   const bool greedy = w.temperature == 0.f;
   const float inv_temp = greedy ? 1.0f : 1.0f / w.temperature;
+  struct WindowScope {  // the residual stream's L2 window for this pass's launches
+    L2Window saved;
+    WindowScope(const Engine* e, int rows) : saved(l2_window()) {
+      if (e->l2_window_bytes == 0) return;
+      const size_t bytes = std::min(e->l2_window_bytes, static_cast<size_t>(rows) * e->model.hidden * sizeof(float));
+      const float ratio = std::min(1.0f, static_cast<float>(e->l2_setaside) / static_cast<float>(bytes));
+      l2_window() = L2Window{e->x, bytes, ratio};
+    }
+    ~WindowScope() { l2_window() = saved; }
+  } window_scope(e, Q);
   // feature slot of every layer (-1: not a drafter feature layer)
   std::vector<int> feature_slot(static_cast<size_t>(m.num_layers), -1);
   const int nfeat = w.num_feature_layers;
