@@ -26,6 +26,8 @@
 // shared memory.
 #pragma once
 
+#include <type_traits>
+
 #include "sm100.cuh"
 
 namespace sg {
@@ -162,7 +164,18 @@ struct SegIter {
     it += kb1 - kb0;
     return true;
   }
+  __device__ bool more(const Shape& s) const { return dp_next < s.sp.t_dp || it < end; }
 };
+
+// An epilogue that reads a [BM, BN] fp32 tile of global memory may set
+// kStagesTile and provide tile_src(...) and apply_staged(...): on the CTA's
+// last segment (when the operand ring is idle) the tile's rows come into the
+// ring by bulk copy, one row per epilogue thread, and the epilogue reads them
+// from shared memory instead of issuing dependent global loads.
+template <class E, class = void>
+struct stages_tile : std::false_type {};
+template <class E>
+struct stages_tile<E, std::void_t<decltype(E::kStagesTile)>> : std::bool_constant<E::kStagesTile> {};
 
 // Epi must provide:
 //   struct Params;  (int32_t* status member)
@@ -188,6 +201,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint64_t* pbar = bars + 2 * STAGES + 5;  // stream-K partials -> operand ring
   uint64_t* cbar = bars + 2 * STAGES + 6;  // the owner's 128 threads are done with a round of the ring
+  uint64_t* xbar = bars + 2 * STAGES + 7;  // the last tile's epilogue input -> operand ring
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -204,6 +218,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
     }
     mbar_init(pbar, 1);
     mbar_init(cbar, 128);
+    mbar_init(xbar, 128);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tensormap(&tma_a);
@@ -401,7 +416,33 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
             if (atomicAdd(f, 1) == 255) atomicExch(f, 0);
           }
         }
-        Epi::apply(ep, shape, taddr, m0, n0, quarter, lane, epi_stage + (warp - 2) * (EPI_STAGE_BYTES / 16));
+        uint4* wst = epi_stage + (warp - 2) * (EPI_STAGE_BYTES / 16);
+        bool staged = false;
+        if constexpr (stages_tile<Epi>::value) {
+          if (!si.more(shape)) {
+            // The last segment: the ring is idle (no loads follow, the
+            // accumulator is complete).  After an owner's combine, wait until
+            // every thread is done with the partials' second round.
+            const int et = static_cast<int>(threadIdx.x) - 64;
+            const float* src = nullptr;
+            uint32_t bytes = 0;
+            if (Epi::tile_src(ep, shape, m0 + et, n0, src, bytes)) {
+              if (g.kind == kSegOwner && !mbar_wait(cbar, 1u)) {
+                fail_wait();
+                break;
+              }
+              mbar_arrive_expect_tx(xbar, bytes);
+              if (bytes != 0) bulk_g2s(smem + et * (BN * sizeof(float)), src, bytes, xbar);
+              if (!mbar_wait(xbar, 0u)) {
+                fail_wait();
+                break;
+              }
+              Epi::apply_staged(ep, shape, taddr, m0, n0, quarter, lane, wst, reinterpret_cast<const float*>(smem));
+              staged = true;
+            }
+          }
+        }
+        if (!staged) Epi::apply(ep, shape, taddr, m0, n0, quarter, lane, wst);
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
@@ -551,8 +592,25 @@ struct EpiResidual {
     float* ssq;                   // may be null; [rows][ss_parts]
     int ss_parts;
   };
+  static constexpr bool kStagesTile = true;
+  // Row `row` of the tile's x: its source and byte count (0 past M).  False
+  // when x's rows are not 16-byte aligned (the epilogue then loads directly);
+  // the same answer for every row of a launch.
+  static __device__ __forceinline__ bool tile_src(const Params& p, const Shape& s, int row, int n0, const float*& src,
+                                                  uint32_t& bytes) {
+    if (((reinterpret_cast<uintptr_t>(p.x) & 15u) != 0) || (p.ldx & 3) != 0) return false;
+    src = p.x + static_cast<int64_t>(row) * p.ldx + n0;
+    bytes = row < s.M ? static_cast<uint32_t>(min(BN, s.N - n0)) * 4u : 0u;
+    return true;
+  }
   static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int m0, int n0,
                                                int quarter, int lane, uint4* st) {
+    apply_staged(p, s, taddr, m0, n0, quarter, lane, st, nullptr);
+  }
+  // xs: the tile's x rows in shared memory ([BM][BN] fp32), or null to load
+  // them from global memory.
+  static __device__ __forceinline__ void apply_staged(const Params& p, const Shape& s, uint32_t taddr, int m0,
+                                                      int n0, int quarter, int lane, uint4* st, const float* xs) {
     const int row0 = m0 + quarter * 32;
     const int q = lane & 7;
     float ssr[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // rows i * 4 + lane / 8, this lane's columns
@@ -571,8 +629,11 @@ struct EpiResidual {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int row = row0 + i * 4 + (lane >> 3);
-        xv[i] = row < s.M ? *reinterpret_cast<const float4*>(p.x + static_cast<int64_t>(row) * p.ldx + col + q * 4)
-                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (xs != nullptr)
+          xv[i] = *reinterpret_cast<const float4*>(xs + (quarter * 32 + i * 4 + (lane >> 3)) * BN + c * 32 + q * 4);
+        else
+          xv[i] = row < s.M ? *reinterpret_cast<const float4*>(p.x + static_cast<int64_t>(row) * p.ldx + col + q * 4)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
