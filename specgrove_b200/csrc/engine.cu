@@ -388,11 +388,14 @@ int run_stack(Engine* e, const StackArgs& a, cudaStream_t stream) {
   const gemm::Shape s_gu = gemm::make_shape(Q, 2 * I, H);
   const gemm::Shape s_down = gemm::make_shape(Q, H, I);
   const gemm::Shape s_ctx = gemm::make_shape(a.ctx_rows, 2 * nkv * D, H);
-  // Shapes with at most half a wave of tiles (few packed rows) give each
-  // tile's k-blocks to two CTAs; everything else runs whole tiles, which
-  // measured faster (a tile split across CTA runs makes its owner wait).
+  // Shapes with at most half a wave of tiles (few packed rows) and a long K
+  // give each tile's k-blocks to two CTAs; everything else runs whole tiles,
+  // which measured faster (a split tile's owner waits for its contributor,
+  // adds the partial and only then runs the epilogue: about 15 µs that only
+  // a long k-loop pays back, e.g. the 512-row down projection, K = 12288,
+  // 85 -> 65 µs, but not the O projection, K = 4096, 34 -> 37 µs).
   auto small_wave = [&](const gemm::Shape& sh) -> const gemm::SplitWorkspace* {
-    return 2 * sh.tiles <= e->sms ? &e->split : nullptr;
+    return 2 * sh.tiles <= e->sms && sh.k_blocks >= 96 ? &e->split : nullptr;
   };
   for (int l = 0; l < m.num_layers; ++l) {
     const void* const* lw = &e->layer_ptrs[static_cast<size_t>(l) * W_COUNT];
