@@ -69,10 +69,31 @@ bool norm_fused() {
 
 namespace {
 
+// Narrow tile width for the residual (O and down) projections: 160 columns
+// make a 2560-wide output 16 tiles per 128 rows instead of 10, so a
+// 512-row wave keeps 64 SMs busy instead of 40 (configuration 3: 8.83 ->
+// 8.35 ms per pass).  Where 256-wide tiles already fill a wave the narrow
+// tile is slower (configuration 4: 37.1 against 35.0 ms: more A re-reads per
+// flop), so each pass picks the width (residual_width).
+constexpr int kNarrowBN = 160;
+
+// Tile width of a pass's residual projections: the narrow tile when its
+// waves, weighted by its width and a 1.25 efficiency penalty, beat the
+// 256-wide tile's waves.
+int residual_width(int rows, int hidden, int sms) {
+  const int mt = (rows + gemm::BM - 1) / gemm::BM;
+  const int t_wide = mt * ((hidden + gemm::BN - 1) / gemm::BN);
+  const int t_narrow = mt * ((hidden + kNarrowBN - 1) / kNarrowBN);
+  const double wide = static_cast<double>((t_wide + sms - 1) / sms);
+  const double narrow = static_cast<double>((t_narrow + sms - 1) / sms) * kNarrowBN / gemm::BN * 1.25;
+  return narrow < wide ? kNarrowBN : gemm::BN;
+}
+
 enum { W_IN_NORM = 0, W_QKV, W_Q_NORM, W_K_NORM, W_O, W_POST_NORM, W_GATE_UP, W_DOWN, W_COUNT };
 
 struct LayerMaps {
   CUtensorMap qkv, o, gate_up, down;
+  CUtensorMap o_narrow, down_narrow;  // the same weights with kNarrowBN-row boxes
 };
 
 struct Engine {
@@ -164,7 +185,7 @@ size_t workspace_size(const sg_model_desc& m, int rows, int sms) {
   s += rows * vt * 16 + 256;                  // partials
   s += rows * 4 + 256;                        // lse
   s += rows * 8 + 256;                        // posterior
-  s += rows * ((H + gemm::BN - 1) / gemm::BN) * 4 + 256;  // row sums of squares (folded norms)
+  s += rows * ((H + kNarrowBN - 1) / kNarrowBN) * 4 + 256;  // row sums of squares (folded norms)
   s += rows * layers::kAncWords * 4 + 256;    // anc
   s += rows * 4 * 3 + 3 * 256;                // position, tree, local
   s += rows * 8 + 256;                        // request id
@@ -232,9 +253,11 @@ int create_engine(const sg_model_desc* model, const sg_arena_desc* arena, int32_
     LayerMaps& lm = e->maps[l];
     if ((st = make_tmap_2d_bf16(&lm.qkv, lw[W_QKV], H, qkv_n, H * 2, gemm::BK, gemm::BN)) != SG_OK) return st;
     if ((st = make_tmap_2d_bf16(&lm.o, lw[W_O], qw, H, qw * 2, gemm::BK, gemm::BN)) != SG_OK) return st;
+    if ((st = make_tmap_2d_bf16(&lm.o_narrow, lw[W_O], qw, H, qw * 2, gemm::BK, kNarrowBN)) != SG_OK) return st;
     if ((st = make_tmap_2d_bf16(&lm.gate_up, lw[W_GATE_UP], H, 2 * I, H * 2, gemm::BK, gemm::BN)) != SG_OK)
       return st;
     if ((st = make_tmap_2d_bf16(&lm.down, lw[W_DOWN], I, H, I * 2, gemm::BK, gemm::BN)) != SG_OK) return st;
+    if ((st = make_tmap_2d_bf16(&lm.down_narrow, lw[W_DOWN], I, H, I * 2, gemm::BK, kNarrowBN)) != SG_OK) return st;
   }
   if ((st = make_tmap_2d_bf16(&e->lm_map, m.lm_head, H, m.vocab, H * 2, gemm::BK, gemm::BN)) != SG_OK) return st;
   {
@@ -278,7 +301,7 @@ int create_engine(const sg_model_desc* model, const sg_arena_desc* arena, int32_
   e->partials = carve<float4>(cur, static_cast<size_t>(max_rows) * e->vocab_tiles);
   e->lse_ws = carve<float>(cur, max_rows);
   e->posterior_ws = carve<int64_t>(cur, max_rows);
-  e->ss_parts = (H + gemm::BN - 1) / gemm::BN;
+  e->ss_parts = (H + kNarrowBN - 1) / kNarrowBN;  // the most column tiles a residual GEMM writes
   e->ssq = carve<float>(cur, static_cast<size_t>(max_rows) * e->ss_parts);
   e->meta.anc = carve<uint32_t>(cur, static_cast<size_t>(max_rows) * layers::kAncWords);
   e->meta.position = carve<int32_t>(cur, max_rows);
@@ -373,7 +396,8 @@ int run_stack(Engine* e, const StackArgs& a, cudaStream_t stream) {
   const int64_t plane_stride = plane_rows * D;  // elements between kv heads
   __nv_bfloat16* arena = static_cast<__nv_bfloat16*>(e->arena.storage);
   const bool nf = norm_fused();
-  const int P = e->ss_parts;
+  const int rbn = residual_width(Q, H, e->sms);
+  const int P = (H + rbn - 1) / rbn;  // column tiles of this pass's residual GEMMs
   const float inv_h = 1.0f / static_cast<float>(H);
   int st;
   if (nf && (st = layers::launch_norm_fold(e->x, static_cast<const __nv_bfloat16*>(e->layer_ptrs[W_IN_NORM]), H, Q,
@@ -384,9 +408,9 @@ int run_stack(Engine* e, const StackArgs& a, cudaStream_t stream) {
     return st;
   trace_at(a, 1, stream);
   const gemm::Shape s_qkv = gemm::make_shape(Q, qkv_n, H);
-  const gemm::Shape s_o = gemm::make_shape(Q, H, qw);
+  const gemm::Shape s_o = gemm::make_shape(Q, H, qw, rbn);
   const gemm::Shape s_gu = gemm::make_shape(Q, 2 * I, H);
-  const gemm::Shape s_down = gemm::make_shape(Q, H, I);
+  const gemm::Shape s_down = gemm::make_shape(Q, H, I, rbn);
   const gemm::Shape s_ctx = gemm::make_shape(a.ctx_rows, 2 * nkv * D, H);
   // Shapes with at most half a wave of tiles (few packed rows) and a long K
   // give each tile's k-blocks to two CTAs; everything else runs whole tiles,
@@ -513,7 +537,10 @@ int run_stack(Engine* e, const StackArgs& a, cudaStream_t stream) {
       po.ssq = e->ssq;
       po.ss_parts = P;
     }
-    if ((st = gemm::launch<gemm::EpiResidual>(e->attn_map, lm.o, s_o, po, stream, small_wave(s_o))) != SG_OK)
+    if ((st = rbn == kNarrowBN ? gemm::launch<gemm::EpiResidual, kNarrowBN>(e->attn_map, lm.o_narrow, s_o, po, stream,
+                                                                            small_wave(s_o))
+                               : gemm::launch<gemm::EpiResidual>(e->attn_map, lm.o, s_o, po, stream, small_wave(s_o))) !=
+        SG_OK)
       return st;
     if (l == 0) trace_at(a, 6, stream);
     if (!nf && (st = layers::launch_rmsnorm(e->x, static_cast<const __nv_bfloat16*>(lw[W_POST_NORM]), H, Q,
@@ -538,7 +565,10 @@ int run_stack(Engine* e, const StackArgs& a, cudaStream_t stream) {
       pd.ssq = e->ssq;
       pd.ss_parts = P;
     }
-    if ((st = gemm::launch<gemm::EpiResidual>(e->h_map, lm.down, s_down, pd, stream, small_wave(s_down))) != SG_OK)
+    if ((st = rbn == kNarrowBN ? gemm::launch<gemm::EpiResidual, kNarrowBN>(e->h_map, lm.down_narrow, s_down, pd,
+                                                                            stream, small_wave(s_down))
+                               : gemm::launch<gemm::EpiResidual>(e->h_map, lm.down, s_down, pd, stream,
+                                                                 small_wave(s_down))) != SG_OK)
       return st;
     if (l == 0) trace_at(a, 9, stream);
   }

@@ -48,29 +48,51 @@ constexpr size_t SMEM_BYTES =
     static_cast<size_t>(STAGES) * STAGE_BYTES + 1024 + BARRIER_BYTES + 4 * EPI_STAGE_BYTES;
 constexpr uint32_t IDESC = sm100::idesc_bf16_f32(BM, BN);
 
+// Per tile width: the default 256 columns, or 160 for the residual
+// projections (a 4096-wide output is 26 tiles per 128 rows, 2.81 waves of
+// 148 SMs at 2048 rows against 1.73 for 256-wide tiles).  Narrower tiles
+// leave room for a fifth ring stage, and two fp32 partials of a split tile
+// fit the ring in one combine round.
+template <int TBN>
+struct Cfg {
+  static_assert(TBN % 32 == 0 && TBN >= 32 && TBN <= 256, "tile width");
+  static constexpr int B_TILE = TBN * BK * 2;
+  static constexpr int STAGE_BYTES = A_TILE + B_TILE;
+  static constexpr int STAGES = TBN == 256 ? 4 : 5;
+  static constexpr size_t SMEM_BYTES =
+      static_cast<size_t>(STAGES) * STAGE_BYTES + 1024 + BARRIER_BYTES + 4 * EPI_STAGE_BYTES;
+  static constexpr uint32_t IDESC = sm100::idesc_bf16_f32(BM, TBN);
+  static constexpr int ROUNDS = TBN == 256 ? 2 : 1;  // stream-K combine rounds (2 partials per round fit the ring)
+  static_assert(2 * BM * (TBN / ROUNDS) * 4 <= STAGES * STAGE_BYTES, "combine round exceeds the ring");
+  static_assert(BM * TBN * 4 <= STAGES * STAGE_BYTES, "staged tile exceeds the ring");
+  static_assert(2 * TBN <= static_cast<int>(TMEM_COLS), "two accumulators exceed TMEM");
+};
+
 // Stream-K plan for the tiles after the last full wave (sk_ctas == 0: none).
 struct Split {
   int t_dp;         // tiles [0, t_dp) run whole, round-robin over the grid
   int sk_ctas;      // CTAs [0, sk_ctas) share the k-blocks of tiles [t_dp, tiles)
   int per, rem;     // CTA c takes per (+1 when c < rem) consecutive iterations
   int max_slots;    // partial buffers per split tile (contributors per tile)
-  float* partials;  // [split tile][slot][BN / 4][BM] float4: column quad-major, rows contiguous
+  float* partials;  // [split tile][slot][tile width / 4][BM] float4 (slot stride BM * BN floats)
   int* flags;       // [split tile][slot]: 128 once the contributor's threads are done
 };
 
 struct Shape {
   int M, N, K;
+  int bn;  // tile width (columns)
   int m_tiles, n_tiles, k_blocks, tiles;
   Split sp;
 };
 
-inline Shape make_shape(int M, int N, int K) {
+inline Shape make_shape(int M, int N, int K, int bn = BN) {
   Shape s;
   s.M = M;
   s.N = N;
   s.K = K;
+  s.bn = bn;
   s.m_tiles = (M + BM - 1) / BM;
-  s.n_tiles = (N + BN - 1) / BN;
+  s.n_tiles = (N + bn - 1) / bn;
   s.k_blocks = K / BK;
   s.tiles = s.m_tiles * s.n_tiles;
   s.sp = Split{s.tiles, 0, 0, 0, 0, nullptr, nullptr};
@@ -114,7 +136,7 @@ inline void plan_split(Shape& s, int sms, const SplitWorkspace* ws) {
 
 __device__ __forceinline__ void tile_coords(const Shape& s, int tile, int& m0, int& n0) {
   m0 = (tile % s.m_tiles) * BM;
-  n0 = (tile / s.m_tiles) * BN;
+  n0 = (tile / s.m_tiles) * s.bn;
 }
 
 // One unit of a CTA's work: k-blocks [kb0, kb1) of a tile.
@@ -182,11 +204,15 @@ struct stages_tile<E, std::void_t<decltype(E::kStagesTile)>> : std::bool_constan
 //   static __device__ void apply(const Params&, const Shape&, uint32_t taddr,
 //                                int m0, int n0, int quarter, int lane,
 //                                uint4* stage);  // the warp's staging slice
-template <class Epi>
+template <class Epi, int TBN = BN>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
             const Shape shape, const typename Epi::Params ep) {
   using namespace sm100;
+  using C = Cfg<TBN>;
+  constexpr int STAGES = C::STAGES;
+  constexpr int STAGE_BYTES = C::STAGE_BYTES;
+  constexpr int B_TILE = C::B_TILE;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -276,7 +302,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * TBN);
         bool ok = true;
         for (int kb = g.kb0; kb < g.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase)) {
@@ -289,7 +315,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
           const uint32_t b_base = smem_u32(sB + stage * B_TILE);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            mma_bf16(d, desc_k_sw128(a_base + k * 32), desc_k_sw128(b_base + k * 32), IDESC,
+            mma_bf16(d, desc_k_sw128(a_base + k * 32), desc_k_sw128(b_base + k * 32), C::IDESC,
                      ((kb - g.kb0) | k) != 0 ? 1u : 0u);
           mma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -321,7 +347,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
       int m0, n0;
       tile_coords(shape, g.tile, m0, n0);
       const uint32_t taddr =
-          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * TBN);
       const Split& sp = shape.sp;
       const int sk_tile = g.tile - sp.t_dp;
       if (g.kind == kSegContrib) {
@@ -332,7 +358,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
         // contiguous bytes.
         float4* d4 = reinterpret_cast<float4*>(dst) + r;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = 0; c < TBN / 32; ++c) {
           float v[32];
           tmem_ld32(taddr + c * 32, v);
 #pragma unroll
@@ -357,13 +383,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
           }
           __threadfence();
           // acc += partials in k order, written back to TMEM for the epilogue.
-          // Round h brings columns [128h, 128h + 128) of every contributor
-          // (quads 32h .. 32h + 31: 64 KB contiguous per partial) into the
-          // idle ring; thread 0 of the epilogue warps issues the copies.
-          constexpr uint32_t kHalf = BM * (BN / 2) * sizeof(float);
+          // Round h brings columns [h TBN / ROUNDS, (h + 1) TBN / ROUNDS) of
+          // every contributor (contiguous quads of the partial) into the idle
+          // ring; thread 0 of the epilogue warps issues the copies.
+          constexpr uint32_t kHalf = BM * (TBN / C::ROUNDS) * sizeof(float);
+          constexpr int kRoundChunks = TBN / (32 * C::ROUNDS);
           const float4* ring4 = reinterpret_cast<const float4*>(smem);
           const bool issuer = threadIdx.x == 64;
-          for (int h = 0; h < 2 && ready; ++h) {
+          for (int h = 0; h < C::ROUNDS && ready; ++h) {
             if (issuer) {
               if (h > 0 && !mbar_wait(cbar, 0u)) {  // round 0 fully read
                 fail_wait();
@@ -386,9 +413,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
               break;
             }
 #pragma unroll 1
-            for (int c = 0; c < BN / 64; ++c) {
+            for (int c = 0; c < kRoundChunks; ++c) {
               float v[32];
-              const uint32_t col = static_cast<uint32_t>((h * (BN / 64) + c) * 32);
+              const uint32_t col = static_cast<uint32_t>((h * kRoundChunks + c) * 32);
               tmem_ld32(taddr + col, v);
               for (int slot = 0; slot < g.ncontrib; ++slot) {
                 const float4* src = ring4 + slot * (kHalf / 16) + r;
@@ -427,12 +454,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ C
             const float* src = nullptr;
             uint32_t bytes = 0;
             if (Epi::tile_src(ep, shape, m0 + et, n0, src, bytes)) {
-              if (g.kind == kSegOwner && !mbar_wait(cbar, 1u)) {
+              if (g.kind == kSegOwner && !mbar_wait(cbar, static_cast<uint32_t>((C::ROUNDS - 1) & 1))) {
                 fail_wait();
                 break;
               }
               mbar_arrive_expect_tx(xbar, bytes);
-              if (bytes != 0) bulk_g2s(smem + et * (BN * sizeof(float)), src, bytes, xbar);
+              if (bytes != 0) bulk_g2s(smem + et * (TBN * sizeof(float)), src, bytes, xbar);
               if (!mbar_wait(xbar, 0u)) {
                 fail_wait();
                 break;
@@ -577,7 +604,7 @@ struct RowNorm {
 // Residual stream update: x (fp32) += acc.  Optional outputs, all from the
 // updated x: x_bf16 = bf16(x) (the drafter's hidden state), xw = bf16(x *
 // norm_w) (the next GEMM's A operand with the next RMSNorm's weight folded
-// in), ssq[row][n0 / BN] = sum of x^2 over this tile's columns (the next
+// in), ssq[row][n0 / s.bn] = sum of x^2 over this tile's columns (the next
 // GEMM's row scale, RowNorm).
 struct EpiResidual {
   struct Params {
@@ -593,6 +620,7 @@ struct EpiResidual {
     int ss_parts;
   };
   static constexpr bool kStagesTile = true;
+  static constexpr bool kAnyWidth = true;  // reads the tile width from the shape
   // Row `row` of the tile's x: its source and byte count (0 past M).  False
   // when x's rows are not 16-byte aligned (the epilogue then loads directly);
   // the same answer for every row of a launch.
@@ -600,14 +628,14 @@ struct EpiResidual {
                                                   uint32_t& bytes) {
     if (((reinterpret_cast<uintptr_t>(p.x) & 15u) != 0) || (p.ldx & 3) != 0) return false;
     src = p.x + static_cast<int64_t>(row) * p.ldx + n0;
-    bytes = row < s.M ? static_cast<uint32_t>(min(BN, s.N - n0)) * 4u : 0u;
+    bytes = row < s.M ? static_cast<uint32_t>(min(s.bn, s.N - n0)) * 4u : 0u;
     return true;
   }
   static __device__ __forceinline__ void apply(const Params& p, const Shape& s, uint32_t taddr, int m0, int n0,
                                                int quarter, int lane, uint4* st) {
     apply_staged(p, s, taddr, m0, n0, quarter, lane, st, nullptr);
   }
-  // xs: the tile's x rows in shared memory ([BM][BN] fp32), or null to load
+  // xs: the tile's x rows in shared memory ([BM][s.bn] fp32), or null to load
   // them from global memory.
   static __device__ __forceinline__ void apply_staged(const Params& p, const Shape& s, uint32_t taddr, int m0,
                                                       int n0, int quarter, int lane, uint4* st, const float* xs) {
@@ -615,7 +643,7 @@ struct EpiResidual {
     const int q = lane & 7;
     float ssr[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // rows i * 4 + lane / 8, this lane's columns
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int c = 0; c < s.bn / 32; ++c) {
       const int col = n0 + c * 32;
       if (col >= s.N) break;
       float v[32];
@@ -630,7 +658,7 @@ struct EpiResidual {
       for (int i = 0; i < 8; ++i) {
         const int row = row0 + i * 4 + (lane >> 3);
         if (xs != nullptr)
-          xv[i] = *reinterpret_cast<const float4*>(xs + (quarter * 32 + i * 4 + (lane >> 3)) * BN + c * 32 + q * 4);
+          xv[i] = *reinterpret_cast<const float4*>(xs + (quarter * 32 + i * 4 + (lane >> 3)) * s.bn + c * 32 + q * 4);
         else
           xv[i] = row < s.M ? *reinterpret_cast<const float4*>(p.x + static_cast<int64_t>(row) * p.ldx + col + q * 4)
                             : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -671,7 +699,7 @@ struct EpiResidual {
         v += __shfl_xor_sync(0xffffffffu, v, 2);
         v += __shfl_xor_sync(0xffffffffu, v, 4);
         const int row = row0 + i * 4 + (lane >> 3);
-        if (q == 0 && row < s.M) p.ssq[static_cast<int64_t>(row) * p.ss_parts + n0 / BN] = v;
+        if (q == 0 && row < s.M) p.ssq[static_cast<int64_t>(row) * p.ss_parts + n0 / s.bn] = v;
       }
     }
   }
@@ -1016,9 +1044,18 @@ struct EpiLmHead {
 };
 
 // Host launcher: persistent grid of min(tiles, SMs) CTAs.
-template <class Epi>
+template <class E, class = void>
+struct any_width : std::false_type {};
+template <class E>
+struct any_width<E, std::void_t<decltype(E::kAnyWidth)>> : std::bool_constant<E::kAnyWidth> {};
+
+// Launch with tile width TBN; shape_in must come from make_shape(..., TBN)
+// and the B tensor map's box must be {BK, TBN}.
+template <class Epi, int TBN = BN>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Shape& shape_in, const typename Epi::Params& ep,
            cudaStream_t stream, const SplitWorkspace* split = nullptr) {
+  static_assert(TBN == BN || any_width<Epi>::value, "this epilogue assumes 256-column tiles");
+  if (shape_in.bn != TBN) return fail(SG_ERR_INVALID_ARGUMENT, "gemm: shape planned for another tile width");
   // Devices on which this instantiation's shared-memory limit is raised.
   // Setting it twice (two host threads racing on the first call) is harmless.
   static std::atomic<uint64_t> configured_devices{0};
@@ -1027,8 +1064,8 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Shape& shape_in, 
   if (dev < 0 || dev >= kMaxDevices) return fail(SG_ERR_UNSUPPORTED, "gemm: device index >= 64");
   const uint64_t bit = 1ull << dev;
   if (!(configured_devices.load(std::memory_order_acquire) & bit)) {
-    SG_CUDA_CHECK(cudaFuncSetAttribute(gemm_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(SMEM_BYTES)));
+    SG_CUDA_CHECK(cudaFuncSetAttribute(gemm_kernel<Epi, TBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(Cfg<TBN>::SMEM_BYTES)));
     configured_devices.fetch_or(bit, std::memory_order_acq_rel);
   }
   const int sms = device_sm_count();
@@ -1037,8 +1074,8 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Shape& shape_in, 
   int grid = shape.tiles < sms ? shape.tiles : sms;
   if (shape.sp.sk_ctas > grid) grid = shape.sp.sk_ctas;
   if (grid <= 0) return SG_OK;
-  return launch_pdl("gemm_kernel", gemm_kernel<Epi>, dim3(grid), dim3(THREADS), SMEM_BYTES, stream, ta, tb, shape,
-                    ep);
+  return launch_pdl("gemm_kernel", gemm_kernel<Epi, TBN>, dim3(grid), dim3(THREADS), Cfg<TBN>::SMEM_BYTES, stream, ta,
+                    tb, shape, ep);
 }
 
 }  // namespace gemm
