@@ -81,6 +81,12 @@ constexpr int kNarrowBN = 160;
 // waves, weighted by its width and a 1.25 efficiency penalty, beat the
 // 256-wide tile's waves.
 int residual_width(int rows, int hidden, int sms) {
+  static const int forced = [] {  // SG_RESIDUAL_BN=160 or 256 pins the width (tests, A/B timing)
+    const char* v = std::getenv("SG_RESIDUAL_BN");
+    const int w = v != nullptr ? std::atoi(v) : 0;
+    return w == kNarrowBN || w == gemm::BN ? w : 0;
+  }();
+  if (forced != 0) return forced;
   const int mt = (rows + gemm::BM - 1) / gemm::BM;
   const int t_wide = mt * ((hidden + gemm::BN - 1) / gemm::BN);
   const int t_narrow = mt * ((hidden + kNarrowBN - 1) / kNarrowBN);
