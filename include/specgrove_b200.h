@@ -95,6 +95,41 @@ SG_API int sg_tree_accept_probs(const float* probs, int64_t vocab,
                          uint64_t seed, const int64_t* request_ids,
                          int64_t* out, int32_t* status, void* stream);
 
+/*
+ * Terminal-mass tree verifier.  Replaces
+ *   sampling.py:542-735   tree_block_verify_terminal_mass (exit_mode
+ *                         "internal", prefix_mode "batched"), the decoder's
+ *                         default verifier (continuous_tree_block_decode.py:1328)
+ * which draws the same output law as the ancestral walk as one terminal node
+ * (weight P(prefix(v)) * P(exit | v)) and one bonus token from that node's
+ * row with its children's tokens removed.
+ *
+ * probs, vocab, row_offsets, parents, tokens, num_trees, max_depth, out,
+ * status: as sg_tree_accept_probs (same output layout).
+ * total_rows   packed rows (row_offsets[num_trees]); one CTA per row sums
+ *              the rows of internal nodes.
+ * uniforms     explicit uniforms [num_trees, uniform_stride >= 2] fp64:
+ *              u[0] draws the terminal node, u[1] the bonus token.  NULL
+ *              selects Philox4x32-10(key=seed, counter=(0, request lo,
+ *              request hi, 2)) with request_ids[t] (t when NULL).
+ * workspace    device scratch of sg_tree_verify_terminal_mass_workspace_bytes
+ *              (total_rows) bytes, 16-byte aligned (row masses).
+ * Row masses are exact 64.64 fixed-point sums; normalisation, prefix
+ * products and the terminal draw run in fp64 in node order; the bonus token
+ * is the exact fixed-point inverse CDF (first token whose running mass
+ * exceeds floor(u * total)).  Device-detected problems set status
+ * (SG_ERR_TREE, SG_ERR_PROBABILITY) and leave the tree's output row -1.
+ */
+SG_API size_t sg_tree_verify_terminal_mass_workspace_bytes(int64_t total_rows);
+SG_API int sg_tree_verify_terminal_mass(const float* probs, int64_t vocab,
+                         const int64_t* row_offsets, const int64_t* parents,
+                         const int64_t* tokens, int32_t num_trees,
+                         int64_t total_rows, int32_t max_depth,
+                         const double* uniforms, int32_t uniform_stride,
+                         uint64_t seed, const int64_t* request_ids,
+                         int64_t* out, int32_t* status, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
 /* Element types of logit rows (sg_tree_accept_logits `dtype`). */
 enum sg_dtype { SG_DTYPE_F32 = 0, SG_DTYPE_BF16 = 1 };
 

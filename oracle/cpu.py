@@ -42,6 +42,9 @@ def lib() -> ctypes.CDLL:
         L.sgo_kv_commit.restype = ctypes.c_int
         L.sgo_kv_commit.argtypes = [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64,
                                     c_void_p, c_void_p, c_int64]
+        L.sgo_tree_verify_terminal_mass.restype = ctypes.c_int
+        L.sgo_tree_verify_terminal_mass.argtypes = [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int32,
+                                                    c_int32, c_void_p, c_int32, c_uint64, c_void_p, c_void_p]
         L.sgo_node_uniforms.restype = None
         L.sgo_node_uniforms.argtypes = [c_uint64, c_uint64, ctypes.c_uint32, POINTER(c_double),
                                         POINTER(c_double)]
@@ -100,6 +103,27 @@ def accept_logits(logits: np.ndarray, row_offsets, parents, tokens, max_depth: i
     st = lib().sgo_tree_accept_logits(_p(logits), logits.shape[1], _p(row_offsets), _p(parents), _p(tokens), trees,
                                       max_depth, float(temperature), _p(uniforms), stride, seed, _p(request_ids),
                                       arith, _p(out))
+    return out, st
+
+
+def terminal_mass(probs: np.ndarray, row_offsets, parents, tokens, max_depth: int,
+                  uniforms: np.ndarray | None = None, seed: int = 0, request_ids=None) -> tuple[np.ndarray, int]:
+    """Terminal-mass verifier (sampling.py:542-735) over packed rows; returns
+    (out [trees, max_depth+2] int64, status)."""
+    probs = np.ascontiguousarray(probs, dtype=np.float32)
+    row_offsets = np.ascontiguousarray(row_offsets, dtype=np.int64)
+    parents = np.ascontiguousarray(parents, dtype=np.int64)
+    tokens = np.ascontiguousarray(tokens, dtype=np.int64)
+    trees = len(row_offsets) - 1
+    stride = 0
+    if uniforms is not None:
+        uniforms = np.ascontiguousarray(uniforms, dtype=np.float64).reshape(trees, -1)
+        stride = uniforms.shape[1]
+    if request_ids is not None:
+        request_ids = np.ascontiguousarray(request_ids, dtype=np.int64)
+    out = np.full((trees, max_depth + 2), -1, dtype=np.int64)
+    st = lib().sgo_tree_verify_terminal_mass(_p(probs), probs.shape[1], _p(row_offsets), _p(parents), _p(tokens),
+                                             trees, max_depth, _p(uniforms), stride, seed, _p(request_ids), _p(out))
     return out, st
 
 

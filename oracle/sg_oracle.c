@@ -451,3 +451,147 @@ void sgo_mass_scale(double u, uint64_t tlo, uint64_t thi, uint64_t* lo, uint64_t
   *lo = (uint64_t)r;
   *hi = (uint64_t)(r >> 64);
 }
+
+/* ---- terminal-mass verifier ---------------------------------------------
+ * Restates sampling.py:542-735 (tree_block_verify_terminal_mass, exit_mode
+ * "internal", prefix_mode "batched") with explicit uniforms, in the
+ * arithmetic of the CUDA kernel (specgrove_b200/csrc/terminal_mass.cu): row
+ * masses as exact 64.64 sums converted once to the nearest double,
+ * normalisation / prefix products / terminal masses in fp64 in node order,
+ * the terminal node as the first node whose running terminal mass exceeds
+ * u0 * total, the bonus token by the exact fixed-point inverse CDF over the
+ * terminal node's row without its children's tokens.  Output layout as
+ * sgo_tree_accept_probs.  Returns the worst status (3 tree, 4 probability).
+ */
+static double u128_to_double(u128 m) {
+  uint64_t hi = (uint64_t)(m >> 64), lo = (uint64_t)m;
+  if (hi == 0) return (double)lo;
+  int lz = __builtin_clzll(hi);
+  uint64_t top = lz ? (hi << lz) | (lo >> (64 - lz)) : hi;
+  uint64_t rest = lz ? (lo << lz) : lo;
+  uint64_t v = top | (rest != 0 ? 1ull : 0ull);
+  return ldexp((double)v, 64 - lz);
+}
+
+static int terminal_one(const float* probs, int64_t V, const int64_t* par, const int64_t* tok, int n,
+                        int32_t D, double u_node, double u_bonus, int64_t* out) {
+  int bad = 0;
+  for (int i = 0; i < D + 2; ++i) out[i] = -1;
+  if (n < 1 || n > 256 || par[0] != -1) return 3;
+  int* dep = (int*)calloc((size_t)n, sizeof(int));
+  for (int j = 1; j < n; ++j) {
+    if (par[j] < 0 || par[j] >= j || tok[j] < 0 || tok[j] >= V) { free(dep); return 3; }
+    dep[j] = dep[par[j]] + 1;
+    if (dep[j] > D) { free(dep); return 3; }
+    for (int i = 1; i < j; ++i)
+      if (par[i] == par[j] && tok[i] == tok[j]) { free(dep); return 3; }
+  }
+  u128* covered = (u128*)calloc((size_t)n, sizeof(u128));
+  u128* total = (u128*)calloc((size_t)n, sizeof(u128));
+  u128* edge = (u128*)calloc((size_t)n, sizeof(u128));
+  char* internal = (char*)calloc((size_t)n, 1);
+  double* prefix = (double*)calloc((size_t)n, sizeof(double));
+  double* term = (double*)calloc((size_t)n, sizeof(double));
+  int status = 0, pick = -1;
+  for (int j = 1; j < n; ++j) {
+    bad |= mass_of(probs[(int64_t)par[j] * V + tok[j]], &edge[j]);
+    covered[par[j]] += edge[j];
+    internal[par[j]] = 1;
+  }
+  for (int j = 0; j < n; ++j) {
+    if (!internal[j]) continue;
+    u128 s = 0, m;
+    for (int64_t t = 0; t < V; ++t) {
+      bad |= mass_of(probs[(int64_t)j * V + t], &m);
+      s += m;
+    }
+    total[j] = s;
+  }
+  double total_term = 0.0;
+  prefix[0] = 1.0;
+  for (int j = 0; j < n && !status; ++j) {
+    if (j > 0) prefix[j] = prefix[par[j]] * (u128_to_double(edge[j]) / u128_to_double(total[par[j]]));
+    double exit_frac = 1.0;
+    if (internal[j]) {
+      if (total[j] == 0 || total[j] < covered[j]) { status = 4; break; }
+      exit_frac = u128_to_double(total[j] - covered[j]) / u128_to_double(total[j]);
+    }
+    term[j] = prefix[j] * exit_frac;
+    total_term += term[j];
+  }
+  if (bad) status = 4;
+  if (!status && total_term > 0.0 && isfinite(total_term)) {
+    double thr = u_node * total_term, cum = 0.0;
+    for (int j = 0; j < n; ++j) {
+      cum += term[j];
+      if (term[j] > 0.0) pick = j;
+      if (cum > thr && term[j] > 0.0) break;
+    }
+  }
+  if (!status && pick < 0) status = 4;
+  if (!status) {
+    const float* row = probs + (int64_t)pick * V;
+    u128 exit_total, m;
+    if (internal[pick]) {
+      exit_total = total[pick] - covered[pick];
+    } else {
+      exit_total = 0;
+      for (int64_t t = 0; t < V; ++t) {
+        bad |= mass_of(row[t], &m);
+        exit_total += m;
+      }
+    }
+    for (int64_t t = 0; t < V; ++t) bad |= mass_of(row[t], &m);  /* the terminal row is read whole */
+    if (bad || exit_total == 0) {
+      status = 4;
+    } else {
+      u128 thr = mass_scale(u_bonus, exit_total), run = 0;
+      int64_t bonus = -1;
+      for (int64_t t = 0; t < V && bonus < 0; ++t) {
+        int excluded = 0;
+        for (int j = 1; j < n; ++j) excluded |= par[j] == pick && tok[j] == t;
+        if (excluded) continue;
+        mass_of(row[t], &m);
+        run += m;
+        if (run > thr) bonus = t;
+      }
+      if (bonus < 0) {
+        status = 4;
+      } else {
+        int count = dep[pick];
+        for (int x = pick, i = count - 1; x != 0; x = (int)par[x], --i) out[i] = x;
+        out[D] = count;
+        out[D + 1] = bonus;
+      }
+    }
+  }
+  free(dep); free(covered); free(total); free(edge); free(internal); free(prefix); free(term);
+  return status;
+}
+
+int sgo_tree_verify_terminal_mass(const float* probs, int64_t vocab, const int64_t* row_offsets,
+                                  const int64_t* parents, const int64_t* tokens, int32_t num_trees,
+                                  int32_t max_depth, const double* uniforms, int32_t uniform_stride,
+                                  uint64_t seed, const int64_t* request_ids, int64_t* out) {
+  int worst = 0;
+#pragma omp parallel for schedule(dynamic, 1) reduction(max : worst)
+  for (int t = 0; t < num_trees; ++t) {
+    int64_t r0 = row_offsets[t];
+    int n = (int)(row_offsets[t + 1] - r0);
+    double u0, u1;
+    if (uniforms) {
+      u0 = uniforms[(int64_t)t * uniform_stride];
+      u1 = uniforms[(int64_t)t * uniform_stride + 1];
+    } else {
+      uint64_t req = request_ids ? (uint64_t)request_ids[t] : (uint64_t)t;
+      uint32_t c[4] = {0u, (uint32_t)req, (uint32_t)(req >> 32), 2u};
+      philox(c, (uint32_t)seed, (uint32_t)(seed >> 32));
+      u0 = u53(c[0], c[1]);
+      u1 = u53(c[2], c[3]);
+    }
+    int st = terminal_one(probs + r0 * vocab, vocab, parents + r0, tokens + r0, n, max_depth, u0, u1,
+                          out + (int64_t)t * (max_depth + 2));
+    if (st > worst) worst = st;
+  }
+  return worst;
+}

@@ -47,6 +47,10 @@ _SIGNATURES = {
     "sg_gemm_bf16": (ctypes.c_int, [
         c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int32, c_int32, c_int32, c_int32,
         c_void_p, c_int64, c_void_p, c_void_p]),
+    "sg_tree_verify_terminal_mass_workspace_bytes": (ctypes.c_size_t, [c_int64]),
+    "sg_tree_verify_terminal_mass": (ctypes.c_int, [
+        c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int32, c_int64, c_int32, c_void_p, c_int32, c_uint64,
+        c_void_p, c_void_p, c_void_p, c_void_p, ctypes.c_size_t, c_void_p]),
     "sg_gemm_split_workspace_bytes": (ctypes.c_size_t, []),
     "sg_gemm_split_workspace_init": (ctypes.c_int, [c_void_p, ctypes.c_size_t, c_void_p]),
     "sg_gemm_bf16_ws": (ctypes.c_int, [

@@ -250,6 +250,27 @@ __host__ __device__ __forceinline__ void mass_accumulate(Mass& acc, uint32_t bit
   }
 }
 
+// The mass's value (an integer: p * 2^64 units) as the nearest double: the
+// top 64 significant bits with the rest folded into a sticky low bit, one
+// round-to-nearest conversion, then an exact power-of-two scale.
+__host__ __device__ __forceinline__ double mass_to_double(Mass m) {
+#ifdef __CUDA_ARCH__
+  if (m.hi == 0ull) return __ull2double_rn(m.lo);
+  const int lz = __clzll(static_cast<long long>(m.hi));
+#else
+  if (m.hi == 0ull) return static_cast<double>(m.lo);
+  const int lz = __builtin_clzll(m.hi);
+#endif
+  const uint64_t top = lz != 0 ? (m.hi << lz) | (m.lo >> (64 - lz)) : m.hi;
+  const uint64_t rest = lz != 0 ? (m.lo << lz) : m.lo;
+  const uint64_t v = top | (rest != 0ull ? 1ull : 0ull);
+#ifdef __CUDA_ARCH__
+  return ldexp(__ull2double_rn(v), 64 - lz);
+#else
+  return __builtin_ldexp(static_cast<double>(v), 64 - lz);
+#endif
+}
+
 __host__ __device__ __forceinline__ uint64_t mul_hi64(uint64_t a, uint64_t b) {
 #ifdef __CUDA_ARCH__
   return __umul64hi(a, b);

@@ -5,7 +5,8 @@ types of the reference verifiers in
 ``gbv_experiments/fused_tree_sampling.py`` (``tree_verify_ancestral_fused_scan`` :2172-2202,
 ``tree_verify_ancestral_sparse_exit_fused_scan`` :2205-2259,
 ``..._batched`` :2262-2373, ``tree_verify_ancestral_same_draw_fused``
-:2376-2414), so the decoder's verifier dispatch
+:2376-2414; ``tree_block_verify_terminal_mass_fused`` follows
+``sampling.py:542-735``), so the decoder's verifier dispatch
 (``continuous_tree_block_decode.py:1965-2107``) can call them unchanged.  They
 draw their uniforms from the request's ``torch.Generator`` exactly as the
 reference does (``torch.rand(max_depth + 1)`` or ``2 * (max_depth + 1)``
@@ -360,6 +361,67 @@ def tree_verify_ancestral_logits_fused_scan_batched(parents_batch, tokens_batch,
         nodes, out_toks, bonus = decode_output(row, depth, vocab, toks, "Batched direct-logits sampler")
         results.append((nodes, out_toks, bonus, _logit_stats(len(nodes), len(par))))
     return results
+
+
+def terminal_mass_packed(probs: torch.Tensor, trees: PackedTrees, *, uniforms: torch.Tensor | None = None,
+                         seed: int = 0, request_ids: torch.Tensor | None = None, max_depth: int | None = None,
+                         out: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                         stream=None) -> torch.Tensor:
+    """One call of ``sg_tree_verify_terminal_mass`` (two launches) over packed
+    rows; returns the device ``[trees, max_depth + 2]`` int64 output
+    (reference layout).  ``uniforms``: ``[trees, 2]`` float64 (terminal node,
+    bonus token) or None for the Philox stream keyed by (seed, request)."""
+    from . import _lib
+    if probs.dtype != torch.float32 or not probs.is_cuda or probs.ndim != 2:
+        raise ValueError("terminal_mass_packed expects a CUDA float32 [rows, vocab] tensor")
+    probs = probs.contiguous()
+    if probs.shape[0] < trees.total_rows:
+        raise ValueError("fewer probability rows than packed tree nodes")
+    depth = trees.max_depth if max_depth is None else int(max_depth)
+    if depth < trees.max_depth:
+        raise ValueError("max_depth is below the depth of a packed tree")
+    stride = 0
+    if uniforms is not None:
+        if uniforms.dtype != torch.float64 or uniforms.device != probs.device:
+            raise ValueError("uniforms must be float64 on the probabilities' device")
+        uniforms = uniforms.reshape(trees.count, -1).contiguous()
+        stride = uniforms.shape[1]
+        if stride < 2:
+            raise ValueError("terminal-mass draws need two uniforms per tree")
+    if out is None:
+        out = torch.empty((trees.count, depth + 2), dtype=torch.long, device=probs.device)
+    lib = _lib.load()
+    nbytes = lib.sg_tree_verify_terminal_mass_workspace_bytes(trees.total_rows)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=probs.device)
+    st = lib.sg_tree_verify_terminal_mass(
+        _lib.ptr(probs), probs.shape[1], _lib.ptr(trees.row_offsets), _lib.ptr(trees.parents),
+        _lib.ptr(trees.tokens), trees.count, trees.total_rows, depth, _lib.ptr(uniforms), stride, seed,
+        _lib.ptr(request_ids), _lib.ptr(out), _lib.ptr(status), _lib.ptr(ws), nbytes, _lib.stream_ptr(stream))
+    _lib.check(st, "sg_tree_verify_terminal_mass")
+    return out
+
+
+def tree_block_verify_terminal_mass_fused(parents, tokens, all_p, generator=None, validate: bool = True):
+    """Reference sampling.py:542-735 (``tree_block_verify_terminal_mass``, the
+    decoder's default verifier) on the B200 kernel: (nodes, tokens, bonus)
+    with the same output law, its two draws taken from ``torch.rand(2)`` on
+    the request's generator (terminal node, then bonus token)."""
+    parents, tokens, max_depth = _topology(parents, tokens)
+    node_count = len(parents)
+    _check_rows(all_p, node_count, "Terminal-mass tree")
+    if any(token < 0 or token >= all_p.shape[1] for token in tokens):
+        raise ValueError("Tree token is outside the Target vocabulary")
+    if validate:
+        _validate_probabilities(all_p, normalised=False)
+    uniforms = torch.rand(2, dtype=torch.float64, device=all_p.device, generator=generator)
+    trees = PackedTrees([parents], [tokens], all_p.device)
+    status = torch.zeros(1, dtype=torch.int32, device=all_p.device)
+    out = terminal_mass_packed(_as_fp32_rows(all_p), trees, uniforms=uniforms, max_depth=max_depth,
+                               status=status)
+    row, st = out[0].tolist(), int(status.item())
+    if st != 0:
+        raise FloatingPointError(f"Terminal-mass tree sampler: device status {st}")
+    return decode_output(row, max_depth, all_p.shape[1], tokens, "Terminal-mass tree sampler")
 
 
 def philox_node_uniforms(seed: int, request: int, node: int) -> tuple[float, float]:

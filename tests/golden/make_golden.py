@@ -30,6 +30,12 @@ functions (no restatement):
                      random fp32 logits: the top-k log masses it ranks, the
                      tree, and _prefix_tree / _draft_tree_expected_tokens
                      (continuous_tree_block_decode.py:560-586) per tier.
+  terminal_mass.npz  sampling.tree_block_verify_terminal_mass (sampling.py:542-735,
+                     default modes) on float64 rows, with its `sample` replaced
+                     by an inverse-CDF draw at given uniforms (first index whose
+                     running mass exceeds u * total): u[0] draws the terminal
+                     node, u[1] the bonus token (a one-node tree's only draw is
+                     its bonus, so it gets u[1]).
   dflash_step.npz    third_party/ddtree_official/model/dflash.py
                      DFlashDraftModel (tiny configuration, weights of
                      tests/dflash_case.py) over two drafter steps per request
@@ -164,6 +170,41 @@ def save_accept(name: str, cases):
         arrays[f"bonus_{i}"] = np.int64(c["bonus"])
     arrays["count"] = np.int64(len(cases))
     np.savez_compressed(OUT / name, **arrays)
+
+
+def build_terminal_mass(ref, gen):
+    """Terminal-mass verifier cases: the reference function itself with its
+    categorical draws made inverse-CDF draws at recorded uniforms."""
+    sampling = ref.sampling
+    specs = [(1, 64, "softmax"), (2, 64, "softmax"), (5, 64, "softmax"), (9, 500, "softmax"),
+             (17, 300, "softmax"), (8, 1001, "softmax"), (6, 1000, "sparse_zeros"), (20, 256, "softmax"),
+             (33, 256, "softmax"), (4, 2048, "softmax"), (13, 300, "unnormalised"), (6, 77, "unnormalised"),
+             (12, 128, "softmax"), (3, 4096, "sparse_zeros")]
+    cases = []
+    original = sampling.sample
+    try:
+        for n, vocab, kind in specs:
+            parents, tokens, depths = random_tree(gen, n, vocab)
+            probs = tree_rows(gen, parents, tokens, vocab, kind)
+            uniforms = torch.rand(2, dtype=torch.float64, generator=gen)
+            queue = [float(uniforms[1])] if n == 1 else [float(uniforms[0]), float(uniforms[1])]
+
+            def inverse_cdf(weights, generator=None, _queue=queue):
+                cumulative = weights.reshape(-1).to(torch.float64).cumsum(0)
+                u = _queue.pop(0)
+                index = torch.searchsorted(cumulative, torch.tensor(u * float(cumulative[-1]), dtype=torch.float64),
+                                           right=True)
+                return index.clamp_max(cumulative.numel() - 1).reshape(())
+
+            sampling.sample = inverse_cdf
+            nodes, _, bonus = sampling.tree_block_verify_terminal_mass(
+                parents, tokens[1:], probs.to(torch.float64), generator=None, validate=False)
+            cases.append(dict(parents=parents, tokens=tokens, probs=probs.numpy(), uniforms=uniforms.numpy(),
+                              max_depth=max(depths), nodes=nodes, bonus=bonus, vocab=vocab))
+    finally:
+        sampling.sample = original
+    save_accept("terminal_mass.npz", cases)
+    return cases
 
 
 def build_accept_logits(ref, gen):
@@ -455,12 +496,16 @@ def build_dflash_step(reference: Path):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the specgrove checkout")
+    ap.add_argument("--only", default=None, help="regenerate one fixture builder (e.g. terminal_mass)")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "code" / "natural" / "src"))
     from gbv_experiments import continuous_tree_block_decode as decode
     from gbv_experiments import fused_tree_sampling as fused
     from gbv_experiments import sampling, tree, tree_block_skip as tbs
     ref = SimpleNamespace(decode=decode, fused=fused, sampling=sampling, tree=tree, tbs=tbs)
+    if args.only == "terminal_mass":
+        build_terminal_mass(ref, torch.Generator().manual_seed(20261204))
+        return
     gen = torch.Generator().manual_seed(20261201)
     save_accept("accept_scan.npz", build_accept_cases(ref, gen, "scan"))
     save_accept("accept_sparse.npz", build_accept_cases(ref, gen, "sparse"))
@@ -478,6 +523,7 @@ def main():
     np.savez_compressed(OUT / "accept_logits.npz", **arrays)
     build_draft_trees(ref, torch.Generator().manual_seed(20261203))
     build_dflash_step(Path(args.reference))
+    build_terminal_mass(ref, torch.Generator().manual_seed(20261204))
     for p in sorted(OUT.glob("*.*")):
         print(p.name, p.stat().st_size)
 

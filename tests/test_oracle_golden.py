@@ -274,3 +274,34 @@ def test_dflash_oracle_matches_reference():
         for l in range(c["num_layers"]):
             assert np.max(np.abs(ck[l].numpy() - z[f"r{r}_k{l}"])) < 1e-5
             assert np.max(np.abs(cv[l].numpy() - z[f"r{r}_v{l}"])) < 1e-5
+
+
+def test_oracle_terminal_mass_matches_reference(golden_dir):
+    """Terminal-mass verifier (sampling.py:542-735): the oracle's exact-mass
+    restatement picks the reference function's terminal node and bonus token
+    at the recorded uniforms, on every case (softmax, sparse-zero and
+    unnormalised rows, one-node trees included)."""
+    n_cases = 0
+    for c in _cases(golden_dir / "terminal_mass.npz"):
+        out, st = oracle.terminal_mass(c["probs"], [0, len(c["parents"])], c["parents"], c["tokens"],
+                                       c["max_depth"], uniforms=c["uniforms"][None])
+        assert st == 0
+        D = c["max_depth"]
+        count = int(out[0, D])
+        assert out[0, :count].tolist() == c["nodes"]
+        assert int(out[0, D + 1]) == c["bonus"]
+        n_cases += 1
+    assert n_cases >= 12
+
+
+def test_oracle_terminal_mass_rejects_bad_input():
+    probs = np.full((3, 8), 1 / 8, dtype=np.float32)
+    u = np.array([[0.3, 0.6]])
+    _, st = oracle.terminal_mass(probs, [0, 3], [-1, 0, 0], [-1, 2, 2], 2, uniforms=u)
+    assert st == 3  # a node repeats a child token
+    bad = probs.copy()
+    bad[0, 5] = -0.1
+    _, st = oracle.terminal_mass(bad, [0, 3], [-1, 0, 0], [-1, 2, 3], 2, uniforms=u)
+    assert st == 4
+    out, st = oracle.terminal_mass(probs, [0, 3], [-1, 0, 1], [-1, 2, 3], 1, uniforms=u)
+    assert st == 3 and (out == -1).all()  # depth 2 > max_depth 1
