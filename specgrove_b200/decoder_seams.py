@@ -19,6 +19,8 @@ the same attribute substitution, scripts/paper_dp_allocators.py:59-80):
   request's arena tail, and the output carries ``last_hidden_state`` (final
   norm applied) and the drafter's ``hidden_states[l + 1]``;
 * ``append_packed_sequence`` of the arena keeps the accepted rows in place;
+* ``tree_block_verify_terminal_mass`` (the decoder's default verifier,
+  sampling.py:542-735) -> the terminal-mass kernel, same name and arguments;
 * the lazy-projection verifiers (``tree_verify_ancestral_lazy_projection_*``,
   fused_tree_sampling.py:2758-3031), which receive hidden states and the
   LM-head module, become one fused LM-head + sampling launch over the
@@ -36,12 +38,28 @@ import torch
 from . import ops
 from .arena import ArenaRequest, PersistentKVArena
 from .engine import B200Engine, Wave, Weights
-from .sampling import PackedTrees, _topology, decode_output, follow_packed
+from .sampling import PackedTrees, _topology, decode_output, follow_packed, tree_block_verify_terminal_mass_fused
 
 # Reference attribute name -> this module's replacement (see ``install``).
 VERIFIER_SEAMS = ("tree_verify_ancestral_lazy_projection_fused_scan",
                   "tree_verify_ancestral_lazy_projection_fused_scan_batched",
-                  "tree_verify_ancestral_lazy_projection_sparse_exit_batched")
+                  "tree_verify_ancestral_lazy_projection_sparse_exit_batched",
+                  "tree_block_verify_terminal_mass")
+
+
+# --------------------------------------------------------------------------
+# The decoder's default verifier (sampling.py:542-735)
+# --------------------------------------------------------------------------
+def tree_block_verify_terminal_mass(parents, tokens, all_p, generator=None, validate: bool = True, *,
+                                    prefix_mode: str = "batched", exit_mode: str = "internal"):
+    """``tree_block_verify_terminal_mass`` as the decoder calls it
+    (continuous_tree_block_decode.py:2097-2106) on ``sg_tree_verify_terminal_mass``.
+    The reference's ablation modes all draw the same law; the kernel computes
+    its masses one way (exact row sums, fp64 prefix products), so the modes
+    are checked and otherwise ignored.  Rows are read as fp32."""
+    if prefix_mode not in {"batched", "serial"} or exit_mode not in {"internal", "dense", "complement", "joint"}:
+        raise ValueError("Unknown terminal-mass ablation mode")
+    return tree_block_verify_terminal_mass_fused(parents, tokens, all_p, generator, validate)
 
 
 # --------------------------------------------------------------------------

@@ -99,6 +99,19 @@ def test_wave_through_the_seams(cuda_lib):
             walk.append(node)
         assert nodes == walk and bonus == arg[node]
 
+    # the decoder's default verifier seam (terminal mass), called as the
+    # decoder calls it, on the same rows' probabilities
+    for (par, tok), h in zip(wave_trees, rows):
+        probs = torch.softmax(h.float() @ lm.weight.float().t(), dim=-1)
+        g = torch.Generator(device="cuda").manual_seed(7)
+        nodes, toks, bonus = seams.tree_block_verify_terminal_mass(par, tok[1:], probs, g, validate=False,
+                                                                  prefix_mode="batched", exit_mode="internal")
+        node = 0
+        for n, t in zip(nodes, toks):
+            assert par[n] == node and tok[n] == t
+            node = n
+        assert 0 <= bonus < 1024 and (node, bonus) not in {(par[j], tok[j]) for j in range(1, len(par))}
+
     # commit: the arena keeps [0] + accepted rows of each request in place
     tail_before = pool.storage.clone()
     keep = [[0] + r[0] for r in res]
