@@ -325,6 +325,27 @@ def measure_accept(args, world, rank, wl=None):
     moved_rows = float((moved & (outs[..., :wl.D] != depth_idx)).sum()) / K
     accept_gbs = accept_bytes / (statistics.mean(accept_ms) / 1000) / 1e9
     commit_gbs = commit_bytes / (statistics.mean(commit_ms) / 1000) / 1e9
+    # The decoder's default verifier (terminal mass) on the same trees: it
+    # reads every internal node's row once plus each tree's terminal row.
+    from specgrove_b200.sampling import terminal_mass_packed
+    tm_out = torch.empty((wl.T, wl.D + 2), dtype=torch.long, device="cuda")
+    for i in range(W):
+        terminal_mass_packed(wl.probs, wl.trees, seed=20_000 + i, request_ids=wl.request_ids, out=tm_out,
+                             status=wl.status)
+    tm_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    torch.cuda.synchronize()
+    for i in range(K):
+        flush.fill_(i & 0xFF)
+        tm_ev[i][0].record()
+        terminal_mass_packed(wl.probs, wl.trees, seed=30_000 + i, request_ids=wl.request_ids, out=tm_out,
+                             status=wl.status)
+        tm_ev[i][1].record()
+    torch.cuda.synchronize()
+    if int(wl.status) != 0:
+        raise RuntimeError(f"device status {int(wl.status)}")
+    tm_ms = statistics.mean(a.elapsed_time(b) for a, b in tm_ev)
+    internal_rows = sum(len(set(p[1:])) for p in wl.batch.parents)
+    tm_bytes = float(internal_rows + wl.T) * wl.vocab * 4
     return {
         "workload": wl.name, "value": total_units / (ms * K / 1000.0), "unit": UNIT, "ms_per_step": ms,
         "launches": launches, "rule": "scan (Philox per node)",
@@ -335,6 +356,10 @@ def measure_accept(args, world, rank, wl=None):
                        "peak_kind": peak_kind, "unit": "GB/s", "frac": accept_gbs / hbm,
                        "traffic": NCU_ACCEPT_TRAFFIC_CFG2, "algorithmic_bytes_per_launch": accept_bytes,
                        "launch_ms": statistics.mean(accept_ms)},
+        "terminal_mass": {"bound": "hbm", "kernel": "row_mass_kernel + terminal_kernel (two launches)",
+                          "achieved": tm_bytes / (tm_ms / 1000) / 1e9, "peak": hbm, "unit": "GB/s",
+                          "frac": tm_bytes / (tm_ms / 1000) / 1e9 / hbm, "algorithmic_bytes_per_call": tm_bytes,
+                          "internal_rows": internal_rows, "call_ms": tm_ms},
         "commit": {"bound": "hbm", "kernel": "kv_commit_accepted_kernel", "achieved": commit_gbs, "peak": hbm,
                    "unit": "GB/s", "frac": commit_gbs / hbm, "algorithmic_bytes_per_launch": commit_bytes,
                    "moved_bytes_per_launch": moved_rows * KV_BYTES_PER_TOKEN * 2,
@@ -1028,6 +1053,7 @@ def run_accept(args, world, rank):
     cpu = cpu_baseline_accept(wl) if (rank == 0 and world == 1 and not args.no_cpu) else None
     roof = dict(m["acceptance"])
     roof["commit"] = m["commit"]
+    roof["terminal_mass"] = m["terminal_mass"]
     return {
         "metric": METRIC, "value": m["value"], "unit": UNIT,
         "per_gpu": {"metric": "accepted tokens/s/GPU", "value": m["value"] / world},

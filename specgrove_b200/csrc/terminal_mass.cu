@@ -22,8 +22,10 @@
 // reference's own fp64 sums differ from these only by rounding.
 //
 // Two launches: row_mass_kernel sums the rows of internal nodes (one CTA
-// per packed row, leaves return at once), terminal_kernel (one CTA per tree)
-// does the rest.
+// per packed row with coalesced loads, leaves return at once),
+// terminal_kernel (one CTA per tree) does the rest; its bonus draw sums the
+// exit row in 512-token chunks (a warp each), finds the crossing chunk and
+// scans it with one warp.
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -34,6 +36,7 @@ namespace {
 
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
+constexpr int kMaxChunks = 512;  // exit-row chunks of the bonus draw
 
 __device__ __forceinline__ void report(int32_t* status, int code) {
   if (status != nullptr) atomicMax(status, code);
@@ -66,37 +69,39 @@ __device__ Mass block_sum(Mass v, Mass* sh) {
   return t;
 }
 
-// Exact exclusive block prefix of v (thread order).
-__device__ Mass block_exclusive_scan(Mass v, Mass* sh) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  Mass inc = v;
-#pragma unroll
-  for (int d = 1; d < 32; d <<= 1) {
-    const Mass o = shfl_up_mass(inc, d);
-    if (lane >= d) inc = mass_add(inc, o);
-  }
-  if (lane == 31) sh[warp] = inc;
-  __syncthreads();
-  Mass base = mass_zero();
-  for (int w = 0; w < warp; ++w) base = mass_add(base, sh[w]);
-  __syncthreads();
-  return mass_add(base, mass_sub(inc, v));
-}
-
-// Exact mass of a row's fp32 probabilities over [t0, t1); t0 % 4 == 0 and a
-// 16-byte aligned row when `vec`.
-__device__ Mass range_mass(const uint32_t* bits, int64_t t0, int64_t t1, bool vec, uint32_t* bad) {
+// Exact mass of a whole row, coalesced: thread i takes float4s i, i + n,
+// i + 2n, ... (the sum is exact, so the partition does not matter), eight
+// loads in flight per thread.
+__device__ Mass row_mass_strided(const uint32_t* bits, int64_t vocab, bool vec, uint32_t* bad) {
   Mass acc = mass_zero();
-  int64_t t = t0;
-  if (vec)
-    for (; t + 4 <= t1; t += 4) {
-      const uint4 q = *reinterpret_cast<const uint4*>(bits + t);
+  const int64_t nthr = blockDim.x;
+  if (vec) {
+    const uint4* q4 = reinterpret_cast<const uint4*>(bits);
+    const int64_t n4 = vocab / 4;
+    int64_t i = threadIdx.x;
+    for (; i + 7 * nthr < n4; i += 8 * nthr) {
+      uint4 q[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) q[k] = q4[i + k * nthr];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        mass_accumulate(acc, q[k].x, bad);
+        mass_accumulate(acc, q[k].y, bad);
+        mass_accumulate(acc, q[k].z, bad);
+        mass_accumulate(acc, q[k].w, bad);
+      }
+    }
+    for (; i < n4; i += nthr) {
+      const uint4 q = q4[i];
       mass_accumulate(acc, q.x, bad);
       mass_accumulate(acc, q.y, bad);
       mass_accumulate(acc, q.z, bad);
       mass_accumulate(acc, q.w, bad);
     }
-  for (; t < t1; ++t) mass_accumulate(acc, bits[t], bad);
+    for (int64_t t = n4 * 4 + threadIdx.x; t < vocab; t += nthr) mass_accumulate(acc, bits[t], bad);
+  } else {
+    for (int64_t t = threadIdx.x; t < vocab; t += nthr) mass_accumulate(acc, bits[t], bad);
+  }
   return acc;
 }
 
@@ -132,12 +137,9 @@ __global__ void __launch_bounds__(kThreads) row_mass_kernel(const float* __restr
     return;
   }
   const float* p = probs + row * vocab;
-  const bool vec = (vocab & 3) == 0 && (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
-  const int64_t per = ((vocab + kThreads - 1) / kThreads + 3) & ~int64_t(3);
-  const int64_t t0 = min64(vocab, static_cast<int64_t>(threadIdx.x) * per);
-  const int64_t t1 = min64(vocab, t0 + per);
+  const bool vec = (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
   uint32_t bad = 0;
-  const Mass m = range_mass(reinterpret_cast<const uint32_t*>(p), t0, t1, vec, &bad);
+  const Mass m = row_mass_strided(reinterpret_cast<const uint32_t*>(p), vocab, vec, &bad);
   const Mass total = block_sum(m, sh);
   const int any_bad = __syncthreads_or(bad);
   if (threadIdx.x == 0) {
@@ -169,13 +171,13 @@ __global__ void __launch_bounds__(kThreads) terminal_kernel(const TerminalArgs a
   __shared__ int32_t par[kMaxTreeRows];
   __shared__ int64_t tok[kMaxTreeRows];
   __shared__ int32_t dep[kMaxTreeRows];
-  __shared__ Mass sh[kWarps];
   __shared__ int64_t s_child_tok[kMaxTreeRows];
   __shared__ double prefix[kMaxTreeRows], term[kMaxTreeRows];
-  __shared__ Mass covered[kMaxTreeRows], edge[kMaxTreeRows];
+  __shared__ Mass covered[kMaxTreeRows], edge[kMaxTreeRows], tot[kMaxTreeRows];
   __shared__ bool internal[kMaxTreeRows];
-  __shared__ int s_nchild, s_pick, s_fail;
-  __shared__ Mass s_exit_total;
+  __shared__ int s_nchild, s_pick, s_fail, s_cross;
+  __shared__ Mass s_exit_total, s_before, s_thr;
+  __shared__ Mass s_chunk[kMaxChunks];
   __shared__ int64_t s_bonus;
   pdl_trigger();
   pdl_wait();
@@ -231,16 +233,26 @@ __global__ void __launch_bounds__(kThreads) terminal_kernel(const TerminalArgs a
     u_node = uniform53(r.x, r.y);
     u_bonus = uniform53(r.z, r.w);
   }
-  // Masses and the terminal-node draw: one thread, node order.
+  // The edge probabilities and row totals come into shared memory in
+  // parallel; the masses and the terminal-node draw then run on one thread in
+  // node order.
+  {
+    uint32_t bad_e = 0;
+    const uint32_t* rows = reinterpret_cast<const uint32_t*>(a.probs);
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+      edge[j] = j > 0 ? mass_from_bits(rows[(r0 + par[j]) * a.vocab + tok[j]], &bad_e) : mass_zero();
+      tot[j] = a.totals[r0 + j];
+    }
+    if (__syncthreads_or(bad_e) && threadIdx.x == 0) s_fail = SG_ERR_PROBABILITY;
+    __syncthreads();
+  }
   if (threadIdx.x == 0) {
-    uint32_t bad = 0;
+    uint32_t bad = s_fail != 0;
     for (int j = 0; j < n; ++j) {
       covered[j] = mass_zero();
       internal[j] = false;
     }
-    const uint32_t* rows = reinterpret_cast<const uint32_t*>(a.probs);
     for (int j = 1; j < n; ++j) {
-      edge[j] = mass_from_bits(rows[(r0 + par[j]) * a.vocab + tok[j]], &bad);
       covered[par[j]] = mass_add(covered[par[j]], edge[j]);
       internal[par[j]] = true;
     }
@@ -249,7 +261,7 @@ __global__ void __launch_bounds__(kThreads) terminal_kernel(const TerminalArgs a
     int fail = bad ? SG_ERR_PROBABILITY : 0;
     for (int j = 0; j < n && !fail; ++j) {
       if (j > 0) {
-        const Mass pt = a.totals[r0 + par[j]];
+        const Mass pt = tot[par[j]];
         if (pt.hi == ~0ull) {
           fail = SG_ERR_PROBABILITY;
           break;
@@ -258,7 +270,7 @@ __global__ void __launch_bounds__(kThreads) terminal_kernel(const TerminalArgs a
       }
       double exit_frac = 1.0;
       if (internal[j]) {
-        const Mass total = a.totals[r0 + j];
+        const Mass total = tot[j];
         if (total.hi == ~0ull || mass_is_zero(total) || mass_lt(total, covered[j])) {
           fail = SG_ERR_PROBABILITY;
           break;
@@ -282,7 +294,7 @@ __global__ void __launch_bounds__(kThreads) terminal_kernel(const TerminalArgs a
     s_fail = fail;
     s_pick = pick;
     if (!fail) {
-      s_exit_total = internal[pick] ? mass_sub(a.totals[r0 + pick], covered[pick]) : mass_zero();
+      s_exit_total = internal[pick] ? mass_sub(tot[pick], covered[pick]) : mass_zero();
       int k = 0;
       for (int j = 1; j < n; ++j)
         if (par[j] == pick) s_child_tok[k++] = tok[j];
@@ -299,36 +311,100 @@ __global__ void __launch_bounds__(kThreads) terminal_kernel(const TerminalArgs a
   const float* row = a.probs + (r0 + v) * a.vocab;
   const uint32_t* rbits = reinterpret_cast<const uint32_t*>(row);
   const bool vec = (a.vocab & 3) == 0 && (reinterpret_cast<uintptr_t>(row) & 15u) == 0;
-  const int64_t per = ((a.vocab + kThreads - 1) / kThreads + 3) & ~int64_t(3);
-  const int64_t t0 = min64(a.vocab, static_cast<int64_t>(threadIdx.x) * per);
-  const int64_t t1 = min64(a.vocab, t0 + per);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // The exit row in chunks of `ch` tokens (a multiple of 512, at most
+  // kMaxChunks chunks), each summed by one warp with coalesced loads; the
+  // children's tokens leave their chunk's mass.
+  const int64_t ch = 512 * ((a.vocab + 512 * kMaxChunks - 1) / (512 * kMaxChunks));
+  const int nch = static_cast<int>((a.vocab + ch - 1) / ch);
   uint32_t bad = 0;
-  Mass chunk = range_mass(rbits, t0, t1, vec, &bad);
-  for (int c = 0; c < k; ++c) {  // the children's tokens leave the exit row
-    const int64_t ct = s_child_tok[c];
-    if (ct >= t0 && ct < t1) chunk = mass_sub(chunk, mass_from_bits(rbits[ct], &bad));
+  for (int c = warp; c < nch; c += kWarps) {
+    const int64_t c0 = c * ch, c1 = min64(a.vocab, c0 + ch);
+    Mass acc = mass_zero();
+    if (vec) {
+      const uint4* q4 = reinterpret_cast<const uint4*>(rbits + c0);
+      const int64_t n4 = (c1 - c0) / 4;  // a multiple of 4 tokens when vocab is
+      for (int64_t x = lane; x < n4; x += 32) {
+        const uint4 q = q4[x];
+        mass_accumulate(acc, q.x, &bad);
+        mass_accumulate(acc, q.y, &bad);
+        mass_accumulate(acc, q.z, &bad);
+        mass_accumulate(acc, q.w, &bad);
+      }
+    } else {
+      for (int64_t x = c0 + lane; x < c1; x += 32) mass_accumulate(acc, rbits[x], &bad);
+    }
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1) acc = mass_add(acc, shfl_down_mass(acc, d));
+    if (lane == 0) {
+      for (int e = 0; e < k; ++e) {
+        const int64_t ct = s_child_tok[e];
+        if (ct >= c0 && ct < c1) acc = mass_sub(acc, mass_from_bits(rbits[ct], &bad));
+      }
+      s_chunk[c] = acc;
+    }
   }
-  Mass exit_total = s_exit_total;
-  if (k == 0) exit_total = block_sum(chunk, sh);  // a leaf: its whole row
-  const Mass before = block_exclusive_scan(chunk, sh);
   if (threadIdx.x == 0) s_bonus = -1;
   __syncthreads();
-  if (mass_is_zero(exit_total)) {
+  // The crossing chunk: thread 0 walks the chunk masses in order.
+  if (threadIdx.x == 0) {
+    Mass total = s_exit_total;
+    if (k == 0) {  // a leaf: its whole row
+      total = mass_zero();
+      for (int c = 0; c < nch; ++c) total = mass_add(total, s_chunk[c]);
+    }
+    s_cross = -1;
+    if (!mass_is_zero(total)) {
+      const Mass thr = mass_scale(u_bonus, total);
+      Mass run = mass_zero();
+      for (int c = 0; c < nch; ++c) {
+        const Mass next = mass_add(run, s_chunk[c]);
+        if (mass_lt(thr, next)) {
+          s_cross = c;
+          s_before = run;
+          s_thr = thr;
+          break;
+        }
+        run = next;
+      }
+    }
+  }
+  __syncthreads();
+  if (s_cross < 0) {  // zero exit mass: no token to draw
     if (threadIdx.x == 0) report(a.status, SG_ERR_PROBABILITY);
     return;
   }
-  const Mass thr = mass_scale(u_bonus, exit_total);
-  const Mass after = mass_add(before, chunk);
-  if (!mass_lt(thr, before) && mass_lt(thr, after)) {  // before <= thr < after: the crossing chunk
-    Mass run = before;
-    for (int64_t x = t0; x < t1; ++x) {
-      bool excluded = false;
-      for (int c = 0; c < k; ++c) excluded |= s_child_tok[c] == x;
-      if (excluded) continue;
-      run = mass_add(run, mass_from_bits(rbits[x], &bad));
-      if (mass_lt(thr, run)) {
-        s_bonus = x;
-        break;
+  if (warp == 0) {
+    // Inside the crossing chunk: lane l takes tokens [c0 + l * per, ...), a
+    // warp scan gives each lane the mass before its run, and the lane whose
+    // run crosses the threshold walks it.
+    const int64_t c0 = static_cast<int64_t>(s_cross) * ch, c1 = min64(a.vocab, c0 + ch);
+    const int64_t per = ch / 32;
+    const int64_t l0 = min64(c1, c0 + lane * per), l1 = min64(c1, l0 + per);
+    auto excluded = [&](int64_t x) {
+      bool e = false;
+      for (int c = 0; c < k; ++c) e |= s_child_tok[c] == x;
+      return e;
+    };
+    Mass mine = mass_zero();
+    for (int64_t x = l0; x < l1; ++x)
+      if (!excluded(x)) mine = mass_add(mine, mass_from_bits(rbits[x], &bad));
+    Mass inc = mine;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const Mass o = shfl_up_mass(inc, d);
+      if (lane >= d) inc = mass_add(inc, o);
+    }
+    Mass run = mass_add(s_before, mass_sub(inc, mine));
+    const Mass thr = s_thr;
+    if (!mass_lt(thr, run) && mass_lt(thr, mass_add(run, mine))) {
+      for (int64_t x = l0; x < l1; ++x) {
+        if (excluded(x)) continue;
+        run = mass_add(run, mass_from_bits(rbits[x], &bad));
+        if (mass_lt(thr, run)) {
+          s_bonus = x;
+          break;
+        }
       }
     }
   }
