@@ -59,8 +59,8 @@ UNIT = "accepted tokens/s"
 # DRAM bytes (read + write) per launch from ncu captures of the same kernels
 # (profiles/): the layer-0 tree attention and gate/up + SwiGLU GEMM on the
 # configuration-4 wave, and the acceptance launch of the configuration-2 sweep.
-NCU_ATTENTION_TRAFFIC_CFG4 = 736.310016e6 + 15.491584e6
-NCU_SWIGLU_TRAFFIC_CFG4 = 218.232576e6 + 41.149184e6
+NCU_ATTENTION_TRAFFIC_CFG4 = 736.275200e6 + 15.357440e6
+NCU_SWIGLU_TRAFFIC_CFG4 = 218.211840e6 + 39.758592e6
 NCU_ACCEPT_TRAFFIC_CFG2 = 53.622528e6 + 0.811264e6
 
 
