@@ -162,6 +162,7 @@ struct TerminalArgs {
   uint64_t seed;
   const int64_t* request_ids;
   const Mass* totals;
+  int64_t total_rows;  // rows covered by `totals`
   int64_t* out;
   int32_t* status;
 };
@@ -186,8 +187,9 @@ __global__ void __launch_bounds__(kThreads) terminal_kernel(const TerminalArgs a
   int64_t* out = a.out + static_cast<int64_t>(t) * (D + 2);
   for (int64_t i = threadIdx.x; i < D + 2; i += blockDim.x) out[i] = -1;
   const int64_t r0 = a.row_offsets[t];
-  const int n = static_cast<int>(a.row_offsets[t + 1] - r0);
-  if (n < 1 || n > kMaxTreeRows) {
+  const int64_t n64 = a.row_offsets[t + 1] - r0;
+  const int n = static_cast<int>(n64);
+  if (r0 < 0 || n64 < 1 || n64 > kMaxTreeRows || r0 + n64 > a.total_rows) {  // rows beyond total_rows have no sums
     if (threadIdx.x == 0) report(a.status, SG_ERR_TREE);
     return;
   }
@@ -457,7 +459,7 @@ extern "C" int sg_tree_verify_terminal_mass(const float* probs, int64_t vocab, c
   int st = check_launch("row_mass_kernel");
   if (st != SG_OK) return st;
   TerminalArgs a{probs, vocab, row_offsets, parents, tokens, num_trees, max_depth, uniforms, uniform_stride,
-                 seed, request_ids, totals, out, status};
+                 seed, request_ids, totals, total_rows, out, status};
   return launch_pdl("terminal_kernel", terminal_kernel, dim3(static_cast<unsigned>(num_trees)), dim3(kThreads), 0,
                     stream, a);
 }

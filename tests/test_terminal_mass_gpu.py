@@ -142,3 +142,25 @@ def test_reference_named_wrapper(cuda_lib):
     nodes, toks, bonus = tree_block_verify_terminal_mass_fused([-1, 0, 1], [7, 9], p, generator=g)
     assert nodes in ([], [1], [1, 2]) and 0 <= bonus < 64
     assert toks == [[7, 9][n - 1] for n in nodes]
+
+
+def test_rows_beyond_total_rows_are_reported(cuda_lib):
+    """A tree that reaches past `total_rows` (no row sums there) is reported
+    as SG_ERR_TREE and its output stays -1; the other trees are drawn."""
+    from specgrove_b200 import _lib
+    from specgrove_b200._lib import ptr, stream_ptr
+    probs = torch.full((5, 16), 1 / 16, device="cuda")
+    trees = PackedTrees([[-1, 0], [-1, 0, 1]], [[3], [4, 5]], "cuda")
+    out = torch.empty((2, 4), dtype=torch.long, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    u = torch.tensor([[0.5, 0.5], [0.5, 0.5]], dtype=torch.float64, device="cuda")
+    lib = _lib.load()
+    nbytes = lib.sg_tree_verify_terminal_mass_workspace_bytes(4)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    st = lib.sg_tree_verify_terminal_mass(ptr(probs), 16, ptr(trees.row_offsets), ptr(trees.parents),
+                                          ptr(trees.tokens), 2, 4, 2, ptr(u), 2, 0, None, ptr(out), ptr(status),
+                                          ptr(ws), nbytes, stream_ptr())
+    assert st == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) == 3
+    assert (out[1] == -1).all() and int(out[0, 3]) >= 0
