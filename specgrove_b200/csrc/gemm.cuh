@@ -850,13 +850,20 @@ struct EpiQkvPost {
         float a[32], b[32];
         sm100::tmem_ld32(hbase + c * 32, a);
         sm100::tmem_ld32(hbase + HALF + c * 32, b);
+        // The row's (cos, sin) pairs of these 32 dims as 16 float4 loads
+        // issued together (one memory round trip, not one per dim pair).
+        float4 cs4[16];
+        const float4* rp4 = reinterpret_cast<const float4*>(rp + c * 32);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) cs4[k] = rv ? rp4[k] : make_float4(1.f, 0.f, 1.f, 0.f);
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           float ra[2], rb[2];
 #pragma unroll
           for (int k = 0; k < 2; ++k) {
             const int d = c * 32 + e + k;
-            const float2 cs = rv ? rp[d] : make_float2(1.f, 0.f);
+            const float4 q4 = cs4[e / 2];
+            const float2 cs = k == 0 ? make_float2(q4.x, q4.y) : make_float2(q4.z, q4.w);
             const float xa = a[e + k] * rstd * __bfloat162float(wn[d]);
             const float xb = b[e + k] * rstd * __bfloat162float(wn[d + HALF]);
             // rotate_half: out_d = x_d cos - x_{d+H} sin,  out_{d+H} = x_{d+H} cos + x_d sin
